@@ -1,0 +1,615 @@
+// Attention forward for sm_100a: tcgen05 MMA with TMEM accumulators, TMA-staged
+// Q/K/V tiles, online softmax with one thread per query row, out + natural-log LSE.
+//
+// Replaces the FlashAttention-4 call of the reference (fa4_ring/fa4_backend.py:58-123)
+// and, with `accumulate`, also fuses the incremental LSE merge of fa4_ring/merge.py:45-64
+// into the epilogue.  The three zig-zag ring step patterns
+// (fa4_ring/ring_attention.py:109-166) address their row halves in place.
+//
+// CTA = one (query tile of 128 rows, query head, sequence).  192 threads:
+//   warps 0-3  softmax + epilogue; thread t owns query row t = TMEM lane t
+//   warp  4    TMA producer (one thread): Q once, then K_j / V_j into a ring of stages
+//   warp  5    TMEM allocator + MMA issuer (one thread)
+// TMEM (512 columns): S0 | S1 (BN fp32 columns each, double-buffered) | O (D columns).
+// P = softmax numerators overwrites the first BN*elem/4 columns of its S buffer and
+// is consumed directly from TMEM as the A operand of O += P V.
+// MMA issue order: S0, S1, PV0, S2, PV1, ... so the tensor core computes S_{j+1}
+// while the softmax warps turn S_j into P_j.  O is rescaled lazily: only when a
+// row's running max grows by more than 2^8 (log2 domain), so P <= 256.
+#include "common.cuh"
+
+namespace fa4cp {
+
+__device__ int g_attn_status = 0;
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int kThreads = 192;
+constexpr float kNegInf = -__builtin_huge_valf();
+constexpr float kRescaleThreshold = 8.0f;  // log2 units
+
+// codes written to the device status word when a bounded wait gives up
+enum : int {
+  kErrQ = 0x101, kErrKEmpty, kErrVEmpty, kErrKFull, kErrPFull, kErrVFull,
+  kErrSFull, kErrODone, kErrDrain
+};
+
+struct Params {
+  const int32_t* cu_q;
+  const int32_t* cu_k;
+  void* out;
+  float* lse;
+  const float* q_descale;
+  const float* k_descale;
+  const float* v_descale;
+  int nseq, n_qtiles, Hq, Hkv, group;
+  int pattern, causal, accumulate;
+  int in_fmt;    // kind::f16 operand format: 0 f16, 1 bf16 (unused for e4m3)
+  int out_bf16;  // 1 -> bf16 output, 0 -> f16 output
+  float scale_log2;
+};
+
+template <int D_, int BN_, int STAGES_, bool FP8_>
+struct Traits {
+  static constexpr int D = D_, BN = BN_, STAGES = STAGES_;
+  static constexpr bool FP8 = FP8_;
+  static constexpr int ELEM = FP8 ? 1 : 2;
+  static constexpr int CHUNK = 128 / ELEM;  // elements of one 128-byte swizzle row
+  static constexpr int NCH = D / CHUNK;     // 128-byte column blocks along D
+  static constexpr int MMA_K = FP8 ? 32 : 16;
+  static constexpr int Q_BYTES = BM * D * ELEM;
+  static constexpr int KV_BYTES = BN * D * ELEM;
+  static constexpr int Q_CHUNK_BYTES = BM * 128;
+  static constexpr int KV_CHUNK_BYTES = BN * 128;
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_K = OFF_Q + Q_BYTES;
+  static constexpr int OFF_V = OFF_K + STAGES * KV_BYTES;
+  static constexpr int OFF_BAR = OFF_V + STAGES * KV_BYTES;
+  // q_full, k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], p_full[2], o_done[2], teardown
+  static constexpr int NUM_BARS = 1 + 4 * STAGES + 2 + 2 + 2 + 1;
+  static constexpr int SMEM_BYTES = OFF_BAR + NUM_BARS * 8 + 16 + 1024;
+  static constexpr int TM_O = 2 * BN;
+  static constexpr int TM_COLS = 512;
+  // P columns per S buffer: 32-bit columns holding BN values of ELEM bytes
+  static constexpr int P_COLS = BN * ELEM / 4;
+  static_assert(D % CHUNK == 0, "head_dim must be a multiple of one 128-byte swizzle row");
+  static_assert(2 * BN + D <= TM_COLS, "TMEM budget");
+  static_assert(BN % 32 == 0 && D % 32 == 0, "tile shape");
+  static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+};
+
+struct Geometry {
+  int q_start, q_len, k_start, k_len;
+};
+
+__device__ __forceinline__ Geometry seq_geometry(const Params& p, int seq) {
+  Geometry g;
+  const int a = p.cu_q[seq], b = p.cu_q[seq + 1];
+  if (p.pattern == FA4CP_PATTERN_VARLEN) {
+    g.q_start = a;
+    g.q_len = b - a;
+    g.k_start = p.cu_k[seq];
+    g.k_len = p.cu_k[seq + 1] - g.k_start;
+  } else {
+    const int n = b - a, hh = n / 2;
+    if (p.pattern == FA4CP_PATTERN_FRONT_KV) {
+      g.q_start = a; g.q_len = n; g.k_start = a; g.k_len = hh;
+    } else {  // FA4CP_PATTERN_BACK_Q
+      g.q_start = a + hh; g.q_len = n - hh; g.k_start = a; g.k_len = n;
+    }
+  }
+  return g;
+}
+
+template <class TR>
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const Params p) {
+  constexpr int D = TR::D, BN = TR::BN, ST = TR::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int head = blockIdx.x;
+  const int qtile = p.n_qtiles - 1 - int(blockIdx.y);  // heaviest causal tiles first
+  const int seq = blockIdx.z;
+
+  const Geometry g = seq_geometry(p, seq);
+  const int q0 = qtile * BM;
+  if (q0 >= g.q_len) return;  // uniform for the whole CTA, before any setup
+  const int rows = min(BM, g.q_len - q0);
+  const int diag = g.k_len - g.q_len;  // causal: key j visible to row i iff j <= i + diag
+  int kv_end = g.k_len;
+  if (p.causal) kv_end = min(g.k_len, q0 + rows + diag);
+  const int n_kv = kv_end > 0 ? (kv_end + BN - 1) / BN : 0;
+  const int kvh = head / p.group;
+
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TR::OFF_BAR);
+  const uint32_t bar0 = smem_u32(bars);
+  auto BAR = [&](int i) -> uint32_t { return bar0 + 8u * uint32_t(i); };
+  const uint32_t q_full = BAR(0);
+  auto k_full = [&](int s) { return BAR(1 + s); };
+  auto k_empty = [&](int s) { return BAR(1 + ST + s); };
+  auto v_full = [&](int s) { return BAR(1 + 2 * ST + s); };
+  auto v_empty = [&](int s) { return BAR(1 + 3 * ST + s); };
+  auto s_full = [&](int b) { return BAR(1 + 4 * ST + b); };
+  auto p_full = [&](int b) { return BAR(3 + 4 * ST + b); };
+  // PV_i commits o_done(i & 1): a waiter for PV_i is then never two phases away
+  // from the barrier's current phase (PV_{i-2} is known complete, PV_{i+2} cannot
+  // have been issued), so parity waits are exact.
+  auto o_done = [&](int b) { return BAR(5 + 4 * ST + b); };
+  const uint32_t td_bar = BAR(7 + 4 * ST);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + TR::NUM_BARS);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* status = &g_attn_status;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(k_full(s), 1);
+      mbar_init(k_empty(s), 1);
+      mbar_init(v_full(s), 1);
+      mbar_init(v_empty(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(s_full(b), 1);
+      mbar_init(p_full(b), 128);
+    }
+    mbar_init(o_done(0), 1);
+    mbar_init(o_done(1), 1);
+    mbar_init(td_bar, 1);
+    *abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 4 && lane == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 5) {
+    tmem_alloc(smem_u32(tmem_slot), TR::TM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 4) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      const uint64_t pol_kv = policy_evict_last();
+      int last_k[ST], last_v[ST];
+      for (int s = 0; s < ST; ++s) last_k[s] = last_v[s] = -1;
+      mbar_arrive_expect_tx(q_full, TR::Q_BYTES);
+#pragma unroll
+      for (int c = 0; c < TR::NCH; ++c)
+        tma_load_3d(smem_u32(smem + TR::OFF_Q + c * TR::Q_CHUNK_BYTES), &tmQ, c * TR::CHUNK, head,
+                    g.q_start + q0, q_full);
+      for (int j = 0; j < n_kv; ++j) {
+        const int s = j % ST, ph = (j / ST) & 1;
+        const int row = g.k_start + j * BN;
+        if (j >= ST && !mbar_wait(k_empty(s), ph ^ 1, abort, kErrKEmpty, status)) break;
+        mbar_arrive_expect_tx(k_full(s), TR::KV_BYTES);
+#pragma unroll
+        for (int c = 0; c < TR::NCH; ++c)
+          tma_load_3d_hint(smem_u32(smem + TR::OFF_K + s * TR::KV_BYTES + c * TR::KV_CHUNK_BYTES),
+                           &tmK, c * TR::CHUNK, kvh, row, k_full(s), pol_kv);
+        last_k[s] = j;
+        if (j >= ST && !mbar_wait(v_empty(s), ph ^ 1, abort, kErrVEmpty, status)) break;
+        mbar_arrive_expect_tx(v_full(s), TR::KV_BYTES);
+#pragma unroll
+        for (int c = 0; c < TR::NCH; ++c)
+          tma_load_3d_hint(smem_u32(smem + TR::OFF_V + s * TR::KV_BYTES + c * TR::KV_CHUNK_BYTES),
+                           &tmV, c * TR::CHUNK, kvh, row, v_full(s), pol_kv);
+        last_v[s] = j;
+      }
+      if (*abort) {
+        // give-up path: let every copy already issued land before the CTA exits
+        int zero = 0;
+        volatile int* no_abort = &zero;
+        mbar_wait(q_full, 0, no_abort, kErrDrain, status);
+        for (int s = 0; s < ST; ++s) {
+          if (last_k[s] >= 0) mbar_wait(k_full(s), (last_k[s] / ST) & 1, no_abort, kErrDrain, status);
+          if (last_v[s] >= 0) mbar_wait(v_full(s), (last_v[s] / ST) & 1, no_abort, kErrDrain, status);
+        }
+      }
+    }
+  } else if (warp == 5) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const int fmt = TR::FP8 ? 0 : p.in_fmt;
+      const uint32_t idesc_qk = make_idesc(BM, BN, fmt, fmt, 0, 0);
+      const uint32_t idesc_pv = make_idesc(BM, D, fmt, fmt, 0, 1);
+      const uint32_t sQ = smem_u32(smem + TR::OFF_Q);
+      auto issue_pv = [&](int i) -> bool {
+        const int s = i % ST, b = i & 1;
+        if (!mbar_wait(p_full(b), (i >> 1) & 1, abort, kErrPFull, status)) return false;
+        if (!mbar_wait(v_full(s), (i / ST) & 1, abort, kErrVFull, status)) return false;
+        tc_fence_after();
+        const uint32_t sV = smem_u32(smem + TR::OFF_V + s * TR::KV_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < BN / TR::MMA_K; ++kk) {
+          const uint64_t bdesc = make_desc_sw128(sV + kk * TR::MMA_K * 128, TR::KV_CHUNK_BYTES, 1024);
+          const uint32_t a_tmem = tmem + uint32_t(b * BN + kk * 8);
+          if constexpr (TR::FP8)
+            mma_f8_ts(tmem + TR::TM_O, a_tmem, bdesc, idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
+          else
+            mma_f16_ts(tmem + TR::TM_O, a_tmem, bdesc, idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
+        }
+        tc_commit(o_done(b));
+        tc_commit(v_empty(s));
+        return true;
+      };
+      bool ok = mbar_wait(q_full, 0, abort, kErrQ, status);
+      tc_fence_after();
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int s = j % ST, b = j & 1;
+        if (!mbar_wait(k_full(s), (j / ST) & 1, abort, kErrKFull, status)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t sK = smem_u32(smem + TR::OFF_K + s * TR::KV_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < D / TR::MMA_K; ++kk) {
+          const int off = kk * 32;  // bytes along D of this K-step
+          const uint32_t ca = (off / 128) * TR::Q_CHUNK_BYTES + (off % 128);
+          const uint32_t cb = (off / 128) * TR::KV_CHUNK_BYTES + (off % 128);
+          const uint64_t adesc = make_desc_sw128(sQ + ca, 16, 1024);
+          const uint64_t bdesc = make_desc_sw128(sK + cb, 16, 1024);
+          if constexpr (TR::FP8)
+            mma_f8_ss(tmem + uint32_t(b * BN), adesc, bdesc, idesc_qk, kk > 0 ? 1u : 0u);
+          else
+            mma_f16_ss(tmem + uint32_t(b * BN), adesc, bdesc, idesc_qk, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(s_full(b));
+        tc_commit(k_empty(s));
+        if (j > 0 && !issue_pv(j - 1)) { ok = false; break; }
+      }
+      if (ok && n_kv > 0) issue_pv(n_kv - 1);
+      // every MMA issued above has completed before TMEM is released
+      tc_commit(td_bar);
+      int zero = 0;
+      volatile int* no_abort = &zero;
+      mbar_wait(td_bar, 0, no_abort, kErrDrain, status);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax + epilogue
+    const int r = warp * 32 + lane;
+    const uint32_t t_lane = tmem + (uint32_t(warp * 32) << 16);
+    const int key_lim = q0 + r + diag;
+    float scale = p.scale_log2;
+    float vscale = 1.0f;
+    if (p.q_descale) scale *= p.q_descale[kvh];
+    if (p.k_descale) scale *= p.k_descale[kvh];
+    if (p.v_descale) vscale = p.v_descale[kvh];
+    float m = kNegInf, l = 0.f;
+    bool aborted = false;
+
+    for (int j = 0; j < n_kv; ++j) {
+      const int b = j & 1;
+      bool ok = mbar_wait(s_full(b), (j >> 1) & 1, abort, kErrSFull, status);
+      if (!__all_sync(0xffffffffu, ok)) { aborted = true; break; }
+      tc_fence_after();
+      uint32_t sr[BN / 32][32];
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) tmem_ld32(t_lane + uint32_t(b * BN + c * 32), sr[c]);
+      tmem_wait_ld();
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) reg_fence32(sr[c]);
+
+      const int kbase = j * BN;
+      const bool need_mask = (kbase + BN > g.k_len) || (p.causal && kbase + BN - 1 > q0 + diag);
+      if (need_mask) {
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c)
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int key = kbase + c * 32 + e;
+            if (key >= g.k_len || (p.causal && key > key_lim)) sr[c][e] = __float_as_uint(kNegInf);
+          }
+      }
+      float mx = kNegInf;
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c)
+#pragma unroll
+        for (int e = 0; e < 32; ++e) mx = fmaxf(mx, __uint_as_float(sr[c][e]));
+      const float m_new = fmaxf(m, mx);
+      if (j == 0) {
+        m = m_new;
+      } else {
+        const bool need = (m_new - m) * scale > kRescaleThreshold;
+        if (__any_sync(0xffffffffu, need)) {
+          const float f = need ? ex2_approx((m - m_new) * scale) : 1.0f;
+          if (need) { l *= f; m = m_new; }
+          ok = mbar_wait(o_done((j - 1) & 1), ((j - 1) >> 1) & 1, abort, kErrODone, status);
+          if (!__all_sync(0xffffffffu, ok)) { aborted = true; break; }
+          tc_fence_after();
+#pragma unroll 1
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t o[32];
+            tmem_ld32(t_lane + uint32_t(TR::TM_O + c * 32), o);
+            tmem_wait_ld();
+            reg_fence32(o);
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * f);
+            tmem_st32(t_lane + uint32_t(TR::TM_O + c * 32), o);
+          }
+          tmem_wait_st();
+        }
+      }
+      const float neg_m = (m == kNegInf) ? 0.f : -m * scale;
+      float rs = 0.f;
+      if constexpr (TR::FP8) {
+        uint32_t pw[32];
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c) {
+#pragma unroll
+          for (int e = 0; e < 32; e += 4) {
+            float x0 = ex2_approx(fmaf(__uint_as_float(sr[c][e + 0]), scale, neg_m));
+            float x1 = ex2_approx(fmaf(__uint_as_float(sr[c][e + 1]), scale, neg_m));
+            float x2 = ex2_approx(fmaf(__uint_as_float(sr[c][e + 2]), scale, neg_m));
+            float x3 = ex2_approx(fmaf(__uint_as_float(sr[c][e + 3]), scale, neg_m));
+            rs += (x0 + x1) + (x2 + x3);
+            pw[(c * 32 + e) / 4] = pack_e4m3x4(x0, x1, x2, x3);
+          }
+        }
+        static_assert(!TR::FP8 || BN == 128, "FP8 P store assumes 128 keys (32 columns)");
+        tmem_st32(t_lane + uint32_t(b * BN), pw);
+      } else {
+#pragma unroll
+        for (int half = 0; half < BN / 64; ++half) {
+          uint32_t pw[32];
+#pragma unroll
+          for (int e = 0; e < 64; e += 2) {
+            const int c = half * 2 + (e >> 5), ee = e & 31;
+            float x0 = ex2_approx(fmaf(__uint_as_float(sr[c][ee]), scale, neg_m));
+            float x1 = ex2_approx(fmaf(__uint_as_float(sr[c][ee + 1]), scale, neg_m));
+            rs += x0 + x1;
+            pw[e >> 1] = p.in_fmt ? pack_bf16x2(x0, x1) : pack_f16x2(x0, x1);
+          }
+          tmem_st32(t_lane + uint32_t(b * BN + half * 32), pw);
+        }
+      }
+      l += rs;
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(p_full(b));
+    }
+
+    // ------------------------------------------------------------ epilogue
+    if (!aborted && n_kv > 0) {
+      bool ok = mbar_wait(o_done((n_kv - 1) & 1), ((n_kv - 1) >> 1) & 1, abort, kErrODone, status);
+      if (!__all_sync(0xffffffffu, ok)) aborted = true;
+      tc_fence_after();
+    }
+    if (!aborted) {
+      const bool valid = r < rows;
+      const int64_t grow = int64_t(g.q_start) + q0 + r;
+      const float lse_new = (l > 0.f) ? (m * scale + lg2_approx(l)) * kLn2 : kNegInf;
+      float* lse_ptr = p.lse + grow * p.Hq + head;
+      // output coefficients: out = acc * ca + O_raw * cb
+      float ca = 0.f, cb = (l > 0.f) ? vscale / l : 0.f, lse_out = lse_new;
+      bool write = valid;
+      bool read_acc = false;
+      if (valid && p.accumulate) {
+        const float acc_lse = *lse_ptr;
+        if (lse_new == kNegInf) {
+          write = false;  // this partial covers nothing for the row
+        } else if (acc_lse != kNegInf) {
+          const float mm = fmaxf(acc_lse, lse_new);
+          const float wa = ex2_approx((acc_lse - mm) * kLog2e);
+          const float wb = ex2_approx((lse_new - mm) * kLog2e);
+          const float inv = 1.0f / (wa + wb);
+          ca = wa * inv;
+          cb *= wb * inv;
+          lse_out = mm + lg2_approx(wa + wb) * kLn2;
+          read_acc = true;
+        }
+      }
+      uint8_t* orow = static_cast<uint8_t*>(p.out) + (grow * p.Hq + head) * int64_t(D) * 2;
+      const bool has_o = n_kv > 0;  // CTA-uniform
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        if (has_o) {
+          tmem_ld32(t_lane + uint32_t(TR::TM_O + c * 32), o);
+          tmem_wait_ld();
+          reg_fence32(o);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = 0u;
+        }
+        if (write) {
+          uint4* dst = reinterpret_cast<uint4*>(orow + c * 64);
+          float f[32];
+#pragma unroll
+          for (int e = 0; e < 32; ++e) f[e] = has_o ? __uint_as_float(o[e]) * cb : 0.f;
+          if (read_acc) {
+#pragma unroll
+            for (int v4 = 0; v4 < 4; ++v4) {
+              const uint4 a = dst[v4];
+              const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                float lo, hi;
+                if (p.out_bf16) {
+                  lo = __uint_as_float(w[i] << 16);
+                  hi = __uint_as_float(w[i] & 0xFFFF0000u);
+                } else {
+                  const float2 t = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+                  lo = t.x; hi = t.y;
+                }
+                f[v4 * 8 + 2 * i] = fmaf(lo, ca, f[v4 * 8 + 2 * i]);
+                f[v4 * 8 + 2 * i + 1] = fmaf(hi, ca, f[v4 * 8 + 2 * i + 1]);
+              }
+            }
+          }
+#pragma unroll
+          for (int v4 = 0; v4 < 4; ++v4) {
+            uint32_t w[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              w[i] = p.out_bf16 ? pack_bf16x2(f[v4 * 8 + 2 * i], f[v4 * 8 + 2 * i + 1])
+                                : pack_f16x2(f[v4 * 8 + 2 * i], f[v4 * 8 + 2 * i + 1]);
+            dst[v4] = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+        }
+      }
+      if (write) *lse_ptr = lse_out;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 5) tmem_dealloc(tmem, TR::TM_COLS);
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (fn == nullptr) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+// 3-D view [rows, heads, D] with a 128-byte-swizzled box of (128 bytes, 1 head, box_rows).
+int make_map(CUtensorMap* map, const void* base, int64_t rows, int heads, int D, int elem,
+             int box_rows) {
+  EncodeTiledFn enc = get_encode_fn();
+  FA4CP_CHECK_ARG(enc != nullptr, "cuTensorMapEncodeTiled is unavailable");
+  const cuuint64_t dims[3] = {cuuint64_t(D), cuuint64_t(heads), cuuint64_t(rows)};
+  const cuuint64_t strides[2] = {cuuint64_t(D) * elem, cuuint64_t(heads) * D * elem};
+  const cuuint32_t box[3] = {cuuint32_t(128 / elem), 1, cuuint32_t(box_rows)};
+  const cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = enc(map, elem == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16,
+                   3, const_cast<void*>(base), dims, strides, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_last_error("cuTensorMapEncodeTiled failed (%d)", int(r));
+    return FA4CP_ERR_CUDA;
+  }
+  return FA4CP_OK;
+}
+
+template <class TR>
+int launch(const void* q, const void* k, const void* v, int64_t total_q, int64_t total_k,
+           int max_seqlen_q, const Params& p0, cudaStream_t stream) {
+  static bool attr_set = false;
+  if (!attr_set) {
+    FA4CP_CHECK_CUDA(cudaFuncSetAttribute(attn_fwd_kernel<TR>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          TR::SMEM_BYTES));
+    attr_set = true;
+  }
+  CUtensorMap mq, mk, mv;
+  int rc = make_map(&mq, q, total_q, p0.Hq, TR::D, TR::ELEM, BM);
+  if (rc) return rc;
+  if (total_k > 0) {
+    if ((rc = make_map(&mk, k, total_k, p0.Hkv, TR::D, TR::ELEM, TR::BN))) return rc;
+    if ((rc = make_map(&mv, v, total_k, p0.Hkv, TR::D, TR::ELEM, TR::BN))) return rc;
+  } else {  // no keys anywhere: the kernel never loads K/V; any valid map will do
+    mk = mq;
+    mv = mq;
+  }
+  Params p = p0;
+  p.n_qtiles = (max_seqlen_q + BM - 1) / BM;
+  if (p.n_qtiles <= 0) return FA4CP_OK;
+  FA4CP_CHECK_ARG(p.n_qtiles <= 65535 && p.nseq <= 65535, "grid too large");
+  dim3 grid(unsigned(p.Hq), unsigned(p.n_qtiles), unsigned(p.nseq));
+  attn_fwd_kernel<TR><<<grid, kThreads, TR::SMEM_BYTES, stream>>>(mq, mk, mv, p);
+  return check_launch("attn_fwd");
+}
+
+bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
+
+}  // namespace
+}  // namespace fa4cp
+
+using namespace fa4cp;
+
+extern "C" int fa4cp_attn_fwd(const void* q, const void* k, const void* v, void* out, float* lse,
+                              const int32_t* cu_q, const int32_t* cu_k, int32_t nseq,
+                              int32_t max_seqlen_q, int64_t total_q, int64_t total_k,
+                              int32_t num_heads_q, int32_t num_heads_kv, int32_t head_dim,
+                              int32_t in_dtype, int32_t out_dtype, int32_t pattern,
+                              int32_t causal, float softmax_scale, const float* q_descale,
+                              const float* k_descale, const float* v_descale, int32_t accumulate,
+                              void* stream) {
+  FA4CP_CHECK_ARG(nseq >= 1 && cu_q != nullptr, "cu_seqlens_q must describe >= 1 sequence");
+  FA4CP_CHECK_ARG(pattern >= FA4CP_PATTERN_VARLEN && pattern <= FA4CP_PATTERN_BACK_Q,
+                  "unknown pattern %d", pattern);
+  FA4CP_CHECK_ARG(pattern != FA4CP_PATTERN_VARLEN || cu_k != nullptr, "cu_seqlens_k is required");
+  FA4CP_CHECK_ARG(num_heads_q > 0 && num_heads_kv > 0 && num_heads_q % num_heads_kv == 0,
+                  "H_q=%d not a multiple of H_kv=%d", num_heads_q, num_heads_kv);
+  FA4CP_CHECK_ARG(total_q >= 0 && total_k >= 0 && max_seqlen_q >= 0, "bad sizes");
+  FA4CP_CHECK_ARG(out_dtype == FA4CP_DTYPE_BF16 || out_dtype == FA4CP_DTYPE_F16,
+                  "output dtype must be f16 or bf16");
+  FA4CP_CHECK_ARG(softmax_scale > 0.f, "softmax_scale must be positive");
+  const bool fp8 = in_dtype == FA4CP_DTYPE_E4M3;
+  FA4CP_CHECK_ARG(fp8 || in_dtype == FA4CP_DTYPE_BF16 || in_dtype == FA4CP_DTYPE_F16,
+                  "input dtype must be f16, bf16 or e4m3");
+  FA4CP_CHECK_ARG(fp8 || (q_descale == nullptr && k_descale == nullptr && v_descale == nullptr),
+                  "descales apply to e4m3 inputs only");
+  if (total_q == 0) return FA4CP_OK;
+  FA4CP_CHECK_ARG(q && out && lse && (total_k == 0 || (k && v)), "null tensor pointer");
+  FA4CP_CHECK_ARG(aligned16(q) && aligned16(k) && aligned16(v) && aligned16(out),
+                  "q/k/v/out must be 16-byte aligned");
+
+  Params p{};
+  p.cu_q = cu_q;
+  p.cu_k = cu_k;
+  p.out = out;
+  p.lse = lse;
+  p.q_descale = q_descale;
+  p.k_descale = k_descale;
+  p.v_descale = v_descale;
+  p.nseq = nseq;
+  p.Hq = num_heads_q;
+  p.Hkv = num_heads_kv;
+  p.group = num_heads_q / num_heads_kv;
+  p.pattern = pattern;
+  p.causal = causal ? 1 : 0;
+  p.accumulate = accumulate ? 1 : 0;
+  p.in_fmt = in_dtype == FA4CP_DTYPE_BF16 ? 1 : 0;
+  p.out_bf16 = out_dtype == FA4CP_DTYPE_BF16 ? 1 : 0;
+  p.scale_log2 = softmax_scale * kLog2e;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+  if (fp8) {
+    FA4CP_CHECK_ARG(out_dtype == FA4CP_DTYPE_BF16, "e4m3 inputs produce a bf16 output");
+    if (head_dim == 128) return launch<Traits<128, 128, 3, true>>(q, k, v, total_q, total_k, max_seqlen_q, p, st);
+  } else {
+    if (head_dim == 128) return launch<Traits<128, 128, 2, false>>(q, k, v, total_q, total_k, max_seqlen_q, p, st);
+    if (head_dim == 64) return launch<Traits<64, 128, 3, false>>(q, k, v, total_q, total_k, max_seqlen_q, p, st);
+  }
+  set_last_error("head_dim %d with dtype %d is not supported", head_dim, in_dtype);
+  return FA4CP_ERR_UNSUPPORTED;
+}
+
+extern "C" int fa4cp_device_status(int32_t* status, int32_t clear) {
+  FA4CP_CHECK_ARG(status != nullptr, "status must not be NULL");
+  FA4CP_CHECK_CUDA(cudaDeviceSynchronize());
+  int v = 0;
+  FA4CP_CHECK_CUDA(cudaMemcpyFromSymbol(&v, g_attn_status, sizeof(int)));
+  if (clear) {
+    int z = 0;
+    FA4CP_CHECK_CUDA(cudaMemcpyToSymbol(g_attn_status, &z, sizeof(int)));
+  }
+  *status = v;
+  return FA4CP_OK;
+}

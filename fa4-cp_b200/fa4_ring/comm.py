@@ -1,0 +1,113 @@
+"""Chain-forward KV rotation for the zig-zag ring (replaces fa4_ring/ring_attention.py:121-171).
+
+At step ``s`` a rank attends the K/V that originated on rank ``(rank - s) mod S``.
+Hop ``s`` (``s = 1 .. S-1``) therefore sends the K/V used at step ``s-1`` to
+``rank + 1`` and receives the K/V of step ``s`` from ``rank - 1``; there are exactly
+``S - 1`` transfers and every received shard is attended (the reference's loop
+computes on the shard it holds while labelling it with the next source, so it
+attends its own KV twice and never the shard of ``rank + 1``).
+
+On CUDA the hops run as NCCL send/recv (``torch.distributed.batch_isend_irecv``)
+issued from a dedicated high-priority comm stream into two persistent receive
+buffers (ping-pong).  Ordering is by CUDA events only, no host blocking:
+
+* hop ``s`` waits for the compute of step ``s - 2`` (the last reader of the buffer it
+  overwrites); the previous hop is ordered by the comm stream itself;
+* the compute stream waits for hop ``s`` right before step ``s``.
+
+Hop ``s + 1`` is issued as soon as step ``s`` is enqueued, so it overlaps step ``s``'s
+attention.  With a CPU process group (gloo) the same schedule runs with blocking
+hops; that path exists to test the rotation logic without a GPU.
+"""
+
+from typing import Dict, Optional, Tuple
+
+import torch
+import torch.distributed as dist
+
+_COMM_STREAMS: Dict[int, torch.cuda.Stream] = {}
+
+
+def comm_stream(device: torch.device) -> torch.cuda.Stream:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    st = _COMM_STREAMS.get(idx)
+    if st is None:
+        lo, hi = torch.cuda.Stream.priority_range()
+        st = torch.cuda.Stream(device=torch.device("cuda", idx), priority=hi)
+        _COMM_STREAMS[idx] = st
+    return st
+
+
+def _global_rank(group, r: int) -> int:
+    if group is None:
+        return r
+    return dist.get_global_rank(group, r)
+
+
+class KVRing:
+    """Rotates one rank's (K, V) shard around the cp group, one hop per ring step."""
+
+    def __init__(self, k: torch.Tensor, v: torch.Tensor, cp_rank: int, cp_size: int,
+                 group: Optional["dist.ProcessGroup"] = None):
+        assert cp_size >= 2, "a ring needs at least two ranks"
+        self.S = cp_size
+        self.rank = cp_rank
+        self.group = group
+        self.send_to = _global_rank(group, (cp_rank + 1) % cp_size)
+        self.recv_from = _global_rank(group, (cp_rank - 1) % cp_size)
+        self.cuda = k.is_cuda
+        nbuf = min(2, cp_size - 1)
+        self.bufs = [(torch.empty_like(k), torch.empty_like(v)) for _ in range(nbuf)]
+        self.kv: Dict[int, Tuple[torch.Tensor, torch.Tensor]] = {0: (k, v)}
+        self.hop_done: Dict[int, torch.cuda.Event] = {}
+        self.consumed: Dict[int, torch.cuda.Event] = {}
+        self.stream = comm_stream(k.device) if self.cuda else None
+        self.hops_issued = 0
+
+    def _hop(self, s: int) -> None:
+        sk, sv = self.kv[s - 1]
+        dk, dv = self.bufs[s % len(self.bufs)]
+        ops = [
+            dist.P2POp(dist.isend, sk, self.send_to, group=self.group),
+            dist.P2POp(dist.irecv, dk, self.recv_from, group=self.group),
+            dist.P2POp(dist.isend, sv, self.send_to, group=self.group),
+            dist.P2POp(dist.irecv, dv, self.recv_from, group=self.group),
+        ]
+        if self.cuda:
+            with torch.cuda.stream(self.stream):
+                prev_reader = self.consumed.get(s - 2)
+                if prev_reader is not None:
+                    self.stream.wait_event(prev_reader)
+                for req in dist.batch_isend_irecv(ops):
+                    req.wait()  # comm stream waits for NCCL; the host does not block
+                ev = torch.cuda.Event()
+                ev.record(self.stream)
+            self.hop_done[s] = ev
+        else:
+            for req in dist.batch_isend_irecv(ops):
+                req.wait()
+        self.kv[s] = (dk, dv)
+        self.hops_issued = s
+
+    def start(self) -> None:
+        """Issue hop 1 (overlaps the local step 0)."""
+        self._hop(1)
+
+    def get(self, s: int) -> Tuple[torch.Tensor, torch.Tensor]:
+        """K/V of step ``s``; the current stream is made to wait for its arrival, and
+        the next hop is issued so that it overlaps step ``s``."""
+        if s == 0:
+            return self.kv[0]
+        assert s <= self.hops_issued, "hops are issued in order"
+        if self.cuda:
+            torch.cuda.current_stream(self.kv[0][0].device).wait_event(self.hop_done[s])
+        if s + 1 < self.S:
+            self._hop(s + 1)
+        return self.kv[s]
+
+    def done(self, s: int) -> None:
+        """Mark step ``s``'s compute as enqueued; its K/V buffer may be reused after it."""
+        if self.cuda:
+            ev = torch.cuda.Event()
+            ev.record(torch.cuda.current_stream(self.kv[0][0].device))
+            self.consumed[s] = ev

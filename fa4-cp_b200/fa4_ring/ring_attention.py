@@ -1,0 +1,187 @@
+"""Zig-zag causal ring attention on B200 (mirrors ``fa4_ring/ring_attention.py:43-174``).
+
+Each rank holds ``2h`` local tokens ``[early half | late half]`` per sequence (see
+:mod:`.zigzag`) and runs ``cp_size`` steps; step ``s`` attends the K/V that
+originated on rank ``src = (rank - s) mod cp_size``:
+
+* step 0 (``src == rank``): causal attention over the local tokens;
+* ``s <= rank`` (``src`` is earlier): all local Q x the early half of the source KV;
+* ``s > rank``  (``src`` is later):  the late half of local Q x all of the source KV.
+
+Per step, one launch of the sm_100a attention kernel does the step's attention on
+the rows the pattern selects, in place (no ``index_select`` / ``index_copy_``
+staging), and in ``incremental`` mode merges the partial into the running
+``(out, lse)`` in its epilogue.  ``batched`` mode keeps every partial and runs one
+k-way merge kernel at the end.  The K/V rotation (:class:`.comm.KVRing`) overlaps
+each step's attention with the next hop's transfer.
+"""
+
+import math
+from dataclasses import dataclass
+from typing import Dict, List, Optional, Tuple
+
+import torch
+import torch.distributed as dist
+
+from . import _lib
+from .attn_backend import (PATTERN_BACK_Q, PATTERN_FRONT_KV, PATTERN_VARLEN, _check_qkv,
+                           attn_into, norm_descale, out_dtype_for)
+from .comm import KVRing
+from .config import RingConfig
+from .merge import merge_states
+
+
+@dataclass
+class Descales:
+    """FP8 descales (fa4_ring/ring_attention.py:43-52).  ``k``/``v`` are indexed by the
+    SOURCE rank whose KV is being attended (all-gather them once before the call).
+    Each entry is a float32 tensor: a scalar, ``[H_kv]`` or ``(1, H_kv)``."""
+
+    q: Optional[torch.Tensor] = None
+    k: Optional[List[torch.Tensor]] = None
+    v: Optional[List[torch.Tensor]] = None
+
+
+def ring_schedule(rank: int, cp_size: int) -> List[Tuple[int, int, int]]:
+    """``(step, src, pattern)`` for every step of ``rank``."""
+    sched = [(0, rank, PATTERN_VARLEN)]
+    for s in range(1, cp_size):
+        src = (rank - s) % cp_size
+        sched.append((s, src, PATTERN_BACK_Q if s > rank else PATTERN_FRONT_KV))
+    return sched
+
+
+_CU_CACHE: Dict[Tuple[int, int], torch.Tensor] = {}
+
+
+def _single_cu(total: int, device: torch.device) -> torch.Tensor:
+    key = (device.index if device.index is not None else -1, total)
+    cu = _CU_CACHE.get(key)
+    if cu is None:
+        cu = torch.tensor([0, total], dtype=torch.int32, device=device)
+        _CU_CACHE[key] = cu
+    return cu
+
+
+def _validate_cu(cu) -> None:
+    vals = [int(c) for c in (cu.tolist() if torch.is_tensor(cu) else cu)]
+    assert vals and vals[0] == 0, "cu_seqlens must start at 0"
+    for a, b in zip(vals[:-1], vals[1:]):
+        assert b >= a, "cu_seqlens must be non-decreasing"
+        assert (b - a) % 2 == 0, "each local sequence length must be even (zig-zag)"
+
+
+def ring_flash_attn(
+    local_q: torch.Tensor,   # [T, H, D]   zig-zag local shard
+    local_k: torch.Tensor,   # [T, H_kv, D]
+    local_v: torch.Tensor,   # [T, H_kv, D]
+    cfg: RingConfig,
+    *,
+    group: Optional["dist.ProcessGroup"] = None,
+    descales: Optional[Descales] = None,
+    cu_seqlens: Optional[torch.Tensor] = None,  # local int32 [num_seq+1]; None -> one sequence
+    max_seqlen: Optional[int] = None,
+) -> torch.Tensor:
+    """Causal ring attention; returns this rank's local output ``[T, H, D]``.
+
+    One sequence per rank: leave ``cu_seqlens=None``.  Packed sequences: pass the
+    LOCAL ``cu_seqlens`` (each entry already the zig-zag ``2*h_j`` shard length) and
+    ``max_seqlen`` (max local shard length).  ``cu_seqlens`` given on the host is
+    validated (even lengths); a CUDA ``cu_seqlens`` is trusted, to avoid a sync.
+    Output dtype: the input dtype, or bf16 for e4m3 inputs.
+    """
+    _check_qkv(local_q, local_k, local_v)
+    S, rank = cfg.cp_size, cfg.cp_rank
+    T, Hq, D = local_q.shape
+    assert local_k.shape[0] == T, "q and kv shards must have the same token count"
+    dev = local_q.device
+
+    if cu_seqlens is None:
+        assert T % 2 == 0, "the local shard length must be even (zig-zag)"
+        cu = _single_cu(T, dev)
+        max_seqlen = T
+    else:
+        assert max_seqlen is not None, "max_seqlen required when cu_seqlens is given"
+        if not cu_seqlens.is_cuda:
+            _validate_cu(cu_seqlens)
+        cu = cu_seqlens.to(device=dev, dtype=torch.int32).contiguous()
+    nseq = cu.numel() - 1
+    max_seqlen = int(max_seqlen)
+
+    k0 = local_k.contiguous()
+    v0 = local_v.contiguous()
+    ring = KVRing(k0, v0, rank, S, group) if S > 1 else None
+    if ring is not None:
+        ring.start()  # hop 1 overlaps the local step
+
+    def kv_at(step):
+        return ring.get(step) if (ring is not None and step > 0) else (k0, v0)
+
+    def step_done(step):
+        if ring is not None:
+            ring.done(step)
+
+    return ring_forward(local_q, kv_at, step_done, cfg, cu=cu, nseq=nseq, max_seqlen=max_seqlen,
+                        descales=descales)
+
+
+def ring_forward(local_q, kv_at, step_done, cfg: RingConfig, *, cu: torch.Tensor, nseq: int,
+                 max_seqlen: int, descales: Optional[Descales] = None) -> torch.Tensor:
+    """The per-step compute of :func:`ring_flash_attn` for one rank.
+
+    ``kv_at(step)`` returns the (K, V) that originated on ``(rank - step) mod S`` (the
+    ring supplies it after its hop; a single-GPU test supplies every rank's shard
+    directly); ``step_done(step)`` is called after the step's kernels are enqueued.
+    """
+    S, rank = cfg.cp_size, cfg.cp_rank
+    T, Hq, D = local_q.shape
+    dev = local_q.device
+    scale = cfg.softmax_scale if cfg.softmax_scale is not None else 1.0 / math.sqrt(D)
+    q = local_q.contiguous()
+    k0, _ = kv_at(0)
+    Hkv = k0.shape[1]
+    fp8 = q.dtype == torch.float8_e4m3fn
+    qd = norm_descale(descales.q, Hkv, dev) if (fp8 and descales and descales.q is not None) else None
+
+    def kd(src):
+        if fp8 and descales and descales.k:
+            return norm_descale(descales.k[src], Hkv, dev)
+        return None
+
+    def vd(src):
+        if fp8 and descales and descales.v:
+            return norm_descale(descales.v[src], Hkv, dev)
+        return None
+
+    out_dt = out_dtype_for(q.dtype)
+    batched = cfg.merge_mode == "batched"
+    out = torch.empty((T, Hq, D), dtype=out_dt, device=dev)
+    lse = torch.empty((T, Hq), dtype=torch.float32, device=dev)
+    partials = [(out, lse)]
+    stream = _lib.stream_of(q)
+    lib = _lib.load()
+
+    for step, src, pattern in ring_schedule(rank, S):
+        k, v = kv_at(step)
+        q_rows = (max_seqlen + 1) // 2 if pattern == PATTERN_BACK_Q else max_seqlen
+        if step == 0 or not batched:
+            o_t, l_t, acc = out, lse, step > 0
+        else:
+            o_t = torch.empty((T, Hq, D), dtype=out_dt, device=dev)
+            l_t = torch.empty((T, Hq), dtype=torch.float32, device=dev)
+            if pattern == PATTERN_BACK_Q:  # rows this step does not cover: identity
+                _lib.check(lib.fa4cp_fill_f32(l_t.data_ptr(), l_t.numel(), float("-inf"), stream),
+                           "fill_f32")
+            partials.append((o_t, l_t))
+            acc = False
+        attn_into(q, k, v, o_t, l_t, cu, cu, nseq=nseq, max_seqlen_q=q_rows, pattern=pattern,
+                  causal=(step == 0), softmax_scale=scale, q_descale=qd, k_descale=kd(src),
+                  v_descale=vd(src), accumulate=acc)
+        step_done(step)
+
+    if batched and len(partials) > 1:
+        final = torch.empty((T, Hq, D), dtype=out_dt, device=dev)
+        merge_states([p[0] for p in partials], [p[1] for p in partials], out=final,
+                     lse_out=torch.empty((T, Hq), dtype=torch.float32, device=dev))
+        return final
+    return out

@@ -1,0 +1,167 @@
+/*
+ * fa4cp_b200 -- C ABI of the B200 (sm_100a) zig-zag ring-attention hot path.
+ *
+ * The reference (hxy0118/fa4-cp, package `fa4_ring`) is pure Python: its GPU work
+ * goes through third-party Python-callable kernels (FlashAttention-4
+ * `_flash_attn_fwd`, flashinfer `cascade.merge_state_in_place` / `merge_states`)
+ * and ATen indexing.  Each entry point below replaces one of those call sites;
+ * the citation names the reference file:line of the call it stands in for.
+ *
+ * Conventions (all entry points):
+ *   - every pointer argument is a DEVICE pointer unless documented as host;
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream);
+ *   - tensors are contiguous, row-major: Q/O [T, H, D], K/V [T, Hkv, D], LSE [T, H];
+ *   - LSE is float32 natural log, layout [T, H];
+ *   - nothing is allocated; every launch is asynchronous on `stream`;
+ *   - return 0 on success or a negative FA4CP_ERR_* code; fa4cp_last_error()
+ *     returns a description of the most recent failure of the calling thread.
+ */
+#ifndef FA4CP_B200_H_
+#define FA4CP_B200_H_
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define FA4CP_API __attribute__((visibility("default")))
+#else
+#define FA4CP_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define FA4CP_OK 0
+#define FA4CP_ERR_INVALID (-1)     /* bad argument (maps to AssertionError/ValueError) */
+#define FA4CP_ERR_UNSUPPORTED (-2) /* valid but not implemented (head_dim, dtype, ...) */
+#define FA4CP_ERR_CUDA (-3)        /* CUDA runtime/driver error */
+#define FA4CP_ERR_DEVICE (-4)      /* a kernel gave up a bounded wait (see device status) */
+
+/* element types */
+#define FA4CP_DTYPE_F16 0
+#define FA4CP_DTYPE_BF16 1
+#define FA4CP_DTYPE_F32 2
+#define FA4CP_DTYPE_E4M3 3
+
+/* ring step patterns (fa4_ring/ring_attention.py:11-16) */
+#define FA4CP_PATTERN_VARLEN 0   /* q rows [cu_q[j],cu_q[j+1]) x k rows [cu_k[j],cu_k[j+1]) */
+#define FA4CP_PATTERN_FRONT_KV 1 /* q rows [cu[j],cu[j+1]) x k rows [cu[j], mid_j)  (step <= rank) */
+#define FA4CP_PATTERN_BACK_Q 2   /* q rows [mid_j,cu[j+1]) x k rows [cu[j],cu[j+1]) (step > rank) */
+
+/* Library version (major*10000 + minor*100 + patch). */
+FA4CP_API int fa4cp_version(void);
+
+/* Text of the calling thread's most recent error ("" if none). */
+FA4CP_API const char* fa4cp_last_error(void);
+
+/*
+ * Device status word written by kernels that gave up a bounded wait (0 = ok).
+ * Synchronises the current device.  If `clear` != 0 the word is reset to 0.
+ */
+FA4CP_API int fa4cp_device_status(int32_t* status, int32_t clear);
+
+/*
+ * Variable-length attention forward returning out + LSE; also the three zig-zag
+ * ring step patterns with in-place row addressing (no gathers).
+ *
+ * Replaces: fa4_ring/fa4_backend.py:58-123 (FA4 `_flash_attn_fwd` call :106-120,
+ * LSE transpose :121-122) and the step-pattern row selections of
+ * fa4_ring/ring_attention.py:109-166 (index_select/index_copy_ staging).
+ *
+ *   q            [total_q, Hq, D]   f16 | bf16 | e4m3
+ *   k, v         [total_k, Hkv, D]  same dtype as q
+ *   out          [total_q, Hq, D]   out_dtype (f16 | bf16; bf16 for e4m3 inputs)
+ *   lse          [total_q, Hq]      float32, natural log
+ *   cu_q         int32 [nseq+1]     query sequence boundaries (local cu for patterns 1,2)
+ *   cu_k         int32 [nseq+1]     key boundaries (pattern VARLEN only; may equal cu_q)
+ *   max_seqlen_q upper bound on any cu_q[j+1]-cu_q[j] (sizes the grid)
+ *   pattern      FA4CP_PATTERN_*
+ *   causal       1: key j visible to query i iff j <= i + (Tk - Tq)  (Tq == Tk: tril)
+ *   softmax_scale  multiplier of q.k (the caller passes 1/sqrt(D) for the default)
+ *   q/k/v_descale  NULL or float32 [Hkv] (e4m3 only): scores *= qd*kd, out *= vd
+ *   accumulate   0: write out/lse of the covered rows;
+ *                1: merge this partial into (out, lse) in place, online-softmax,
+ *                   natural-log (the incremental merge of fa4_ring/merge.py:45-64 fused
+ *                   into the epilogue); rows not covered are left untouched.
+ * Supported: head_dim 64 or 128 (f16/bf16), 128 (e4m3); Hq % Hkv == 0.
+ */
+FA4CP_API int fa4cp_attn_fwd(const void* q, const void* k, const void* v, void* out, float* lse,
+                   const int32_t* cu_q, const int32_t* cu_k, int32_t nseq, int32_t max_seqlen_q,
+                   int64_t total_q, int64_t total_k, int32_t num_heads_q, int32_t num_heads_kv,
+                   int32_t head_dim, int32_t in_dtype, int32_t out_dtype, int32_t pattern,
+                   int32_t causal, float softmax_scale, const float* q_descale,
+                   const float* k_descale, const float* v_descale, int32_t accumulate,
+                   void* stream);
+
+/*
+ * In-place 2-way LSE merge: (v, s) <- merge((v, s), (v_other, s_other)).
+ * Replaces: flashinfer `cascade.merge_state_in_place` as called by
+ * fa4_ring/merge.py:31-36,60 (with natural-log LSE, fa4_ring/merge.py:17-18).
+ *   v, v_other [num_rows, num_heads, head_dim] dtype (f16 | bf16 | f32); s, s_other [num_rows, num_heads]
+ * Rows where s_other is -inf are left unchanged; head_dim % 8 == 0 (f16/bf16), % 4 (f32).
+ */
+FA4CP_API int fa4cp_merge_state_inplace(void* v, float* s, const void* v_other, const float* s_other,
+                              int64_t num_rows, int32_t num_heads, int32_t head_dim, int32_t dtype,
+                              void* stream);
+
+/*
+ * k-way LSE merge of `num_states` partials read through pointer arrays (no stack copy).
+ * Replaces: flashinfer `cascade.merge_states` after torch.stack, fa4_ring/merge.py:39-42,83-85.
+ *   v_ptrs, s_ptrs  HOST arrays of `num_states` device pointers (1 <= num_states <= 32)
+ *   v_out [num_rows, num_heads, head_dim] dtype; s_out [num_rows, num_heads] float32 (may be NULL)
+ */
+FA4CP_API int fa4cp_merge_states(const void* const* v_ptrs, const float* const* s_ptrs, int32_t num_states,
+                       void* v_out, float* s_out, int64_t num_rows, int32_t num_heads,
+                       int32_t head_dim, int32_t dtype, void* stream);
+
+/*
+ * Fill a float32 buffer with `value` (used to mark rows a partial does not cover
+ * with LSE = -inf, as fa4_ring/ring_attention.py:162-163 does with torch.full).
+ */
+FA4CP_API int fa4cp_fill_f32(float* dst, int64_t n, float value, void* stream);
+
+/*
+ * Zig-zag gather: this rank's local shard of every packed sequence.
+ * Replaces: fa4_ring/zigzag.py:31-39 (`zigzag_shard`) and :82-97 (`zigzag_shard_varlen`).
+ *   x        [total_full, row_bytes] bytes; out [total_full / cp_size, row_bytes]
+ *   full_cu  int32 [nseq+1] device boundaries of the FULL sequences, or NULL for a
+ *            single sequence of total_full rows; every length must be divisible by
+ *            2*cp_size (the caller validates; the kernel trusts it).
+ */
+FA4CP_API int fa4cp_zigzag_shard(const void* x, void* out, const int32_t* full_cu, int32_t nseq,
+                       int64_t total_full, int32_t cp_rank, int32_t cp_size, int64_t row_bytes,
+                       void* stream);
+
+/*
+ * Zig-zag scatter: stitch all ranks' local shards back into the full packed sequence.
+ * Replaces: fa4_ring/zigzag.py:42-50 (`zigzag_unshard`) and the per-sequence stitching of
+ * the reference's tests (tests/test_ring_correctness.py:29-36).
+ *   shards   HOST array of `cp_size` device pointers, each [total_full / cp_size, row_bytes]
+ *   out      [total_full, row_bytes]; full_cu as for fa4cp_zigzag_shard (NULL = one sequence)
+ */
+FA4CP_API int fa4cp_zigzag_unshard(const void* const* shards, void* out, const int32_t* full_cu,
+                         int32_t nseq, int64_t total_full, int32_t cp_size, int64_t row_bytes,
+                         void* stream);
+
+/*
+ * Device-side `get_half_index` (no host sync): int64 indices of the front (front=1)
+ * or back (front=0) half of each packed local sequence.
+ * Replaces: fa4_ring/zigzag.py:65-79 (`.tolist()` + Python loop of arange).
+ *   cu int32 [nseq+1] (each length even); out_idx int64 [total / 2]
+ */
+FA4CP_API int fa4cp_half_index(const int32_t* cu, int32_t nseq, int64_t total, int32_t front,
+                     int64_t* out_idx, void* stream);
+
+/*
+ * local_cu[j] = full_cu[j] / cp_size for j in [0, nseq]  (the local cu_seqlens that
+ * fa4_ring/zigzag.py:94-97 builds on the host).
+ */
+FA4CP_API int fa4cp_local_cu(const int32_t* full_cu, int32_t nseq, int32_t cp_size, int32_t* local_cu,
+                   void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FA4CP_B200_H_ */

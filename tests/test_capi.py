@@ -1,0 +1,80 @@
+"""The C-ABI library loads and exports exactly what include/fa4cp_b200.h declares.
+
+Host-side argument validation of the boundary is exercised too; every call here
+returns before any CUDA API call, so no GPU is needed.
+"""
+
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+from conftest import ROOT
+
+HEADER = os.path.join(ROOT, "include", "fa4cp_b200.h")
+
+
+def _declared():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"FA4CP_API\s+[\w\s\*]+?\b(fa4cp_\w+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from fa4_ring import _build, _lib
+    _build.build()
+    return _lib.load()
+
+
+def test_header_declares_the_boundary():
+    names = _declared()
+    for n in ("fa4cp_attn_fwd", "fa4cp_merge_state_inplace", "fa4cp_merge_states",
+              "fa4cp_zigzag_shard", "fa4cp_zigzag_unshard", "fa4cp_half_index"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol(lib):
+    from fa4_ring import _lib
+    for name in _declared():
+        assert hasattr(lib, name), name
+    assert set(_declared()) == set(_lib.EXPORTED)
+    out = subprocess.run(["nm", "-D", "--defined-only", _lib.LIB_PATH], capture_output=True,
+                         text=True).stdout
+    exported = sorted(set(re.findall(r" T (fa4cp_\w+)", out)))
+    assert exported == _declared()
+
+
+def test_version_and_error_text(lib):
+    assert lib.fa4cp_version() >= 100
+    rc = lib.fa4cp_merge_states(None, None, 0, None, None, 1, 1, 8, 1, None)
+    assert rc == -1
+    assert b"num_states" in lib.fa4cp_last_error()
+
+
+@pytest.mark.parametrize("args,needle", [
+    # bad head ratio
+    (dict(hq=6, hkv=4), b"multiple"),
+    # unknown pattern
+    (dict(pattern=7), b"pattern"),
+    # unsupported dtype combination
+    (dict(in_dtype=2), b"dtype"),
+])
+def test_attn_argument_validation(lib, args, needle):
+    a = dict(hq=8, hkv=2, pattern=0, in_dtype=1)
+    a.update(args)
+    dummy = ctypes.c_void_p(16)
+    rc = lib.fa4cp_attn_fwd(dummy, dummy, dummy, dummy, dummy, dummy, dummy, 1, 128, 128, 128,
+                            a["hq"], a["hkv"], 128, a["in_dtype"], 1, a["pattern"], 1, 0.1,
+                            None, None, None, 0, None)
+    assert rc == -1
+    assert needle in lib.fa4cp_last_error()
+
+
+def test_zigzag_argument_validation(lib):
+    dummy = ctypes.c_void_p(16)
+    assert lib.fa4cp_zigzag_shard(dummy, dummy, None, 1, 10, 0, 2, 4, None) == -1  # 10 % 4 != 0
+    assert b"divisible" in lib.fa4cp_last_error()
+    assert lib.fa4cp_zigzag_shard(dummy, dummy, None, 1, 8, 2, 2, 4, None) == -1   # rank >= cp
+    assert lib.fa4cp_half_index(dummy, 1, 7, 1, dummy, None) == -1                  # odd total
