@@ -1,0 +1,424 @@
+"""Benchmark of the zig-zag causal ring-attention forward on B200.
+
+Workload ("cfg2"): one causal ring-attention forward over a
+bf16 sequence of N=32768 tokens, Hq=32, Hkv=8, D=128, softmax scale 1/sqrt(128),
+q/k/v ~ N(0,1) from a seed, cp = number of GPUs, merge_mode incremental.  The
+total work is fixed as cp grows ("strong" scaling).  Metric: causal FLOPs
+(2*N^2*Hq*D per forward) per second, whole job, in TFLOP/s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...        (N > 1)
+
+One JSON line on rank 0.  ``value``: device time with inputs resident in HBM, max
+over ranks, L2 flushed (256 MiB write) before every timed step.  ``e2e``: the same
+forward through the public API with the step's Q/K/V shards copied in from pinned
+host memory and the output copied back, inside the timed region.  ``roofline``:
+the attention kernel (the dominant kernel) -- algorithmic FLOPs / its CUDA-event
+time, against the measured bf16 peak.  ``cpu_baseline``: the numpy restatement of
+the reference's CPU ring simulation (``oracle/``) on rank 0's share of the ring at
+cp=8 (a bounded sample), on the host cores.  ``--impl reference`` times that CPU
+path alone (the reference is pure Python over third-party GPU kernels that are not
+installed here and its GPU orchestration attends wrong KV shards; its own CPU
+simulation is the path that runs).
+"""
+
+import argparse
+import datetime
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path[:0] = [ROOT, os.path.join(ROOT, "fa4-cp_b200")]
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+METRIC = "causal ring-attn prefill TFLOP/s/GPU @cp=1/2/4/8; % tensor peak; exposed comm %"
+CFG2 = dict(N=32768, Hq=32, Hkv=8, D=128)
+L2_FLUSH_BYTES = 256 << 20
+
+
+def causal_flops(N, Hq, D):
+    return 2.0 * N * N * Hq * D
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p, "measured"
+    except (OSError, ValueError):
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+# --------------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = os.path.join("/tmp", f"fa4cp_clocks_{os.getpid()}.csv")
+
+    def __enter__(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
+                stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    mx = float(parts[2])
+                except ValueError:
+                    continue
+                for name, val in zip(names, parts[5:9]):
+                    if val.lower() == "active":
+                        reasons.add(name)
+        os.unlink(self.path)
+        busy = [s for s in sm if mx and s > 0.3 * mx] or sm
+        return {"sm_mhz": statistics.median(busy) if busy else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------- CPU baseline
+def cpu_sample(rank_steps=None, threads=None):
+    """Time the oracle (numpy restatement of the reference's CPU ring simulation) on rank 0's
+    share of the cfg2 ring at cp=8: every step of rank 0 (or the given subset), all heads.
+    Returns (flops, seconds, threads)."""
+    from threadpoolctl import threadpool_info, threadpool_limits
+
+    from oracle import ring_oracle as orc
+    threads = threads or os.cpu_count() or 1
+    limiter = threadpool_limits(limits=threads)
+    info = threadpool_info()
+    threads = max([i.get("num_threads", 1) for i in info if i.get("user_api") == "blas"] or [1])
+    N, Hq, Hkv, D = CFG2["N"], CFG2["Hq"], CFG2["Hkv"], CFG2["D"]
+    cp, rank = 8, 0
+    T = N // cp
+    rng = np.random.default_rng(0)
+    q = rng.standard_normal((T, Hq, D), dtype=np.float32)
+    k = rng.standard_normal((T, Hkv, D), dtype=np.float32)
+    v = rng.standard_normal((T, Hkv, D), dtype=np.float32)
+    scale = 1.0 / math.sqrt(D)
+    sched = orc.ring_schedule(rank, cp)
+    if rank_steps is not None:
+        sched = [sched[i % len(sched)] for i in rank_steps]
+    flops = 0.0
+    t0 = time.perf_counter()
+    acc = None
+    for (_step, _src, pat) in sched:
+        o, l = orc.ring_step(q, k, v, [0, T], pat, scale)
+        acc = (o, l) if acc is None else orc.merge(acc[0], acc[1], o, l)
+        # local causal T x T (N^2/2 convention) and T x T/2 non-causal both count 2*T^2*Hq*D
+        flops += 2.0 * T * T * Hq * D
+    dt = time.perf_counter() - t0
+    limiter.restore_original_limits()
+    return flops, dt, threads
+
+
+# --------------------------------------------------------------------------- GPU arm
+def gpu_main(args, rank, world, local_rank):
+    from fa4_ring import RingConfig, ring_flash_attn, zigzag_shard
+    from fa4_ring import _lib, attn_backend
+    from fa4_ring.ring_attention import ring_forward, _single_cu
+
+    dev = torch.device("cuda", local_rank)
+    Hq, Hkv, D = CFG2["Hq"], CFG2["Hkv"], CFG2["D"]
+    N = args.seq_len
+    cp = world
+    assert N % (2 * cp) == 0
+    g = torch.Generator(device=dev).manual_seed(1234)
+    shards = []
+    for h in (Hq, Hkv, Hkv):
+        full = torch.randn(N, h, D, generator=g, device=dev, dtype=torch.bfloat16)
+        shards.append(zigzag_shard(full, rank, cp))
+        del full
+    lq, lk, lv = shards
+    cfg = RingConfig(cp_size=cp, cp_rank=rank, merge_mode=args.merge)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    step_flops = causal_flops(N, Hq, D)  # whole job, per step
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def run():
+        return ring_flash_attn(lq, lk, lv, cfg)
+
+    # ---- warm-up
+    for _ in range(args.warmup):
+        run()
+    torch.cuda.synchronize()
+    _lib.device_status()
+
+    # ---- timed: K steps, L2 flushed before each (untimed), per-step CUDA events
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    launches = []
+    attn_backend.launch_timer = launches
+    barrier()
+    torch.cuda.synchronize()
+    n_launch0 = _lib.launch_count
+    with ClockSampler(local_rank) as clk:
+        for i in range(args.steps):
+            flush.zero_()
+            ev[i][0].record()
+            run()
+            ev[i][1].record()
+        torch.cuda.synchronize()
+        barrier()
+    attn_backend.launch_timer = None
+    gpu_launches = _lib.launch_count - n_launch0
+    clocks = clk.summary()
+    ms_local = sum(a.elapsed_time(b) for a, b in ev)
+    attn_ms_local = sum(a.elapsed_time(b) for a, b, _ in launches)
+    n_attn_local = len(launches)
+    status = _lib.device_status()
+
+    # ---- exposed communication: same schedule with the transfers skipped
+    exposed = None
+    if world > 1 and not args.quick:
+        cu = _single_cu(lq.shape[0], dev)
+
+        def run_nocomm():
+            return ring_forward(lq, lambda s: (lk, lv), lambda s: None, cfg, cu=cu, nseq=1,
+                                max_seqlen=lq.shape[0])
+        for _ in range(2):
+            run_nocomm()
+        torch.cuda.synchronize()
+        ev2 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(args.steps)]
+        barrier()
+        for i in range(args.steps):
+            flush.zero_()
+            ev2[i][0].record()
+            run_nocomm()
+            ev2[i][1].record()
+        torch.cuda.synchronize()
+        barrier()
+        ms_nocomm_local = sum(a.elapsed_time(b) for a, b in ev2)
+    else:
+        ms_nocomm_local = ms_local
+
+    if args.quick:  # profiling runs: timed loop only
+        vals = torch.tensor([ms_local, attn_ms_local], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+        if rank == 0:
+            ms_step = vals[0].item() / args.steps
+            return {"quick": True, "seq_len": N, "cp": cp, "ms_per_step": round(ms_step, 4),
+                    "value": round(causal_flops(N, Hq, D) / (ms_step * 1e-3) / 1e12, 2),
+                    "attn_ms": round(vals[1].item() / args.steps, 4), "gpu_launches": gpu_launches,
+                    "device_status": status}
+        return None
+
+    # ---- end to end through the public API: pinned host in, host out
+    hq, hk, hv = (t.cpu().pin_memory() for t in (lq, lk, lv))
+    hout = torch.empty(lq.shape, dtype=torch.bfloat16).pin_memory()
+    dq, dk, dv = torch.empty_like(lq), torch.empty_like(lk), torch.empty_like(lv)
+
+    def run_e2e():
+        dq.copy_(hq, non_blocking=True)
+        dk.copy_(hk, non_blocking=True)
+        dv.copy_(hv, non_blocking=True)
+        out = ring_flash_attn(dq, dk, dv, cfg)
+        hout.copy_(out, non_blocking=True)
+
+    for _ in range(2):
+        run_e2e()
+    torch.cuda.synchronize()
+    e2e_steps = max(1, min(args.steps, 10))
+    ev3 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(e2e_steps)]
+    barrier()
+    torch.cuda.synchronize()
+    for i in range(e2e_steps):
+        flush.zero_()
+        ev3[i][0].record()
+        run_e2e()
+        ev3[i][1].record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms_local = sum(a.elapsed_time(b) for a, b in ev3) / e2e_steps
+    h2d = sum(t.numel() * t.element_size() for t in (hq, hk, hv))
+    d2h = hout.numel() * hout.element_size()
+
+    # ---- reduce over ranks (max)
+    vals = torch.tensor([ms_local, attn_ms_local, e2e_ms_local, ms_nocomm_local, float(status)],
+                        dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    ms_total, attn_ms, e2e_ms, ms_nocomm, status_max = vals.tolist()
+    if world > 1 and ms_total > 0:
+        exposed = max(0.0, (ms_total - ms_nocomm) / ms_total * 100.0)
+
+    if rank != 0:
+        return None
+    ms_step = ms_total / args.steps
+    value = step_flops / (ms_step * 1e-3) / 1e12
+    peaks, peaks_kind = load_peaks()
+    # attention roofline: every attention launch of one rank in the timed region;
+    # algorithmic FLOPs of one rank per step = 2*N^2*Hq*D / cp
+    attn_flops_rank = step_flops / cp * args.steps
+    achieved = attn_flops_rank / (attn_ms * 1e-3) / 1e12 if attn_ms > 0 else None
+    peak = peaks["bf16_tflops"]
+    line = {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 4),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic: q/k/v ~ N(0,1) bf16 from seed 1234",
+        "config": {"workload": f"cfg2: causal ring-attention forward, bf16, N={N}, Hq=32, "
+                               f"Hkv=8, D=128, scale=1/sqrt(128), cp={cp}, merge={args.merge}",
+                   "seq_len": N, "num_heads_q": Hq, "num_heads_kv": Hkv, "head_dim": D,
+                   "cp": cp, "merge_mode": args.merge, "parallelism": f"cp{cp} zig-zag ring",
+                   "l2": "flushed before every timed step (256 MiB write, untimed)"},
+        "per_gpu_tflops": round(value / world, 2),
+        "pct_tensor_peak": round(value / world / peak * 100.0, 2),
+        "exposed_comm_pct": None if exposed is None else round(exposed, 2),
+        "roofline": {"bound": "tensor", "kernel": "fa4cp attn_fwd (tcgen05)",
+                     "achieved": None if achieved is None else round(achieved, 1),
+                     "peak": peak, "peak_kind": f"{peaks_kind} bf16 dense (burst)",
+                     "unit": "TFLOP/s",
+                     "frac": None if achieved is None else round(achieved / peak, 4),
+                     "launches_per_step": n_attn_local // max(args.steps, 1),
+                     "traffic": None},
+        "e2e": {"value": round(step_flops / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": round(e2e_ms, 3)},
+        "gpu_launches": gpu_launches,
+        "clocks": clocks,
+        "device_status": int(status_max),
+    }
+    if world == 1:
+        flops_cpu, secs_cpu, threads = cpu_sample()
+        line["cpu_baseline"] = {
+            "value": round(flops_cpu / secs_cpu / 1e12, 5), "unit": "TFLOP/s", "cores": threads,
+            "kind": "port",
+            "sample": "oracle (numpy restatement of the reference's CPU ring simulation) on "
+                      "rank 0 of cfg2 at cp=8: all 8 ring steps, 32 heads, T=4096 local "
+                      f"tokens; {flops_cpu:.3e} FLOP in {secs_cpu:.1f} s"}
+    traffic = _traffic_from_profile(world)
+    if traffic is not None:
+        line["roofline"]["traffic"] = traffic
+    return line
+
+
+def _traffic_from_profile(world):
+    """DRAM bytes per attention launch from the committed ncu summary, if present."""
+    path = os.path.join(ROOT, "profiles", "attn_fwd_traffic.json")
+    try:
+        with open(path) as f:
+            t = json.load(f)
+        return t.get(f"cp{world}")
+    except (OSError, ValueError):
+        return None
+
+
+# --------------------------------------------------------------------------- reference arm
+def reference_main(args):
+    """The reference's CPU ring simulation (restated in numpy, ``oracle/``) on the host
+    cores: each step is a bounded sample -- one ring step of rank 0 of cfg2 at cp=8."""
+    threads = os.cpu_count() or 1
+    for i in range(args.warmup):
+        cpu_sample(rank_steps=[i], threads=threads)
+    flops = secs = 0.0
+    for i in range(args.steps):
+        f, s, _ = cpu_sample(rank_steps=[i], threads=threads)
+        flops += f
+        secs += s
+    value = flops / secs / 1e12
+    return {
+        "metric": METRIC, "impl": "reference", "value": round(value, 5), "unit": "TFLOP/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(secs / args.steps * 1e3, 2), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "cfg2 (N=32768, Hq=32, Hkv=8, D=128) ring at cp=8, rank 0; one "
+                               "ring step per bench step", "parallelism": "host threads"},
+        "cpu_baseline": {"value": round(value, 5), "unit": "TFLOP/s", "cores": threads,
+                         "kind": "port",
+                         "sample": "one ring step (T=4096 local tokens, 32 heads) of rank 0 of "
+                                   "cfg2 at cp=8 per bench step, cycling through the 8 steps"},
+        "e2e": {"value": round(value, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--merge", choices=["incremental", "batched"], default="incremental")
+    ap.add_argument("--seq-len", type=int, default=CFG2["N"],
+                    help="total tokens (the cfg2 workload is 32768; smaller only for profiling)")
+    ap.add_argument("--quick", action="store_true",
+                    help="profiling run: timed loop only (no e2e, no CPU baseline)")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        print(json.dumps(reference_main(args)), flush=True)
+        return 0
+
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        line = gpu_main(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
+    if line is not None:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

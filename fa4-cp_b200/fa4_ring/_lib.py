@@ -88,6 +88,16 @@ def last_error() -> str:
     return msg.decode() if msg else ""
 
 
+# Number of kernel launches made through this binding (successful calls of the
+# launching entry points), for the benchmark's launch count.
+launch_count = 0
+
+
+def count_launches(n: int = 1) -> None:
+    global launch_count
+    launch_count += n
+
+
 def check(rc: int, what: str) -> None:
     if rc == OK:
         return

@@ -68,11 +68,20 @@ def _check_qkv(q, k, v):
         raise NotImplementedError(f"head_dim {D} with dtype {q.dtype} is not supported")
 
 
+# Optional per-launch timing: when set to a list, every attn_into launch appends
+# (start_event, end_event, pattern) recorded on the launching stream.
+launch_timer = None
+
+
 def attn_into(q, k, v, out, lse, cu_q, cu_k, *, nseq: int, max_seqlen_q: int, pattern: int,
               causal: bool, softmax_scale: float, q_descale=None, k_descale=None,
               v_descale=None, accumulate: bool = False) -> None:
     """Launch ``fa4cp_attn_fwd`` on the current stream.  All tensors contiguous CUDA."""
     lib = _lib.load()
+    timer = launch_timer
+    if timer is not None:
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record()
     rc = lib.fa4cp_attn_fwd(
         q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), lse.data_ptr(),
         cu_q.data_ptr(), _lib.ptr(cu_k), nseq, max_seqlen_q, q.shape[0], k.shape[0],
@@ -81,6 +90,10 @@ def attn_into(q, k, v, out, lse, cu_q, cu_k, *, nseq: int, max_seqlen_q: int, pa
         _lib.ptr(q_descale), _lib.ptr(k_descale), _lib.ptr(v_descale), 1 if accumulate else 0,
         _lib.stream_of(q))
     _lib.check(rc, "attn_fwd")
+    _lib.count_launches()
+    if timer is not None:
+        ev1.record()
+        timer.append((ev0, ev1, pattern))
 
 
 def b200_attn(

@@ -41,6 +41,7 @@ def merge_state_in_place(v: torch.Tensor, s: torch.Tensor, v_other: torch.Tensor
     _lib.check(_lib.load().fa4cp_merge_state_inplace(
         v.data_ptr(), s.data_ptr(), v_other.data_ptr(), s_other.data_ptr(), T, H, D,
         _lib.dtype_code(v.dtype), _lib.stream_of(v)), "merge_state_in_place")
+    _lib.count_launches(2)
 
 
 def merge_states(outs: List[torch.Tensor], lses: List[torch.Tensor], *, out: torch.Tensor = None,
@@ -61,6 +62,7 @@ def merge_states(outs: List[torch.Tensor], lses: List[torch.Tensor], *, out: tor
     _lib.check(_lib.load().fa4cp_merge_states(
         _lib.ptr_array(outs), _lib.ptr_array(lses), len(outs), out.data_ptr(), lse_out.data_ptr(),
         T, H, D, _lib.dtype_code(outs[0].dtype), _lib.stream_of(out)), "merge_states")
+    _lib.count_launches()
     return out, lse_out
 
 

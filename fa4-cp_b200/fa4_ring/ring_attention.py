@@ -172,6 +172,7 @@ def ring_forward(local_q, kv_at, step_done, cfg: RingConfig, *, cu: torch.Tensor
             if pattern == PATTERN_BACK_Q:  # rows this step does not cover: identity
                 _lib.check(lib.fa4cp_fill_f32(l_t.data_ptr(), l_t.numel(), float("-inf"), stream),
                            "fill_f32")
+                _lib.count_launches()
             partials.append((o_t, l_t))
             acc = False
         attn_into(q, k, v, o_t, l_t, cu, cu, nseq=nseq, max_seqlen_q=q_rows, pattern=pattern,

@@ -42,6 +42,7 @@ def zigzag_shard(x: torch.Tensor, cp_rank: int, cp_size: int) -> torch.Tensor:
     _lib.check(_lib.load().fa4cp_zigzag_shard(
         x.data_ptr(), out.data_ptr(), None, 1, n, cp_rank, cp_size, _row_bytes(x),
         _lib.stream_of(x)), "zigzag_shard")
+    _lib.count_launches()
     return out
 
 
@@ -61,6 +62,7 @@ def zigzag_unshard(local_shards: List[torch.Tensor], cp_size: int) -> torch.Tens
     _lib.check(_lib.load().fa4cp_zigzag_unshard(
         _lib.ptr_array(shards), out.data_ptr(), None, 1, n, cp_size, _row_bytes(t0),
         _lib.stream_of(t0)), "zigzag_unshard")
+    _lib.count_launches()
     return out
 
 
