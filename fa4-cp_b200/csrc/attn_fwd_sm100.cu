@@ -466,6 +466,462 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
+// v2: two query tiles per CTA, two softmax warpgroups ping-ponging on the tensor core
+// ---------------------------------------------------------------------------
+// CTA = rows [q0, q0 + 256) of one (head, sequence): tile 0 = first 128 rows, tile 1 =
+// next 128.  Both tiles share every K/V tile staged in shared memory.  384 threads:
+//   warps 0-3  softmax + epilogue of tile 0      warps 4-7  softmax + epilogue of tile 1
+//   warp  8    TMA producer                      warp  9    TMEM allocator + MMA issuer
+//   warps 10-11 idle (complete the producer warpgroup for the register re-split)
+// Registers: launched at 168/thread (384 x 168 = 64512); the producer warpgroup drops to
+// 72 and each softmax warpgroup rises to 216: 128 x (216 + 216 + 72) = 64512.
+// TMEM: S0 | S1 (BN fp32 columns each) | O0 | O1 (D columns each).  One S buffer per
+// tile: S_t(j+1) is issued after PV_t(j), so the completion of S_t(j+1) also proves
+// PV_t(j) finished -- a softmax warpgroup may rescale O_t right after its s_full wait.
+// MMA order per KV tile j:  PV0(j) S0(j+1) PV1(j) S1(j+1): while warpgroup 0 turns
+// S0(j+1) into P0(j+1), the tensor core runs PV1(j) and S1(j+1), and vice versa.
+template <int D_, int BN_, int STAGES_, bool FP8_>
+struct Traits2 {
+  static constexpr int D = D_, BN = BN_, STAGES = STAGES_;
+  static constexpr bool FP8 = FP8_;
+  static constexpr int ELEM = FP8 ? 1 : 2;
+  static constexpr int CHUNK = 128 / ELEM;
+  static constexpr int NCH = D / CHUNK;
+  static constexpr int MMA_K = FP8 ? 32 : 16;
+  static constexpr int Q_TILE_BYTES = BM * D * ELEM;
+  static constexpr int KV_BYTES = BN * D * ELEM;
+  static constexpr int Q_CHUNK_BYTES = BM * 128;
+  static constexpr int KV_CHUNK_BYTES = BN * 128;
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_K = 2 * Q_TILE_BYTES;
+  static constexpr int OFF_V = OFF_K + STAGES * KV_BYTES;
+  static constexpr int OFF_BAR = OFF_V + STAGES * KV_BYTES;
+  // q_full, k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], p_full[2], o_done[2], teardown
+  static constexpr int NUM_BARS = 1 + 4 * STAGES + 2 + 2 + 2 + 1;
+  static constexpr int SMEM_BYTES = OFF_BAR + NUM_BARS * 8 + 16 + 1024;
+  static constexpr int TM_COLS = 512;
+  static constexpr int THREADS = 384;
+  static constexpr int REGS_SOFTMAX = 216;
+  static constexpr int REGS_PRODUCER = 72;
+  static_assert(128 * (2 * REGS_SOFTMAX + REGS_PRODUCER) <= THREADS * 168,
+                "register re-split exceeds the launch allocation");
+  __host__ __device__ static constexpr int tm_s(int t) { return t * BN; }
+  __host__ __device__ static constexpr int tm_o(int t) { return 2 * BN + t * D; }
+  static_assert(D % CHUNK == 0, "head_dim must be a multiple of one 128-byte swizzle row");
+  static_assert(2 * BN + 2 * D <= TM_COLS, "TMEM budget");
+  static_assert(BN == 128, "softmax register layout assumes 128 keys per tile");
+  static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+};
+
+template <class TR>
+__global__ void __launch_bounds__(TR::THREADS, 1)
+    attn_fwd_2q_kernel(const __grid_constant__ CUtensorMap tmQ,
+                       const __grid_constant__ CUtensorMap tmK,
+                       const __grid_constant__ CUtensorMap tmV, const Params p) {
+  constexpr int D = TR::D, BN = TR::BN, ST = TR::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int head = blockIdx.x;
+  const int qtile = p.n_qtiles - 1 - int(blockIdx.y);  // heaviest causal tiles first
+  const int seq = blockIdx.z;
+
+  const Geometry g = seq_geometry(p, seq);
+  const int q0 = qtile * 2 * BM;
+  if (q0 >= g.q_len) return;  // uniform for the whole CTA, before any setup
+  const int diag = g.k_len - g.q_len;
+  int rows_t[2], n_t[2];
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    const int first = q0 + t * BM;
+    rows_t[t] = max(0, min(BM, g.q_len - first));
+    int kv_end = g.k_len;
+    if (p.causal) kv_end = min(g.k_len, first + rows_t[t] + diag);
+    n_t[t] = (rows_t[t] > 0 && kv_end > 0) ? (kv_end + BN - 1) / BN : 0;
+  }
+  const int nmax = max(n_t[0], n_t[1]);
+  const int kvh = head / p.group;
+
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TR::OFF_BAR);
+  const uint32_t bar0 = smem_u32(bars);
+  auto BAR = [&](int i) -> uint32_t { return bar0 + 8u * uint32_t(i); };
+  const uint32_t q_full = BAR(0);
+  auto k_full = [&](int s) { return BAR(1 + s); };
+  auto k_empty = [&](int s) { return BAR(1 + ST + s); };
+  auto v_full = [&](int s) { return BAR(1 + 2 * ST + s); };
+  auto v_empty = [&](int s) { return BAR(1 + 3 * ST + s); };
+  auto s_full = [&](int t) { return BAR(1 + 4 * ST + t); };
+  auto p_full = [&](int t) { return BAR(3 + 4 * ST + t); };
+  auto o_done = [&](int t) { return BAR(5 + 4 * ST + t); };
+  const uint32_t td_bar = BAR(7 + 4 * ST);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + TR::NUM_BARS);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* status = &g_attn_status;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(k_full(s), 1);
+      mbar_init(k_empty(s), 1);
+      mbar_init(v_full(s), 1);
+      mbar_init(v_empty(s), 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(s_full(t), 1);
+      mbar_init(p_full(t), 128);
+      mbar_init(o_done(t), 1);
+    }
+    mbar_init(td_bar, 1);
+    *abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 8 && lane == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+  }
+  if (warp == 9) {
+    tmem_alloc(smem_u32(tmem_slot), TR::TM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp >= 8) {
+   setmaxnreg_dec<TR::REGS_PRODUCER>();
+   if (warp == 8) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      const uint64_t pol_kv = policy_evict_last();
+      int last_k[ST], last_v[ST];
+      for (int s = 0; s < ST; ++s) last_k[s] = last_v[s] = -1;
+      mbar_arrive_expect_tx(q_full, 2 * TR::Q_TILE_BYTES);
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int c = 0; c < TR::NCH; ++c)
+          tma_load_3d(smem_u32(smem + TR::OFF_Q + t * TR::Q_TILE_BYTES + c * TR::Q_CHUNK_BYTES),
+                      &tmQ, c * TR::CHUNK, head, g.q_start + q0 + t * BM, q_full);
+      for (int j = 0; j < nmax; ++j) {
+        const int s = j % ST, ph = (j / ST) & 1;
+        const int row = g.k_start + j * BN;
+        if (j >= ST && !mbar_wait(k_empty(s), ph ^ 1, abort, kErrKEmpty, status)) break;
+        mbar_arrive_expect_tx(k_full(s), TR::KV_BYTES);
+#pragma unroll
+        for (int c = 0; c < TR::NCH; ++c)
+          tma_load_3d_hint(smem_u32(smem + TR::OFF_K + s * TR::KV_BYTES + c * TR::KV_CHUNK_BYTES),
+                           &tmK, c * TR::CHUNK, kvh, row, k_full(s), pol_kv);
+        last_k[s] = j;
+        if (j >= ST && !mbar_wait(v_empty(s), ph ^ 1, abort, kErrVEmpty, status)) break;
+        mbar_arrive_expect_tx(v_full(s), TR::KV_BYTES);
+#pragma unroll
+        for (int c = 0; c < TR::NCH; ++c)
+          tma_load_3d_hint(smem_u32(smem + TR::OFF_V + s * TR::KV_BYTES + c * TR::KV_CHUNK_BYTES),
+                           &tmV, c * TR::CHUNK, kvh, row, v_full(s), pol_kv);
+        last_v[s] = j;
+      }
+      if (*abort) {
+        int zero = 0;
+        volatile int* no_abort = &zero;
+        mbar_wait(q_full, 0, no_abort, kErrDrain, status);
+        for (int s = 0; s < ST; ++s) {
+          if (last_k[s] >= 0) mbar_wait(k_full(s), (last_k[s] / ST) & 1, no_abort, kErrDrain, status);
+          if (last_v[s] >= 0) mbar_wait(v_full(s), (last_v[s] / ST) & 1, no_abort, kErrDrain, status);
+        }
+      }
+    }
+   } else if (warp == 9) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const int fmt = TR::FP8 ? 0 : p.in_fmt;
+      const uint32_t idesc_qk = make_idesc(BM, BN, fmt, fmt, 0, 0);
+      const uint32_t idesc_pv = make_idesc(BM, D, fmt, fmt, 0, 1);
+      auto issue_s = [&](int t, int j) {
+        const uint32_t sQ = smem_u32(smem + TR::OFF_Q + t * TR::Q_TILE_BYTES);
+        const uint32_t sK = smem_u32(smem + TR::OFF_K + (j % ST) * TR::KV_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < D / TR::MMA_K; ++kk) {
+          const int off = kk * 32;  // bytes along D of this K-step
+          const uint32_t ca = (off / 128) * TR::Q_CHUNK_BYTES + (off % 128);
+          const uint32_t cb = (off / 128) * TR::KV_CHUNK_BYTES + (off % 128);
+          const uint64_t adesc = make_desc_sw128(sQ + ca, 16, 1024);
+          const uint64_t bdesc = make_desc_sw128(sK + cb, 16, 1024);
+          if constexpr (TR::FP8)
+            mma_f8_ss(tmem + uint32_t(TR::tm_s(t)), adesc, bdesc, idesc_qk, kk > 0 ? 1u : 0u);
+          else
+            mma_f16_ss(tmem + uint32_t(TR::tm_s(t)), adesc, bdesc, idesc_qk, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(s_full(t));
+      };
+      auto issue_pv = [&](int t, int j) {
+        const uint32_t sV = smem_u32(smem + TR::OFF_V + (j % ST) * TR::KV_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < BN / TR::MMA_K; ++kk) {
+          const uint64_t bdesc = make_desc_sw128(sV + kk * TR::MMA_K * 128, TR::KV_CHUNK_BYTES, 1024);
+          const uint32_t a_tmem = tmem + uint32_t(TR::tm_s(t) + kk * 8);
+          const uint32_t acc = (j > 0 || kk > 0) ? 1u : 0u;
+          if constexpr (TR::FP8)
+            mma_f8_ts(tmem + uint32_t(TR::tm_o(t)), a_tmem, bdesc, idesc_pv, acc);
+          else
+            mma_f16_ts(tmem + uint32_t(TR::tm_o(t)), a_tmem, bdesc, idesc_pv, acc);
+        }
+        tc_commit(o_done(t));
+      };
+      bool ok = mbar_wait(q_full, 0, abort, kErrQ, status);
+      if (ok && nmax > 0) {
+        ok = mbar_wait(k_full(0), 0, abort, kErrKFull, status);
+        tc_fence_after();
+        if (ok) {
+          if (n_t[0] > 0) issue_s(0, 0);
+          if (n_t[1] > 0) issue_s(1, 0);
+          tc_commit(k_empty(0));
+        }
+      }
+      for (int j = 0; ok && j < nmax; ++j) {
+        const int s = j % ST;
+        bool v_ready = false, k_next_ready = false;
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          if (j >= n_t[t]) continue;
+          if (!mbar_wait(p_full(t), j & 1, abort, kErrPFull, status)) { ok = false; break; }
+          if (!v_ready) {
+            if (!mbar_wait(v_full(s), (j / ST) & 1, abort, kErrVFull, status)) { ok = false; break; }
+            v_ready = true;
+          }
+          tc_fence_after();
+          issue_pv(t, j);
+          if (j + 1 < n_t[t]) {
+            if (!k_next_ready) {
+              const int s1 = (j + 1) % ST;
+              if (!mbar_wait(k_full(s1), ((j + 1) / ST) & 1, abort, kErrKFull, status)) {
+                ok = false;
+                break;
+              }
+              k_next_ready = true;
+              tc_fence_after();
+            }
+            issue_s(t, j + 1);
+          }
+        }
+        if (!ok) break;
+        tc_commit(v_empty(s));
+        if (k_next_ready) tc_commit(k_empty((j + 1) % ST));
+      }
+      // every MMA issued above has completed before TMEM is released
+      tc_commit(td_bar);
+      int zero = 0;
+      volatile int* no_abort = &zero;
+      mbar_wait(td_bar, 0, no_abort, kErrDrain, status);
+    }
+   }
+  } else {
+    setmaxnreg_inc<TR::REGS_SOFTMAX>();
+    // ------------------------------------------------------------ softmax + epilogue
+    const int t = warp >> 2;  // query tile of this warpgroup
+    const int wq = warp & 3;
+    const int r = wq * 32 + lane;
+    const uint32_t t_lane = tmem + (uint32_t(wq * 32) << 16);
+    const int first = q0 + t * BM;
+    const int key_lim = first + r + diag;
+    const int n = n_t[t];
+    float scale = p.scale_log2;
+    float vscale = 1.0f;
+    if (p.q_descale) scale *= p.q_descale[kvh];
+    if (p.k_descale) scale *= p.k_descale[kvh];
+    if (p.v_descale) vscale = p.v_descale[kvh];
+    const uint64_t scale2 = f2pack(scale, scale);
+    float m = kNegInf, l = 0.f;
+    bool aborted = false;
+
+    for (int j = 0; j < n; ++j) {
+      bool ok = mbar_wait(s_full(t), j & 1, abort, kErrSFull, status);
+      if (!__all_sync(0xffffffffu, ok)) { aborted = true; break; }
+      tc_fence_after();
+      uint32_t sr[BN / 32][32];
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) tmem_ld32(t_lane + uint32_t(TR::tm_s(t) + c * 32), sr[c]);
+      tmem_wait_ld();
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) reg_fence32(sr[c]);
+
+      const int kbase = j * BN;
+      const bool need_mask = (kbase + BN > g.k_len) || (p.causal && kbase + BN - 1 > first + diag);
+      if (need_mask) {
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c)
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int key = kbase + c * 32 + e;
+            if (key >= g.k_len || (p.causal && key > key_lim)) sr[c][e] = __float_as_uint(kNegInf);
+          }
+      }
+      float mx4[4] = {kNegInf, kNegInf, kNegInf, kNegInf};
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c)
+#pragma unroll
+        for (int e = 0; e < 32; e += 2)
+          mx4[c] = fmax3(mx4[c], __uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1]));
+      const float mx = fmax3(fmaxf(mx4[0], mx4[1]), mx4[2], mx4[3]);
+      const float m_new = fmaxf(m, mx);
+      if (j == 0) {
+        m = m_new;
+      } else {
+        const bool need = (m_new - m) * scale > kRescaleThreshold;
+        if (__any_sync(0xffffffffu, need)) {
+          // PV_t(j-1) is complete: S_t(j) was issued after it and has completed.
+          const float f = need ? ex2_approx((m - m_new) * scale) : 1.0f;
+          if (need) { l *= f; m = m_new; }
+          const uint64_t f2 = f2pack(f, f);
+#pragma unroll 1
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t o[32];
+            tmem_ld32(t_lane + uint32_t(TR::tm_o(t) + c * 32), o);
+            tmem_wait_ld();
+            reg_fence32(o);
+#pragma unroll
+            for (int e = 0; e < 32; e += 2) {
+              const uint64_t v = fmul2(f2pack(__uint_as_float(o[e]), __uint_as_float(o[e + 1])), f2);
+              o[e] = __float_as_uint(f2lo(v));
+              o[e + 1] = __float_as_uint(f2hi(v));
+            }
+            tmem_st32(t_lane + uint32_t(TR::tm_o(t) + c * 32), o);
+          }
+          tmem_wait_st();
+        }
+      }
+      const float neg_m = (m == kNegInf) ? 0.f : -m * scale;
+      const uint64_t negm2 = f2pack(neg_m, neg_m);
+      uint64_t rs2[2] = {0ull, 0ull};
+      if constexpr (TR::FP8) {
+        uint32_t pw[32];
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c) {
+#pragma unroll
+          for (int e = 0; e < 32; e += 4) {
+            const uint64_t a = ffma2(f2pack(__uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1])), scale2, negm2);
+            const uint64_t b = ffma2(f2pack(__uint_as_float(sr[c][e + 2]), __uint_as_float(sr[c][e + 3])), scale2, negm2);
+            const float x0 = ex2_approx(f2lo(a)), x1 = ex2_approx(f2hi(a));
+            const float x2 = ex2_approx(f2lo(b)), x3 = ex2_approx(f2hi(b));
+            rs2[0] = fadd2(rs2[0], f2pack(x0, x1));
+            rs2[1] = fadd2(rs2[1], f2pack(x2, x3));
+            pw[(c * 32 + e) / 4] = pack_e4m3x4(x0, x1, x2, x3);
+          }
+        }
+        tmem_st32(t_lane + uint32_t(TR::tm_s(t)), pw);
+      } else {
+#pragma unroll
+        for (int half = 0; half < BN / 64; ++half) {
+          uint32_t pw[32];
+#pragma unroll
+          for (int e = 0; e < 64; e += 2) {
+            const int c = half * 2 + (e >> 5), ee = e & 31;
+            const uint64_t a = ffma2(f2pack(__uint_as_float(sr[c][ee]), __uint_as_float(sr[c][ee + 1])), scale2, negm2);
+            const float x0 = ex2_approx(f2lo(a)), x1 = ex2_approx(f2hi(a));
+            rs2[(e >> 1) & 1] = fadd2(rs2[(e >> 1) & 1], f2pack(x0, x1));
+            pw[e >> 1] = p.in_fmt ? pack_bf16x2(x0, x1) : pack_f16x2(x0, x1);
+          }
+          tmem_st32(t_lane + uint32_t(TR::tm_s(t) + half * 32), pw);
+        }
+      }
+      const uint64_t rs = fadd2(rs2[0], rs2[1]);
+      l += f2lo(rs) + f2hi(rs);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(p_full(t));
+    }
+
+    // ------------------------------------------------------------ epilogue
+    if (!aborted && n > 0) {
+      bool ok = mbar_wait(o_done(t), (n - 1) & 1, abort, kErrODone, status);
+      if (!__all_sync(0xffffffffu, ok)) aborted = true;
+      tc_fence_after();
+    }
+    if (!aborted && rows_t[t] > 0) {
+      const bool valid = r < rows_t[t];
+      const int64_t grow = int64_t(g.q_start) + first + r;
+      const float lse_new = (l > 0.f) ? (m * scale + lg2_approx(l)) * kLn2 : kNegInf;
+      float* lse_ptr = p.lse + grow * p.Hq + head;
+      float ca = 0.f, cb = (l > 0.f) ? vscale / l : 0.f, lse_out = lse_new;
+      bool write = valid;
+      bool read_acc = false;
+      if (valid && p.accumulate) {
+        const float acc_lse = *lse_ptr;
+        if (lse_new == kNegInf) {
+          write = false;
+        } else if (acc_lse != kNegInf) {
+          const float mm = fmaxf(acc_lse, lse_new);
+          const float wa = ex2_approx((acc_lse - mm) * kLog2e);
+          const float wb = ex2_approx((lse_new - mm) * kLog2e);
+          const float inv = 1.0f / (wa + wb);
+          ca = wa * inv;
+          cb *= wb * inv;
+          lse_out = mm + lg2_approx(wa + wb) * kLn2;
+          read_acc = true;
+        }
+      }
+      uint8_t* orow = static_cast<uint8_t*>(p.out) + (grow * p.Hq + head) * int64_t(D) * 2;
+      const bool has_o = n > 0;  // warpgroup-uniform
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        if (has_o) {
+          tmem_ld32(t_lane + uint32_t(TR::tm_o(t) + c * 32), o);
+          tmem_wait_ld();
+          reg_fence32(o);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = 0u;
+        }
+        if (write) {
+          uint4* dst = reinterpret_cast<uint4*>(orow + c * 64);
+          float f[32];
+#pragma unroll
+          for (int e = 0; e < 32; ++e) f[e] = has_o ? __uint_as_float(o[e]) * cb : 0.f;
+          if (read_acc) {
+#pragma unroll
+            for (int v4 = 0; v4 < 4; ++v4) {
+              const uint4 a = dst[v4];
+              const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                float lo, hi;
+                if (p.out_bf16) {
+                  lo = __uint_as_float(w[i] << 16);
+                  hi = __uint_as_float(w[i] & 0xFFFF0000u);
+                } else {
+                  const float2 tt = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+                  lo = tt.x; hi = tt.y;
+                }
+                f[v4 * 8 + 2 * i] = fmaf(lo, ca, f[v4 * 8 + 2 * i]);
+                f[v4 * 8 + 2 * i + 1] = fmaf(hi, ca, f[v4 * 8 + 2 * i + 1]);
+              }
+            }
+          }
+#pragma unroll
+          for (int v4 = 0; v4 < 4; ++v4) {
+            uint32_t w[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              w[i] = p.out_bf16 ? pack_bf16x2(f[v4 * 8 + 2 * i], f[v4 * 8 + 2 * i + 1])
+                                : pack_f16x2(f[v4 * 8 + 2 * i], f[v4 * 8 + 2 * i + 1]);
+            dst[v4] = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+        }
+      }
+      if (write) *lse_ptr = lse_out;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 9) tmem_dealloc(tmem, TR::TM_COLS);
+}
+
+// ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
@@ -535,6 +991,35 @@ int launch(const void* q, const void* k, const void* v, int64_t total_q, int64_t
   return check_launch("attn_fwd");
 }
 
+template <class TR>
+int launch2(const void* q, const void* k, const void* v, int64_t total_q, int64_t total_k,
+            int max_seqlen_q, const Params& p0, cudaStream_t stream) {
+  static bool attr_set = false;
+  if (!attr_set) {
+    FA4CP_CHECK_CUDA(cudaFuncSetAttribute(attn_fwd_2q_kernel<TR>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          TR::SMEM_BYTES));
+    attr_set = true;
+  }
+  CUtensorMap mq, mk, mv;
+  int rc = make_map(&mq, q, total_q, p0.Hq, TR::D, TR::ELEM, BM);
+  if (rc) return rc;
+  if (total_k > 0) {
+    if ((rc = make_map(&mk, k, total_k, p0.Hkv, TR::D, TR::ELEM, TR::BN))) return rc;
+    if ((rc = make_map(&mv, v, total_k, p0.Hkv, TR::D, TR::ELEM, TR::BN))) return rc;
+  } else {
+    mk = mq;
+    mv = mq;
+  }
+  Params p = p0;
+  p.n_qtiles = (max_seqlen_q + 2 * BM - 1) / (2 * BM);
+  if (p.n_qtiles <= 0) return FA4CP_OK;
+  FA4CP_CHECK_ARG(p.n_qtiles <= 65535 && p.nseq <= 65535, "grid too large");
+  dim3 grid(unsigned(p.Hq), unsigned(p.n_qtiles), unsigned(p.nseq));
+  attn_fwd_2q_kernel<TR><<<grid, TR::THREADS, TR::SMEM_BYTES, stream>>>(mq, mk, mv, p);
+  return check_launch("attn_fwd_2q");
+}
+
 bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
 
 }  // namespace
@@ -592,10 +1077,10 @@ extern "C" int fa4cp_attn_fwd(const void* q, const void* k, const void* v, void*
 
   if (fp8) {
     FA4CP_CHECK_ARG(out_dtype == FA4CP_DTYPE_BF16, "e4m3 inputs produce a bf16 output");
-    if (head_dim == 128) return launch<Traits<128, 128, 3, true>>(q, k, v, total_q, total_k, max_seqlen_q, p, st);
+    if (head_dim == 128) return launch2<Traits2<128, 128, 3, true>>(q, k, v, total_q, total_k, max_seqlen_q, p, st);
   } else {
-    if (head_dim == 128) return launch<Traits<128, 128, 2, false>>(q, k, v, total_q, total_k, max_seqlen_q, p, st);
-    if (head_dim == 64) return launch<Traits<64, 128, 3, false>>(q, k, v, total_q, total_k, max_seqlen_q, p, st);
+    if (head_dim == 128) return launch2<Traits2<128, 128, 2, false>>(q, k, v, total_q, total_k, max_seqlen_q, p, st);
+    if (head_dim == 64) return launch2<Traits2<64, 128, 3, false>>(q, k, v, total_q, total_k, max_seqlen_q, p, st);
   }
   set_last_error("head_dim %d with dtype %d is not supported", head_dim, in_dtype);
   return FA4CP_ERR_UNSUPPORTED;
