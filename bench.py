@@ -28,7 +28,6 @@ import json
 import math
 import os
 import statistics
-import subprocess
 import sys
 import time
 
@@ -59,56 +58,67 @@ def load_peaks():
 
 # --------------------------------------------------------------------------- clocks
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """SM clock and clock-event reasons of this GPU, sampled by NVML every 10 ms in a
+    background thread while the timed region runs."""
 
-    def __init__(self, gpu_index):
-        self.gpu = gpu_index
-        self.proc = None
-        self.path = os.path.join("/tmp", f"fa4cp_clocks_{os.getpid()}.csv")
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
+
+    def __init__(self, device_index, interval=0.01):
+        self.dev = device_index
+        self.interval = interval
+        self.samples = []
+        self.max_mhz = None
+        self.error = None
+
+    def _handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        try:
+            prop = torch.cuda.get_device_properties(self.dev)
+            bus = f"{prop.pci_domain_id:08x}:{prop.pci_bus_id:02x}:{prop.pci_device_id:02x}.0"
+            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.dev)
+
+    def _run(self):
+        try:
+            nv, h = self._handle()
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            while not self._stop.is_set():
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                try:
+                    rs = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                except AttributeError:
+                    rs = nv.nvmlDeviceGetCurrentClocksThrottleReasons(h)
+                self.samples.append((sm, rs))
+                time.sleep(self.interval)
+        except Exception as e:  # NVML missing: report it instead of guessing
+            self.error = repr(e)
 
     def __enter__(self):
-        try:
-            self.f = open(self.path, "w")
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
-                stderr=subprocess.DEVNULL)
-        except OSError:
-            self.proc = None
+        import threading
+        self._stop = threading.Event()
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
         return self
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-            self.f.close()
+        self._stop.set()
+        self._t.join(5)
 
     def summary(self):
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        with open(self.path) as f:
-            for line in f:
-                parts = [p.strip() for p in line.split(",")]
-                if len(parts) < 9:
-                    continue
-                try:
-                    sm.append(float(parts[1]))
-                    mx = float(parts[2])
-                except ValueError:
-                    continue
-                for name, val in zip(names, parts[5:9]):
-                    if val.lower() == "active":
-                        reasons.add(name)
-        os.unlink(self.path)
-        busy = [s for s in sm if mx and s > 0.3 * mx] or sm
-        return {"sm_mhz": statistics.median(busy) if busy else None, "sm_max_mhz": mx,
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz,
+                    "reasons": [f"no samples: {self.error}"]}
+        sm = [a for a, _ in self.samples]
+        busy = [a for a in sm if self.max_mhz and a > 0.3 * self.max_mhz] or sm
+        reasons = set()
+        for _, rs in self.samples:
+            for bit, name in self.REASONS.items():
+                if rs & bit:
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(busy), "sm_max_mhz": self.max_mhz,
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
@@ -386,7 +396,7 @@ def reference_main(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--merge", choices=["incremental", "batched"], default="incremental")

@@ -480,10 +480,23 @@ __global__ void __launch_bounds__(kThreads, 1)
 // PV_t(j) finished -- a softmax warpgroup may rescale O_t right after its s_full wait.
 // MMA order per KV tile j:  PV0(j) S0(j+1) PV1(j) S1(j+1): while warpgroup 0 turns
 // S0(j+1) into P0(j+1), the tensor core runs PV1(j) and S1(j+1), and vice versa.
+#ifndef FA4CP_EXP2_EMU_PER_8
+#define FA4CP_EXP2_EMU_PER_8 0
+#endif
+#ifndef FA4CP_P_SPLIT
+#define FA4CP_P_SPLIT 1
+#endif
+
 template <int D_, int BN_, int STAGES_, bool FP8_>
 struct Traits2 {
   static constexpr int D = D_, BN = BN_, STAGES = STAGES_;
   static constexpr bool FP8 = FP8_;
+  // of every 8 element pairs of P, this many take exp2 on the FMA pipe (exp2_poly_x2)
+  // and the rest on the MUFU unit, balancing the two pipes against the tensor core
+  static constexpr int EXP2_EMU_PER_8 = FA4CP_EXP2_EMU_PER_8;
+  // P is handed to the MMA warp in this many key slices (one barrier each), so the PV
+  // MMAs of the first slice run while the softmax warpgroup finishes the rest
+  static constexpr int P_SPLIT = FA4CP_P_SPLIT;
   static constexpr int ELEM = FP8 ? 1 : 2;
   static constexpr int CHUNK = 128 / ELEM;
   static constexpr int NCH = D / CHUNK;
@@ -496,8 +509,9 @@ struct Traits2 {
   static constexpr int OFF_K = 2 * Q_TILE_BYTES;
   static constexpr int OFF_V = OFF_K + STAGES * KV_BYTES;
   static constexpr int OFF_BAR = OFF_V + STAGES * KV_BYTES;
-  // q_full, k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], p_full[2], o_done[2], teardown
-  static constexpr int NUM_BARS = 1 + 4 * STAGES + 2 + 2 + 2 + 1;
+  // q_full, k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], o_done[2], teardown,
+  // p_full[2][P_SPLIT]
+  static constexpr int NUM_BARS = 1 + 4 * STAGES + 2 + 2 + 1 + 2 * FA4CP_P_SPLIT;
   static constexpr int SMEM_BYTES = OFF_BAR + NUM_BARS * 8 + 16 + 1024;
   static constexpr int TM_COLS = 512;
   static constexpr int THREADS = 384;
@@ -512,6 +526,13 @@ struct Traits2 {
   static_assert(BN == 128, "softmax register layout assumes 128 keys per tile");
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 };
+
+// exp2 of one element pair: the pair index decides, at compile time, which pipe does it
+template <class TR>
+__device__ __forceinline__ uint64_t exp2_pair(int pair, uint64_t x) {
+  if ((pair & 7) < TR::EXP2_EMU_PER_8) return exp2_poly_x2(x);
+  return f2pack(ex2_approx(f2lo(x)), ex2_approx(f2hi(x)));
+}
 
 template <class TR>
 __global__ void __launch_bounds__(TR::THREADS, 1)
@@ -552,9 +573,9 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
   auto v_full = [&](int s) { return BAR(1 + 2 * ST + s); };
   auto v_empty = [&](int s) { return BAR(1 + 3 * ST + s); };
   auto s_full = [&](int t) { return BAR(1 + 4 * ST + t); };
-  auto p_full = [&](int t) { return BAR(3 + 4 * ST + t); };
-  auto o_done = [&](int t) { return BAR(5 + 4 * ST + t); };
-  const uint32_t td_bar = BAR(7 + 4 * ST);
+  auto o_done = [&](int t) { return BAR(3 + 4 * ST + t); };
+  const uint32_t td_bar = BAR(5 + 4 * ST);
+  auto p_full = [&](int t, int h) { return BAR(6 + 4 * ST + t * TR::P_SPLIT + h); };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + TR::NUM_BARS);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* status = &g_attn_status;
@@ -569,7 +590,7 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(s_full(t), 1);
-      mbar_init(p_full(t), 128);
+      for (int h = 0; h < TR::P_SPLIT; ++h) mbar_init(p_full(t, h), 128);
       mbar_init(o_done(t), 1);
     }
     mbar_init(td_bar, 1);
@@ -656,10 +677,13 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
         }
         tc_commit(s_full(t));
       };
-      auto issue_pv = [&](int t, int j) {
+      // PV of one key slice (the caller has waited for that slice of P)
+      auto issue_pv_slice = [&](int t, int j, int h) {
         const uint32_t sV = smem_u32(smem + TR::OFF_V + (j % ST) * TR::KV_BYTES);
+        constexpr int KS = BN / TR::MMA_K / TR::P_SPLIT;  // K-steps per slice
 #pragma unroll
-        for (int kk = 0; kk < BN / TR::MMA_K; ++kk) {
+        for (int k2 = 0; k2 < KS; ++k2) {
+          const int kk = h * KS + k2;
           const uint64_t bdesc = make_desc_sw128(sV + kk * TR::MMA_K * 128, TR::KV_CHUNK_BYTES, 1024);
           const uint32_t a_tmem = tmem + uint32_t(TR::tm_s(t) + kk * 8);
           const uint32_t acc = (j > 0 || kk > 0) ? 1u : 0u;
@@ -668,7 +692,6 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
           else
             mma_f16_ts(tmem + uint32_t(TR::tm_o(t)), a_tmem, bdesc, idesc_pv, acc);
         }
-        tc_commit(o_done(t));
       };
       bool ok = mbar_wait(q_full, 0, abort, kErrQ, status);
       if (ok && nmax > 0) {
@@ -686,13 +709,18 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
 #pragma unroll
         for (int t = 0; t < 2; ++t) {
           if (j >= n_t[t]) continue;
-          if (!mbar_wait(p_full(t), j & 1, abort, kErrPFull, status)) { ok = false; break; }
           if (!v_ready) {
             if (!mbar_wait(v_full(s), (j / ST) & 1, abort, kErrVFull, status)) { ok = false; break; }
             v_ready = true;
           }
-          tc_fence_after();
-          issue_pv(t, j);
+#pragma unroll
+          for (int h = 0; h < TR::P_SPLIT; ++h) {
+            if (!mbar_wait(p_full(t, h), j & 1, abort, kErrPFull, status)) { ok = false; break; }
+            tc_fence_after();
+            issue_pv_slice(t, j, h);
+          }
+          if (!ok) break;
+          tc_commit(o_done(t));
           if (j + 1 < n_t[t]) {
             if (!k_next_ready) {
               const int s1 = (j + 1) % ST;
@@ -803,15 +831,22 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
           for (int e = 0; e < 32; e += 4) {
             const uint64_t a = ffma2(f2pack(__uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1])), scale2, negm2);
             const uint64_t b = ffma2(f2pack(__uint_as_float(sr[c][e + 2]), __uint_as_float(sr[c][e + 3])), scale2, negm2);
-            const float x0 = ex2_approx(f2lo(a)), x1 = ex2_approx(f2hi(a));
-            const float x2 = ex2_approx(f2lo(b)), x3 = ex2_approx(f2hi(b));
-            rs2[0] = fadd2(rs2[0], f2pack(x0, x1));
-            rs2[1] = fadd2(rs2[1], f2pack(x2, x3));
-            pw[(c * 32 + e) / 4] = pack_e4m3x4(x0, x1, x2, x3);
+            const uint64_t ea = exp2_pair<TR>((c * 32 + e) / 2, a);
+            const uint64_t eb = exp2_pair<TR>((c * 32 + e) / 2 + 1, b);
+            rs2[0] = fadd2(rs2[0], ea);
+            rs2[1] = fadd2(rs2[1], eb);
+            pw[(c * 32 + e) / 4] = pack_e4m3x4(f2lo(ea), f2hi(ea), f2lo(eb), f2hi(eb));
           }
         }
         tmem_st32(t_lane + uint32_t(TR::tm_s(t)), pw);
+        tmem_wait_st();
+        tc_fence_before();
+#pragma unroll
+        for (int h = 0; h < TR::P_SPLIT; ++h) mbar_arrive(p_full(t, h));
       } else {
+        // P in 64-key halves: exps of a half are kept (as fp32 bits, in place of S) for
+        // the row sum, which is added up after P has been handed to the MMA warp
+        static_assert(TR::FP8 || BN / 64 == 2, "bf16 path assumes two 64-key halves");
 #pragma unroll
         for (int half = 0; half < BN / 64; ++half) {
           uint32_t pw[32];
@@ -819,18 +854,34 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
           for (int e = 0; e < 64; e += 2) {
             const int c = half * 2 + (e >> 5), ee = e & 31;
             const uint64_t a = ffma2(f2pack(__uint_as_float(sr[c][ee]), __uint_as_float(sr[c][ee + 1])), scale2, negm2);
-            const float x0 = ex2_approx(f2lo(a)), x1 = ex2_approx(f2hi(a));
-            rs2[(e >> 1) & 1] = fadd2(rs2[(e >> 1) & 1], f2pack(x0, x1));
+            const uint64_t ex = exp2_pair<TR>(half * 32 + (e >> 1), a);
+            const float x0 = f2lo(ex), x1 = f2hi(ex);
+            sr[c][ee] = __float_as_uint(x0);
+            sr[c][ee + 1] = __float_as_uint(x1);
             pw[e >> 1] = p.in_fmt ? pack_bf16x2(x0, x1) : pack_f16x2(x0, x1);
           }
           tmem_st32(t_lane + uint32_t(TR::tm_s(t) + half * 32), pw);
+          if (TR::P_SPLIT == 2 || half == BN / 64 - 1) {
+            tmem_wait_st();
+            tc_fence_before();
+            if (TR::P_SPLIT == 2) {
+              mbar_arrive(p_full(t, half));
+            } else {
+#pragma unroll
+              for (int h = 0; h < TR::P_SPLIT; ++h) mbar_arrive(p_full(t, h));
+            }
+          }
         }
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c)
+#pragma unroll
+          for (int e = 0; e < 32; e += 4) {
+            rs2[0] = fadd2(rs2[0], f2pack(__uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1])));
+            rs2[1] = fadd2(rs2[1], f2pack(__uint_as_float(sr[c][e + 2]), __uint_as_float(sr[c][e + 3])));
+          }
       }
       const uint64_t rs = fadd2(rs2[0], rs2[1]);
       l += f2lo(rs) + f2hi(rs);
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(p_full(t));
     }
 
     // ------------------------------------------------------------ epilogue
@@ -842,9 +893,12 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
     if (!aborted && rows_t[t] > 0) {
       const bool valid = r < rows_t[t];
       const int64_t grow = int64_t(g.q_start) + first + r;
-      const float lse_new = (l > 0.f) ? (m * scale + lg2_approx(l)) * kLn2 : kNegInf;
+      // a row that saw no key has m = -inf (the emulated exp2 maps -inf to ~1e-38, not 0,
+      // so l alone cannot tell)
+      const bool any_key = (m != kNegInf) && (l > 0.f);
+      const float lse_new = any_key ? (m * scale + lg2_approx(l)) * kLn2 : kNegInf;
       float* lse_ptr = p.lse + grow * p.Hq + head;
-      float ca = 0.f, cb = (l > 0.f) ? vscale / l : 0.f, lse_out = lse_new;
+      float ca = 0.f, cb = any_key ? vscale / l : 0.f, lse_out = lse_new;
       bool write = valid;
       bool read_acc = false;
       if (valid && p.accumulate) {

@@ -353,6 +353,29 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return d;
 }
 
+// 2^x for two lanes on the FMA/ALU pipes instead of the MUFU unit (Cody-Waite range
+// reduction x = n + f, n = round(x), |f| <= 1/2, then a cubic in f).  The cubic is this
+// project's own minimax fit of 2^f on [-1/2, 1/2] by the Remez exchange algorithm
+// (max relative error 7.5e-5, below the rounding of the bf16/f16/e4m3 P it feeds).
+// 2^n is applied by adding n to the exponent field.  x is clamped to >= -126, so
+// masked (-inf) scores give a denormal ~0 instead of a NaN.
+__device__ __forceinline__ uint64_t exp2_poly_x2(uint64_t x) {
+  const float x0 = fmaxf(f2lo(x), -126.0f), x1 = fmaxf(f2hi(x), -126.0f);
+  const uint64_t xc = f2pack(x0, x1);
+  const uint64_t round_c = f2pack(12582912.0f, 12582912.0f);    // 1.5 * 2^23
+  const uint64_t neg_round_c = f2pack(-12582912.0f, -12582912.0f);
+  const uint64_t minus1 = f2pack(-1.0f, -1.0f);
+  const uint64_t t = fadd2(xc, round_c);        // low mantissa bits of t hold round(x)
+  const uint64_t n = fadd2(t, neg_round_c);     // round(x) as a float
+  const uint64_t f = ffma2(n, minus1, xc);      // x - round(x), in [-1/2, 1/2]
+  uint64_t p = ffma2(f, f2pack(0.0551716685f, 0.0551716685f), f2pack(0.242611125f, 0.242611125f));
+  p = ffma2(p, f, f2pack(0.693260968f, 0.693260968f));
+  p = ffma2(p, f, f2pack(0.999928057f, 0.999928057f));
+  const uint32_t r0 = uint32_t(p) + (uint32_t(t) << 23);
+  const uint32_t r1 = uint32_t(p >> 32) + (uint32_t(t >> 32) << 23);
+  return uint64_t(r0) | (uint64_t(r1) << 32);
+}
+
 // ---------------------------------------------------------------------------
 // packing helpers
 // ---------------------------------------------------------------------------

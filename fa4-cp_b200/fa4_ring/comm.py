@@ -11,6 +11,7 @@ On CUDA the hops run as NCCL send/recv (``torch.distributed.batch_isend_irecv``)
 issued from a dedicated high-priority comm stream into two persistent receive
 buffers (ping-pong).  Ordering is by CUDA events only, no host blocking:
 
+* hop 1 waits for the caller's stream (which produced the local K/V it sends);
 * hop ``s`` waits for the compute of step ``s - 2`` (the last reader of the buffer it
   overwrites); the previous hop is ordered by the comm stream itself;
 * the compute stream waits for hop ``s`` right before step ``s``.
@@ -90,7 +91,12 @@ class KVRing:
         self.hops_issued = s
 
     def start(self) -> None:
-        """Issue hop 1 (overlaps the local step 0)."""
+        """Issue hop 1 (overlaps the local step 0).  The caller's K/V were produced on
+        the current stream, so the comm stream first waits for everything enqueued there."""
+        if self.cuda:
+            ready = torch.cuda.Event()
+            ready.record(torch.cuda.current_stream(self.kv[0][0].device))
+            self.stream.wait_event(ready)
         self._hop(1)
 
     def get(self, s: int) -> Tuple[torch.Tensor, torch.Tensor]:
