@@ -1135,6 +1135,8 @@ extern "C" int fa4cp_attn_fwd(const void* q, const void* k, const void* v, void*
   } else {
     if (head_dim == 128) return launch2<Traits2<128, 128, 2, false>>(q, k, v, total_q, total_k, max_seqlen_q, p, st);
     if (head_dim == 64) return launch2<Traits2<64, 128, 3, false>>(q, k, v, total_q, total_k, max_seqlen_q, p, st);
+    // D=256: S (64 keys) x2 + O (256) fill 384 TMEM columns -- one query tile per CTA
+    if (head_dim == 256) return launch<Traits<256, 64, 2, false>>(q, k, v, total_q, total_k, max_seqlen_q, p, st);
   }
   set_last_error("head_dim %d with dtype %d is not supported", head_dim, in_dtype);
   return FA4CP_ERR_UNSUPPORTED;
@@ -1151,4 +1153,40 @@ extern "C" int fa4cp_device_status(int32_t* status, int32_t clear) {
   }
   *status = v;
   return FA4CP_OK;
+}
+
+extern "C" int64_t fa4cp_attn_kv8_workspace_bytes(int64_t total_k, int32_t num_heads_kv,
+                                                  int32_t head_dim) {
+  if (total_k < 0 || num_heads_kv <= 0 || head_dim <= 0) return -1;
+  return 2 * total_k * int64_t(num_heads_kv) * head_dim * 2;
+}
+
+extern "C" int fa4cp_attn_fwd_kv8(const void* q, const void* k8, const void* v8, void* out,
+                                  float* lse, const int32_t* cu_q, const int32_t* cu_k,
+                                  int32_t nseq, int32_t max_seqlen_q, int64_t total_q,
+                                  int64_t total_k, int32_t num_heads_q, int32_t num_heads_kv,
+                                  int32_t head_dim, int32_t q_dtype, int32_t pattern,
+                                  int32_t causal, float softmax_scale, const float* k_descale,
+                                  const float* v_descale, int32_t accumulate, void* workspace,
+                                  int64_t workspace_bytes, void* stream) {
+  FA4CP_CHECK_ARG(q_dtype == FA4CP_DTYPE_BF16 || q_dtype == FA4CP_DTYPE_F16,
+                  "kv8 attention takes an f16 or bf16 query");
+  FA4CP_CHECK_ARG(num_heads_kv > 0 && head_dim > 0 && total_k >= 0, "bad sizes");
+  const int64_t need = fa4cp_attn_kv8_workspace_bytes(total_k, num_heads_kv, head_dim);
+  FA4CP_CHECK_ARG(workspace_bytes >= need, "workspace too small: %lld < %lld bytes",
+                  (long long)workspace_bytes, (long long)need);
+  FA4CP_CHECK_ARG(need == 0 || workspace != nullptr, "workspace is NULL");
+  FA4CP_CHECK_ARG(q_dtype == FA4CP_DTYPE_BF16, "kv8 attention dequantises K/V to bf16; use a bf16 query");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* kb = static_cast<uint8_t*>(workspace);
+  uint8_t* vb = kb + need / 2;
+  if (total_k > 0) {
+    int rc = launch_dequant_e4m3(k8, k_descale, kb, total_k, num_heads_kv, head_dim, st);
+    if (rc) return rc;
+    rc = launch_dequant_e4m3(v8, v_descale, vb, total_k, num_heads_kv, head_dim, st);
+    if (rc) return rc;
+  }
+  return fa4cp_attn_fwd(q, kb, vb, out, lse, cu_q, cu_k, nseq, max_seqlen_q, total_q, total_k,
+                        num_heads_q, num_heads_kv, head_dim, q_dtype, q_dtype, pattern, causal,
+                        softmax_scale, nullptr, nullptr, nullptr, accumulate, stream);
 }

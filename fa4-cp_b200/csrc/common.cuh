@@ -44,6 +44,10 @@ inline int check_launch(const char* what) {
   return FA4CP_OK;
 }
 
+// e4m3 [rows, heads, dim] x descale[heads] -> bf16 (convert.cu)
+int launch_dequant_e4m3(const void* x, const float* descale, void* out, int64_t rows, int heads,
+                        int dim, cudaStream_t st);
+
 inline int elem_bytes(int dtype) {
   switch (dtype) {
     case FA4CP_DTYPE_F16: return 2;

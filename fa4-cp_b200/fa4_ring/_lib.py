@@ -48,6 +48,11 @@ _SIGNATURES = {
     "fa4cp_device_status": [ctypes.POINTER(_i32), _i32],
     "fa4cp_attn_fwd": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i64, _i64, _i32, _i32,
                        _i32, _i32, _i32, _i32, _i32, _f32, _vp, _vp, _vp, _i32, _vp],
+    "fa4cp_attn_fwd_kv8": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i64, _i64, _i32,
+                           _i32, _i32, _i32, _i32, _i32, _f32, _vp, _vp, _i32, _vp, _i64, _vp],
+    "fa4cp_attn_kv8_workspace_bytes": [_i64, _i32, _i32],
+    "fa4cp_dequant_e4m3": [_vp, _vp, _vp, _i64, _i32, _i32, _vp],
+    "fa4cp_quantize_e4m3": [_vp, _i32, _i64, _vp, _vp, _vp],
     "fa4cp_merge_state_inplace": [_vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _vp],
     "fa4cp_merge_states": [ctypes.POINTER(_vp), ctypes.POINTER(_vp), _i32, _vp, _vp, _i64, _i32,
                            _i32, _i32, _vp],
@@ -57,7 +62,7 @@ _SIGNATURES = {
     "fa4cp_half_index": [_vp, _i32, _i64, _i32, _vp, _vp],
     "fa4cp_local_cu": [_vp, _i32, _i32, _vp, _vp],
 }
-_RESTYPE = {"fa4cp_last_error": ctypes.c_char_p}
+_RESTYPE = {"fa4cp_last_error": ctypes.c_char_p, "fa4cp_attn_kv8_workspace_bytes": _i64}
 
 EXPORTED = tuple(_SIGNATURES)
 

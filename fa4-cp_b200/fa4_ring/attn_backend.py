@@ -23,8 +23,14 @@ PATTERN_VARLEN = _lib.PATTERN_VARLEN
 PATTERN_FRONT_KV = _lib.PATTERN_FRONT_KV
 PATTERN_BACK_Q = _lib.PATTERN_BACK_Q
 
-SUPPORTED_HEAD_DIMS = {torch.bfloat16: (64, 128), torch.float16: (64, 128),
+SUPPORTED_HEAD_DIMS = {torch.bfloat16: (64, 128, 256), torch.float16: (64, 128, 256),
                        torch.float8_e4m3fn: (128,)}
+# bf16 query with e4m3 K/V (K/V dequantised to bf16 in a workspace, then the bf16 kernel)
+MIXED_HEAD_DIMS = (64, 128, 256)
+
+
+def is_mixed(q: torch.Tensor, k: torch.Tensor) -> bool:
+    return q.dtype == torch.bfloat16 and k.dtype == torch.float8_e4m3fn
 
 
 def has_backend() -> bool:
@@ -59,12 +65,17 @@ def out_dtype_for(dt: torch.dtype) -> torch.dtype:
 def _check_qkv(q, k, v):
     _lib.require_cuda(q, k, v)
     assert q.dim() == 3 and k.dim() == 3 and v.dim() == 3, "expected [T, H, D] tensors"
-    assert q.dtype == k.dtype == v.dtype, "q, k, v must share a dtype"
+    assert k.dtype == v.dtype, "k and v must share a dtype"
+    assert q.dtype == k.dtype or is_mixed(q, k), (
+        "q, k, v must share a dtype (or bf16 q with e4m3 k/v)")
     assert k.shape == v.shape, "k and v must have the same shape"
     assert q.shape[2] == k.shape[2], "q and k head_dim differ"
     H, Hkv, D = q.shape[1], k.shape[1], q.shape[2]
     assert H % Hkv == 0, f"H_q={H} not a multiple of H_kv={Hkv}"
-    if q.dtype not in SUPPORTED_HEAD_DIMS or D not in SUPPORTED_HEAD_DIMS[q.dtype]:
+    if is_mixed(q, k):
+        if D not in MIXED_HEAD_DIMS:
+            raise NotImplementedError(f"head_dim {D} is not supported for bf16 q x e4m3 kv")
+    elif q.dtype not in SUPPORTED_HEAD_DIMS or D not in SUPPORTED_HEAD_DIMS[q.dtype]:
         raise NotImplementedError(f"head_dim {D} with dtype {q.dtype} is not supported")
 
 
@@ -82,15 +93,27 @@ def attn_into(q, k, v, out, lse, cu_q, cu_k, *, nseq: int, max_seqlen_q: int, pa
     if timer is not None:
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         ev0.record()
-    rc = lib.fa4cp_attn_fwd(
-        q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), lse.data_ptr(),
-        cu_q.data_ptr(), _lib.ptr(cu_k), nseq, max_seqlen_q, q.shape[0], k.shape[0],
-        q.shape[1], k.shape[1], q.shape[2], _lib.dtype_code(q.dtype),
-        _lib.dtype_code(out.dtype), pattern, 1 if causal else 0, float(softmax_scale),
-        _lib.ptr(q_descale), _lib.ptr(k_descale), _lib.ptr(v_descale), 1 if accumulate else 0,
-        _lib.stream_of(q))
-    _lib.check(rc, "attn_fwd")
-    _lib.count_launches()
+    if is_mixed(q, k):
+        ws_bytes = lib.fa4cp_attn_kv8_workspace_bytes(k.shape[0], k.shape[1], k.shape[2])
+        ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=q.device)
+        rc = lib.fa4cp_attn_fwd_kv8(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), lse.data_ptr(),
+            cu_q.data_ptr(), _lib.ptr(cu_k), nseq, max_seqlen_q, q.shape[0], k.shape[0],
+            q.shape[1], k.shape[1], q.shape[2], _lib.dtype_code(q.dtype), pattern,
+            1 if causal else 0, float(softmax_scale), _lib.ptr(k_descale), _lib.ptr(v_descale),
+            1 if accumulate else 0, ws.data_ptr(), ws.numel(), _lib.stream_of(q))
+        _lib.check(rc, "attn_fwd_kv8")
+        _lib.count_launches(3)
+    else:
+        rc = lib.fa4cp_attn_fwd(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), lse.data_ptr(),
+            cu_q.data_ptr(), _lib.ptr(cu_k), nseq, max_seqlen_q, q.shape[0], k.shape[0],
+            q.shape[1], k.shape[1], q.shape[2], _lib.dtype_code(q.dtype),
+            _lib.dtype_code(out.dtype), pattern, 1 if causal else 0, float(softmax_scale),
+            _lib.ptr(q_descale), _lib.ptr(k_descale), _lib.ptr(v_descale),
+            1 if accumulate else 0, _lib.stream_of(q))
+        _lib.check(rc, "attn_fwd")
+        _lib.count_launches()
     if timer is not None:
         ev1.record()
         timer.append((ev0, ev1, pattern))
@@ -134,9 +157,10 @@ def b200_attn(
     cu_k = cu_seqlens_k.to(device=dev, dtype=torch.int32).contiguous()
     h_kv = k.shape[1]
     fp8 = q.dtype == torch.float8_e4m3fn
+    kv8 = k.dtype == torch.float8_e4m3fn
     qd = norm_descale(q_descale, h_kv, dev) if fp8 else None
-    kd = norm_descale(k_descale, h_kv, dev) if fp8 else None
-    vd = norm_descale(v_descale, h_kv, dev) if fp8 else None
+    kd = norm_descale(k_descale, h_kv, dev) if kv8 else None
+    vd = norm_descale(v_descale, h_kv, dev) if kv8 else None
     q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
     out = torch.empty(q.shape, dtype=out_dtype_for(q.dtype), device=dev)
     lse = torch.empty(q.shape[:2], dtype=torch.float32, device=dev)

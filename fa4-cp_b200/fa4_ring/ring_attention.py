@@ -141,15 +141,16 @@ def ring_forward(local_q, kv_at, step_done, cfg: RingConfig, *, cu: torch.Tensor
     k0, _ = kv_at(0)
     Hkv = k0.shape[1]
     fp8 = q.dtype == torch.float8_e4m3fn
+    kv8 = k0.dtype == torch.float8_e4m3fn  # e4m3 K/V, with an e4m3 or a bf16 query
     qd = norm_descale(descales.q, Hkv, dev) if (fp8 and descales and descales.q is not None) else None
 
     def kd(src):
-        if fp8 and descales and descales.k:
+        if kv8 and descales and descales.k:
             return norm_descale(descales.k[src], Hkv, dev)
         return None
 
     def vd(src):
-        if fp8 and descales and descales.v:
+        if kv8 and descales and descales.v:
             return norm_descale(descales.v[src], Hkv, dev)
         return None
 

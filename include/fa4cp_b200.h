@@ -84,7 +84,7 @@ FA4CP_API int fa4cp_device_status(int32_t* status, int32_t clear);
  *                1: merge this partial into (out, lse) in place, online-softmax,
  *                   natural-log (the incremental merge of fa4_ring/merge.py:45-64 fused
  *                   into the epilogue); rows not covered are left untouched.
- * Supported: head_dim 64 or 128 (f16/bf16), 128 (e4m3); Hq % Hkv == 0.
+ * Supported: head_dim 64, 128 or 256 (f16/bf16), 128 (e4m3); Hq % Hkv == 0.
  */
 FA4CP_API int fa4cp_attn_fwd(const void* q, const void* k, const void* v, void* out, float* lse,
                    const int32_t* cu_q, const int32_t* cu_k, int32_t nseq, int32_t max_seqlen_q,
@@ -93,6 +93,47 @@ FA4CP_API int fa4cp_attn_fwd(const void* q, const void* k, const void* v, void* 
                    int32_t causal, float softmax_scale, const float* q_descale,
                    const float* k_descale, const float* v_descale, int32_t accumulate,
                    void* stream);
+
+/*
+ * Attention with a bf16 query and e4m3 keys/values (mixed precision, e.g. FP8 KV with a
+ * bf16 Q).  One tcgen05 MMA takes a single operand type, so K and V are first
+ * dequantised (value x per-kv-head descale) into `workspace` as bf16 and attended by the
+ * bf16 kernel.  Arguments as fa4cp_attn_fwd (out/lse in the query dtype / float32);
+ * k_descale, v_descale: NULL or float32 [Hkv].
+ *   workspace        device buffer of >= fa4cp_attn_kv8_workspace_bytes(total_k, Hkv, D)
+ *                    bytes (scratch: contents are overwritten; calls sharing it must not
+ *                    overlap on the GPU).
+ * Replaces: the FP8-KV path of fa4_ring/fa4_backend.py:99-120 (FA4 `k_descale`/`v_descale`
+ * with a non-FP8 query) used by the cfg "bf16 Q, FP8 e4m3 KV" of the reference's ring.
+ */
+FA4CP_API int fa4cp_attn_fwd_kv8(const void* q, const void* k8, const void* v8, void* out,
+                                 float* lse, const int32_t* cu_q, const int32_t* cu_k,
+                                 int32_t nseq, int32_t max_seqlen_q, int64_t total_q,
+                                 int64_t total_k, int32_t num_heads_q, int32_t num_heads_kv,
+                                 int32_t head_dim, int32_t q_dtype, int32_t pattern,
+                                 int32_t causal, float softmax_scale, const float* k_descale,
+                                 const float* v_descale, int32_t accumulate, void* workspace,
+                                 int64_t workspace_bytes, void* stream);
+
+/* Workspace bytes fa4cp_attn_fwd_kv8 needs (2 * total_k * Hkv * D * 2), or -1 on bad input. */
+FA4CP_API int64_t fa4cp_attn_kv8_workspace_bytes(int64_t total_k, int32_t num_heads_kv,
+                                                 int32_t head_dim);
+
+/*
+ * e4m3 -> bf16 dequantisation: out = x * descale[head], x [rows, heads, dim] (dim % 16 == 0).
+ * Replaces: the dequantised-KV path FA4 runs internally for descaled FP8 inputs.
+ */
+FA4CP_API int fa4cp_dequant_e4m3(const void* x, const float* descale, void* out, int64_t rows,
+                                 int32_t heads, int32_t dim, void* stream);
+
+/*
+ * Per-tensor e4m3 quantisation of n elements (f16 | bf16 | f32): *scale = amax / 448
+ * (1 if the tensor is all zero), out = satfinite(x / *scale) as e4m3.  `scale` is a device
+ * float written by the call.  This is the per-rank quantisation the FP8 configs prescribe
+ * before the ring (each rank's K/V descales are then all-gathered, indexed by source rank).
+ */
+FA4CP_API int fa4cp_quantize_e4m3(const void* x, int32_t dtype, int64_t n, void* out,
+                                  float* scale, void* stream);
 
 /*
  * In-place 2-way LSE merge: (v, s) <- merge((v, s), (v_other, s_other)).

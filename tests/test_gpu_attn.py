@@ -157,3 +157,52 @@ def test_ring_step_patterns(pattern, accumulate):
         np.testing.assert_allclose(got_l[covered], want_l[covered], atol=LSE_TOL, rtol=0)
         assert np.all(got_o[~covered] == 7.0) and np.all(got_l[~covered] == 7.0)
     assert_device_ok()
+
+
+HD256_CASES = [
+    ([300], [300], 2, 1, 256, True, torch.bfloat16),
+    ([129, 64], [129, 64], 4, 2, 256, False, torch.float16),
+    ([640], [640], 2, 2, 256, True, torch.bfloat16),
+]
+
+
+@pytest.mark.parametrize("case", HD256_CASES, ids=[str(i) for i in range(len(HD256_CASES))])
+def test_attn_head_dim_256(case):
+    _run_case(*case)
+
+
+@pytest.mark.parametrize("D,causal", [(128, True), (256, True), (256, False), (64, False)])
+def test_attn_bf16_query_e4m3_kv(D, causal):
+    """bf16 Q with e4m3 K/V (per-tensor descales): vs the oracle on dequantised K/V."""
+    from fa4_ring.attn_backend import b200_attn
+    g = torch.Generator().manual_seed(D)
+    T, H, Hkv = 333, 4, 2
+    q = (torch.randn(T, H, D, generator=g) * 0.5).bfloat16()
+    (k8, ks), (v8, vs) = (quant_e4m3(torch.randn(T, Hkv, D, generator=g) * 0.5) for _ in range(2))
+    scale = 1.0 / math.sqrt(D)
+    out, lse = b200_attn(q.cuda(), k8.cuda(), v8.cuda(), causal=causal, softmax_scale=scale,
+                         k_descale=ks.cuda(), v_descale=vs.reshape(1).expand(Hkv).cuda())
+    assert out.dtype == torch.bfloat16
+    wo, wl = orc.attn(to_np(q), dequant(k8, ks), dequant(v8, vs), causal, scale)
+    np.testing.assert_allclose(to_np(out), wo, atol=OUT_TOL[torch.float8_e4m3fn], rtol=0)
+    np.testing.assert_allclose(to_np(lse), wl, atol=1e-2, rtol=0)
+    assert_device_ok()
+
+
+def test_quantize_and_dequantize_e4m3():
+    from fa4_ring.fp8 import dequantize_e4m3, quantize_e4m3
+    g = torch.Generator().manual_seed(4)
+    x = (torch.randn(257, 3, 128, generator=g) * 3).bfloat16().cuda()
+    x8, scale = quantize_e4m3(x)
+    amax = x.float().abs().max()
+    assert torch.allclose(scale, amax / 448.0, rtol=0, atol=0)
+    want8 = (x.float() / scale).to(torch.float8_e4m3fn)
+    assert torch.equal(x8.view(torch.uint8), want8.view(torch.uint8))
+    d = dequantize_e4m3(x8, scale)
+    assert torch.equal(d, (x8.float() * scale).bfloat16())
+    per_head = torch.tensor([0.5, 2.0, 1.0], device="cuda")
+    d2 = dequantize_e4m3(x8, per_head)
+    assert torch.equal(d2, (x8.float() * per_head[None, :, None]).bfloat16())
+    z8, zs = quantize_e4m3(torch.zeros(64, device="cuda", dtype=torch.bfloat16))
+    assert float(zs) == 1.0 and torch.all(z8.float() == 0)
+    assert_device_ok()
