@@ -115,6 +115,31 @@ FA4CP_API int fa4cp_attn_fwd_kv8(const void* q, const void* k8, const void* v8, 
                                  const float* v_descale, int32_t accumulate, void* workspace,
                                  int64_t workspace_bytes, void* stream);
 
+/*
+ * fa4cp_attn_fwd_kv8 without a workspace argument, for callers that cannot allocate
+ * device memory when they call (an engine whose memory is already reserved for its own
+ * pools, a caller that must not risk the synchronisation of cudaMalloc/cudaFree, or a
+ * binding that holds only the tensors it was given).  The dequantised K/V go to a fixed
+ * 32 MiB scratch array compiled into the library, so nothing is allocated.
+ * No counterpart in the reference (its FA4 call allocates internally).
+ *   limit: total_k * num_heads_kv * head_dim <= 8,388,608 (K and V in bf16 fill the 32 MiB);
+ *          larger calls return FA4CP_ERR_INVALID;
+ *   every GPU that loads this part of the library holds the 32 MiB until process exit;
+ *   all calls on a device share the array (it keeps the last call's contents; nothing in
+ *   it needs to start at zero); calls that overlap on the GPU race and must be serialised;
+ *   the first call on a device looks up the array's device address (cudaGetSymbolAddress)
+ *   and should come before any stream capture.
+ * Other arguments as fa4cp_attn_fwd_kv8.
+ */
+FA4CP_API int fa4cp_attn_fwd_kv8_noalloc(const void* q, const void* k8, const void* v8, void* out,
+                                         float* lse, const int32_t* cu_q, const int32_t* cu_k,
+                                         int32_t nseq, int32_t max_seqlen_q, int64_t total_q,
+                                         int64_t total_k, int32_t num_heads_q,
+                                         int32_t num_heads_kv, int32_t head_dim, int32_t q_dtype,
+                                         int32_t pattern, int32_t causal, float softmax_scale,
+                                         const float* k_descale, const float* v_descale,
+                                         int32_t accumulate, void* stream);
+
 /* Workspace bytes fa4cp_attn_fwd_kv8 needs (2 * total_k * Hkv * D * 2), or -1 on bad input. */
 FA4CP_API int64_t fa4cp_attn_kv8_workspace_bytes(int64_t total_k, int32_t num_heads_kv,
                                                  int32_t head_dim);
