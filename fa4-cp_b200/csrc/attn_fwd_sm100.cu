@@ -48,6 +48,9 @@ struct Params {
   int in_fmt;    // kind::f16 operand format: 0 f16, 1 bf16 (unused for e4m3)
   int out_bf16;  // 1 -> bf16 output, 0 -> f16 output
   float scale_log2;
+  // self-test only (fa4cp_selftest_wait_expiry): index of the KV tile whose K copy the
+  // producer never issues, so the consumer's bounded wait must expire; -1 otherwise
+  int debug_withhold_kv;
 };
 
 template <int D_, int BN_, int STAGES_, bool FP8_>
@@ -191,12 +194,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int s = j % ST, ph = (j / ST) & 1;
         const int row = g.k_start + j * BN;
         if (j >= ST && !mbar_wait(k_empty(s), ph ^ 1, abort, kErrKEmpty, status)) break;
-        mbar_arrive_expect_tx(k_full(s), TR::KV_BYTES);
+        if (j != p.debug_withhold_kv) {
+          mbar_arrive_expect_tx(k_full(s), TR::KV_BYTES);
 #pragma unroll
-        for (int c = 0; c < TR::NCH; ++c)
-          tma_load_3d_hint(smem_u32(smem + TR::OFF_K + s * TR::KV_BYTES + c * TR::KV_CHUNK_BYTES),
-                           &tmK, c * TR::CHUNK, kvh, row, k_full(s), pol_kv);
-        last_k[s] = j;
+          for (int c = 0; c < TR::NCH; ++c)
+            tma_load_3d_hint(smem_u32(smem + TR::OFF_K + s * TR::KV_BYTES + c * TR::KV_CHUNK_BYTES),
+                             &tmK, c * TR::CHUNK, kvh, row, k_full(s), pol_kv);
+          last_k[s] = j;
+        }
         if (j >= ST && !mbar_wait(v_empty(s), ph ^ 1, abort, kErrVEmpty, status)) break;
         mbar_arrive_expect_tx(v_full(s), TR::KV_BYTES);
 #pragma unroll
@@ -205,14 +210,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                            &tmV, c * TR::CHUNK, kvh, row, v_full(s), pol_kv);
         last_v[s] = j;
       }
-      if (*abort) {
-        // give-up path: let every copy already issued land before the CTA exits
-        int zero = 0;
-        volatile int* no_abort = &zero;
-        mbar_wait(q_full, 0, no_abort, kErrDrain, status);
+      {
+        // every copy this thread issued has landed before it leaves its role (on the
+        // normal path the consumers already waited for them, so this returns at once)
+        mbar_wait_drain(q_full, 0, kErrDrain, status);
         for (int s = 0; s < ST; ++s) {
-          if (last_k[s] >= 0) mbar_wait(k_full(s), (last_k[s] / ST) & 1, no_abort, kErrDrain, status);
-          if (last_v[s] >= 0) mbar_wait(v_full(s), (last_v[s] / ST) & 1, no_abort, kErrDrain, status);
+          if (last_k[s] >= 0) mbar_wait_drain(k_full(s), (last_k[s] / ST) & 1, kErrDrain, status);
+          if (last_v[s] >= 0) mbar_wait_drain(v_full(s), (last_v[s] / ST) & 1, kErrDrain, status);
         }
       }
     }
@@ -268,9 +272,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ok && n_kv > 0) issue_pv(n_kv - 1);
       // every MMA issued above has completed before TMEM is released
       tc_commit(td_bar);
-      int zero = 0;
-      volatile int* no_abort = &zero;
-      mbar_wait(td_bar, 0, no_abort, kErrDrain, status);
+      mbar_wait_drain(td_bar, 0, kErrDrain, status);
     }
   } else {
     // ------------------------------------------------------------ softmax + epilogue
@@ -630,12 +632,14 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
         const int s = j % ST, ph = (j / ST) & 1;
         const int row = g.k_start + j * BN;
         if (j >= ST && !mbar_wait(k_empty(s), ph ^ 1, abort, kErrKEmpty, status)) break;
-        mbar_arrive_expect_tx(k_full(s), TR::KV_BYTES);
+        if (j != p.debug_withhold_kv) {
+          mbar_arrive_expect_tx(k_full(s), TR::KV_BYTES);
 #pragma unroll
-        for (int c = 0; c < TR::NCH; ++c)
-          tma_load_3d_hint(smem_u32(smem + TR::OFF_K + s * TR::KV_BYTES + c * TR::KV_CHUNK_BYTES),
-                           &tmK, c * TR::CHUNK, kvh, row, k_full(s), pol_kv);
-        last_k[s] = j;
+          for (int c = 0; c < TR::NCH; ++c)
+            tma_load_3d_hint(smem_u32(smem + TR::OFF_K + s * TR::KV_BYTES + c * TR::KV_CHUNK_BYTES),
+                             &tmK, c * TR::CHUNK, kvh, row, k_full(s), pol_kv);
+          last_k[s] = j;
+        }
         if (j >= ST && !mbar_wait(v_empty(s), ph ^ 1, abort, kErrVEmpty, status)) break;
         mbar_arrive_expect_tx(v_full(s), TR::KV_BYTES);
 #pragma unroll
@@ -644,13 +648,13 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
                            &tmV, c * TR::CHUNK, kvh, row, v_full(s), pol_kv);
         last_v[s] = j;
       }
-      if (*abort) {
-        int zero = 0;
-        volatile int* no_abort = &zero;
-        mbar_wait(q_full, 0, no_abort, kErrDrain, status);
+      {
+        // every copy this thread issued has landed before it leaves its role (on the
+        // normal path the consumers already waited for them, so this returns at once)
+        mbar_wait_drain(q_full, 0, kErrDrain, status);
         for (int s = 0; s < ST; ++s) {
-          if (last_k[s] >= 0) mbar_wait(k_full(s), (last_k[s] / ST) & 1, no_abort, kErrDrain, status);
-          if (last_v[s] >= 0) mbar_wait(v_full(s), (last_v[s] / ST) & 1, no_abort, kErrDrain, status);
+          if (last_k[s] >= 0) mbar_wait_drain(k_full(s), (last_k[s] / ST) & 1, kErrDrain, status);
+          if (last_v[s] >= 0) mbar_wait_drain(v_full(s), (last_v[s] / ST) & 1, kErrDrain, status);
         }
       }
     }
@@ -740,9 +744,7 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
       }
       // every MMA issued above has completed before TMEM is released
       tc_commit(td_bar);
-      int zero = 0;
-      volatile int* no_abort = &zero;
-      mbar_wait(td_bar, 0, no_abort, kErrDrain, status);
+      mbar_wait_drain(td_bar, 0, kErrDrain, status);
     }
    }
   } else {
@@ -1127,6 +1129,7 @@ extern "C" int fa4cp_attn_fwd(const void* q, const void* k, const void* v, void*
   p.in_fmt = in_dtype == FA4CP_DTYPE_BF16 ? 1 : 0;
   p.out_bf16 = out_dtype == FA4CP_DTYPE_BF16 ? 1 : 0;
   p.scale_log2 = softmax_scale * kLog2e;
+  p.debug_withhold_kv = -1;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
 
   if (fp8) {
@@ -1189,4 +1192,40 @@ extern "C" int fa4cp_attn_fwd_kv8(const void* q, const void* k8, const void* v8,
   return fa4cp_attn_fwd(q, kb, vb, out, lse, cu_q, cu_k, nseq, max_seqlen_q, total_q, total_k,
                         num_heads_q, num_heads_kv, head_dim, q_dtype, q_dtype, pattern, causal,
                         softmax_scale, nullptr, nullptr, nullptr, accumulate, stream);
+}
+
+extern "C" int fa4cp_selftest_wait_expiry(const void* q, const void* k, const void* v, void* out,
+                                          float* lse, const int32_t* cu, int32_t seqlen,
+                                          int32_t* status_out, void* stream) {
+  FA4CP_CHECK_ARG(seqlen >= 1 && seqlen <= 4096, "seqlen must be in [1, 4096]");
+  FA4CP_CHECK_ARG(q && k && v && out && lse && cu && status_out, "null pointer");
+  FA4CP_CHECK_ARG(aligned16(q) && aligned16(k) && aligned16(v) && aligned16(out),
+                  "tensors must be 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int zero = 0;
+  FA4CP_CHECK_CUDA(cudaStreamSynchronize(st));
+  FA4CP_CHECK_CUDA(cudaMemcpyToSymbol(g_attn_status, &zero, sizeof(int)));
+  Params p{};
+  p.cu_q = cu;
+  p.cu_k = cu;
+  p.out = out;
+  p.lse = lse;
+  p.nseq = 1;
+  p.Hq = 1;
+  p.Hkv = 1;
+  p.group = 1;
+  p.pattern = FA4CP_PATTERN_VARLEN;
+  p.causal = 1;
+  p.in_fmt = 1;
+  p.out_bf16 = 1;
+  p.scale_log2 = kLog2e / sqrtf(128.0f);
+  p.debug_withhold_kv = 0;  // the consumer's wait for K tile 0 can only run out
+  int rc = launch2<Traits2<128, 128, 2, false>>(q, k, v, seqlen, seqlen, seqlen, p, st);
+  if (rc) return rc;
+  FA4CP_CHECK_CUDA(cudaStreamSynchronize(st));
+  int observed = 0;
+  FA4CP_CHECK_CUDA(cudaMemcpyFromSymbol(&observed, g_attn_status, sizeof(int)));
+  FA4CP_CHECK_CUDA(cudaMemcpyToSymbol(g_attn_status, &zero, sizeof(int)));
+  *status_out = observed;
+  return FA4CP_OK;
 }

@@ -139,6 +139,23 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   }
 }
 
+// Wait used only on the give-up path, for work this CTA itself already issued (TMA
+// copies, MMAs): they always finish, and the CTA must not exit or free TMEM before they
+// do.  It ignores the abort flags (which are set on this path) and is bounded by time
+// alone; if even that runs out it records `code` and returns false.
+__device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity, int code,
+                                                int* status) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 255u) == 0 && clock64() - t0 > kWaitLimitCycles) {
+      atomicCAS(status, 0, code);
+      return false;
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // TMA (bulk tensor copies, global -> shared), no multicast
 // ---------------------------------------------------------------------------
@@ -299,6 +316,21 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
       "r"(r[29]), "r"(r[30]), "r"(r[31])
       : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void reg_fence16(uint32_t (&r)[16]) {
+  asm volatile(""
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+                 "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
+                 "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]));
 }
 // 16 columns variant (used for 8-bit P, which packs 4 values per column).
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {

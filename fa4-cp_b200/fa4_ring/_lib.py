@@ -46,6 +46,7 @@ _SIGNATURES = {
     "fa4cp_version": [],
     "fa4cp_last_error": [],
     "fa4cp_device_status": [ctypes.POINTER(_i32), _i32],
+    "fa4cp_selftest_wait_expiry": [_vp, _vp, _vp, _vp, _vp, _vp, _i32, ctypes.POINTER(_i32), _vp],
     "fa4cp_attn_fwd": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i64, _i64, _i32, _i32,
                        _i32, _i32, _i32, _i32, _i32, _f32, _vp, _vp, _vp, _i32, _vp],
     "fa4cp_attn_fwd_kv8": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i64, _i64, _i32,

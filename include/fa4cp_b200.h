@@ -62,6 +62,19 @@ FA4CP_API const char* fa4cp_last_error(void);
 FA4CP_API int fa4cp_device_status(int32_t* status, int32_t clear);
 
 /*
+ * Self-test of the kernels' failure handling, with no GPU fault: launches one small
+ * causal attention (q/k/v [seqlen, 1, 128] bf16, out bf16, lse float32, cu = {0, seqlen})
+ * whose copy of K tile 0 is withheld, so the consumer's bounded mbarrier wait (~2 s) must
+ * give up.  The kernel then records a status code, lets its issued copies and MMAs
+ * finish, frees its tensor memory and returns.  Synchronises `stream`, writes the status
+ * word the kernel recorded to *status_out (non-zero expected) and clears it.
+ * No counterpart in the reference (its kernels come from FA4 and have no such path).
+ */
+FA4CP_API int fa4cp_selftest_wait_expiry(const void* q, const void* k, const void* v, void* out,
+                                         float* lse, const int32_t* cu, int32_t seqlen,
+                                         int32_t* status_out, void* stream);
+
+/*
  * Variable-length attention forward returning out + LSE; also the three zig-zag
  * ring step patterns with in-place row addressing (no gathers).
  *
