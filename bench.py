@@ -42,6 +42,50 @@ METRIC = "causal ring-attn prefill TFLOP/s/GPU @cp=1/2/4/8; % tensor peak; expos
 CFG2 = dict(N=32768, Hq=32, Hkv=8, D=128)
 L2_FLUSH_BYTES = 256 << 20
 
+# BASELINE.json configs[1..4]; "kind": operand types (bf16 | e4m3 q/k/v | bf16 q + e4m3 k/v)
+CONFIGS = {
+    "cfg2": dict(kind="bf16", lens=[32768], Hq=32, Hkv=8, D=128, amp=1.0,
+                 text="bf16 single sequence, N=32768, Hq=32, Hkv=8, D=128"),
+    "cfg3": dict(kind="e4m3", lens=[131072], Hq=32, Hkv=8, D=128, amp=1.0,
+                 text="FP8 e4m3 q/k/v quantised per rank (scale=amax/448), N=131072, Hq=32, "
+                      "Hkv=8, D=128, k/v descales all-gathered by source rank"),
+    "cfg4": dict(kind="bf16", lens="varlen16", Hq=16, Hkv=2, D=128, amp=1.0,
+                 text="packed varlen bf16, 16 sequences N_j ~ U[1024,16384] (seed 0) rounded up "
+                      "to a multiple of 2*cp, Hq=16, Hkv=2, D=128"),
+    "cfg5": dict(kind="mixed", lens=[262144], Hq=16, Hkv=2, D=256, amp=0.5,
+                 text="bf16 q with e4m3 k/v (per rank amax/448), N=262144, Hq=16, Hkv=2, D=256, "
+                      "q/k/v ~ 0.5*N(0,1)"),
+}
+
+
+def config_lens(name, cp, seq_len=None):
+    c = CONFIGS[name]
+    if c["lens"] == "varlen16":
+        rng = np.random.default_rng(0)
+        raw = rng.integers(1024, 16385, size=16)
+        m = 2 * cp
+        return [int((n + m - 1) // m * m) for n in raw]
+    return [seq_len if seq_len else c["lens"][0]]
+
+
+def measure_fp8_peak(dev):
+    """Dense e4m3 GEMM throughput on this GPU (torch._scaled_mm, 8192^3, best of 10)."""
+    n = 8192
+    a = torch.randn(n, n, device=dev).to(torch.float8_e4m3fn)
+    b = torch.randn(n, n, device=dev).to(torch.float8_e4m3fn).t()
+    one = torch.tensor(1.0, device=dev)
+    for _ in range(3):
+        torch._scaled_mm(a, b, scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
+    best = float("inf")
+    for _ in range(10):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        torch._scaled_mm(a, b, scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
+        e1.record()
+        torch.cuda.synchronize()
+        best = min(best, e0.elapsed_time(e1))
+    return 2.0 * n ** 3 / (best * 1e-3) / 1e12
+
 
 def causal_flops(N, Hq, D):
     return 2.0 * N * N * Hq * D
@@ -164,28 +208,56 @@ def gpu_main(args, rank, world, local_rank):
     from fa4_ring import _lib, attn_backend
     from fa4_ring.ring_attention import ring_forward, _single_cu
 
+    from fa4_ring import Descales
+    from fa4_ring.fp8 import allgather_descales, quantize_e4m3
+    from fa4_ring.zigzag import zigzag_shard_varlen
+
     dev = torch.device("cuda", local_rank)
-    Hq, Hkv, D = CFG2["Hq"], CFG2["Hkv"], CFG2["D"]
-    N = args.seq_len
+    C = CONFIGS[args.config]
+    Hq, Hkv, D = C["Hq"], C["Hkv"], C["D"]
     cp = world
-    assert N % (2 * cp) == 0
+    lens = config_lens(args.config, cp, args.seq_len)
+    for n in lens:
+        assert n % (2 * cp) == 0, f"sequence length {n} not divisible by 2*cp"
+    full_cu = [0] + [int(x) for x in np.cumsum(lens)]
+    N = full_cu[-1]
     g = torch.Generator(device=dev).manual_seed(1234)
-    shards = []
+    shards, lcu = [], None
     for h in (Hq, Hkv, Hkv):
         full = torch.randn(N, h, D, generator=g, device=dev, dtype=torch.bfloat16)
-        shards.append(zigzag_shard(full, rank, cp))
+        if C["amp"] != 1.0:
+            full.mul_(C["amp"])
+        loc, lcu = zigzag_shard_varlen(full, full_cu, rank, cp)
+        shards.append(loc)
         del full
     lq, lk, lv = shards
+    varlen = len(lens) > 1
+    cu_arg = lcu if varlen else None
+    max_local = max(lens) // cp
+    desc = None
+    if C["kind"] in ("e4m3", "mixed"):
+        # per-rank quantisation (amax/448); k/v descales all-gathered once, by source rank
+        lk, ks = quantize_e4m3(lk)
+        lv, vs = quantize_e4m3(lv)
+        qs = None
+        if C["kind"] == "e4m3":
+            lq, qs = quantize_e4m3(lq)
+        if world > 1:
+            ks_all, vs_all = allgather_descales(ks), allgather_descales(vs)
+        else:
+            ks_all, vs_all = [ks], [vs]
+        desc = Descales(q=qs, k=ks_all, v=vs_all)
     cfg = RingConfig(cp_size=cp, cp_rank=rank, merge_mode=args.merge)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
-    step_flops = causal_flops(N, Hq, D)  # whole job, per step
+    step_flops = float(sum(causal_flops(n, Hq, D) for n in lens))  # whole job, per step
 
     def barrier():
         if world > 1:
             dist.barrier()
 
     def run():
-        return ring_flash_attn(lq, lk, lv, cfg)
+        return ring_flash_attn(lq, lk, lv, cfg, descales=desc, cu_seqlens=cu_arg,
+                               max_seqlen=max_local if varlen else None)
 
     # ---- warm-up
     for _ in range(args.warmup):
@@ -220,11 +292,11 @@ def gpu_main(args, rank, world, local_rank):
     # ---- exposed communication: same schedule with the transfers skipped
     exposed = None
     if world > 1 and not args.quick:
-        cu = _single_cu(lq.shape[0], dev)
+        cu = lcu if varlen else _single_cu(lq.shape[0], dev)
 
         def run_nocomm():
-            return ring_forward(lq, lambda s: (lk, lv), lambda s: None, cfg, cu=cu, nseq=1,
-                                max_seqlen=lq.shape[0])
+            return ring_forward(lq, lambda s: (lk, lv), lambda s: None, cfg, cu=cu,
+                                nseq=cu.numel() - 1, max_seqlen=max_local, descales=desc)
         for _ in range(2):
             run_nocomm()
         torch.cuda.synchronize()
@@ -248,8 +320,9 @@ def gpu_main(args, rank, world, local_rank):
             dist.all_reduce(vals, op=dist.ReduceOp.MAX)
         if rank == 0:
             ms_step = vals[0].item() / args.steps
-            return {"quick": True, "seq_len": N, "cp": cp, "ms_per_step": round(ms_step, 4),
-                    "value": round(causal_flops(N, Hq, D) / (ms_step * 1e-3) / 1e12, 2),
+            return {"quick": True, "config": args.config, "seq_len": N, "cp": cp,
+                    "ms_per_step": round(ms_step, 4),
+                    "value": round(step_flops / (ms_step * 1e-3) / 1e12, 2),
                     "attn_ms": round(vals[1].item() / args.steps, 4), "gpu_launches": gpu_launches,
                     "device_status": status}
         return None
@@ -263,7 +336,8 @@ def gpu_main(args, rank, world, local_rank):
         dq.copy_(hq, non_blocking=True)
         dk.copy_(hk, non_blocking=True)
         dv.copy_(hv, non_blocking=True)
-        out = ring_flash_attn(dq, dk, dv, cfg)
+        out = ring_flash_attn(dq, dk, dv, cfg, descales=desc, cu_seqlens=cu_arg,
+                              max_seqlen=max_local if varlen else None)
         hout.copy_(out, non_blocking=True)
 
     for _ in range(2):
@@ -300,10 +374,15 @@ def gpu_main(args, rank, world, local_rank):
     value = step_flops / (ms_step * 1e-3) / 1e12
     peaks, peaks_kind = load_peaks()
     # attention roofline: every attention launch of one rank in the timed region;
-    # algorithmic FLOPs of one rank per step = 2*N^2*Hq*D / cp
+    # algorithmic FLOPs of one rank per step = (sum_j 2*N_j^2*Hq*D) / cp (zig-zag balance)
     attn_flops_rank = step_flops / cp * args.steps
     achieved = attn_flops_rank / (attn_ms * 1e-3) / 1e12 if attn_ms > 0 else None
-    peak = peaks["bf16_tflops"]
+    if C["kind"] == "e4m3":
+        peak = round(measure_fp8_peak(dev), 1)
+        peak_kind = "measured on this GPU now: e4m3 torch._scaled_mm 8192^3 (burst)"
+    else:
+        peak = peaks["bf16_tflops"]
+        peak_kind = f"{peaks_kind} bf16 dense (burst)"
     line = {
         "metric": METRIC,
         "value": round(value, 2),
@@ -315,11 +394,13 @@ def gpu_main(args, rank, world, local_rank):
         "higher_is_better": True,
         "scaling": "strong",
         "vs_baseline": None,
-        "dtype": "bf16",
-        "data": "synthetic: q/k/v ~ N(0,1) bf16 from seed 1234",
-        "config": {"workload": f"cfg2: causal ring-attention forward, bf16, N={N}, Hq=32, "
-                               f"Hkv=8, D=128, scale=1/sqrt(128), cp={cp}, merge={args.merge}",
-                   "seq_len": N, "num_heads_q": Hq, "num_heads_kv": Hkv, "head_dim": D,
+        "dtype": {"bf16": "bf16", "e4m3": "e4m3", "mixed": "bf16 q, e4m3 k/v"}[C["kind"]],
+        "data": "synthetic: q/k/v ~ N(0,1) bf16 from seed 1234"
+                + (f" x {C['amp']}" if C["amp"] != 1.0 else ""),
+        "config": {"workload": f"{args.config}: causal ring-attention forward, {C['text']}, "
+                               f"scale=1/sqrt(D), cp={cp}, merge={args.merge}",
+                   "seq_len": N, "num_seqs": len(lens), "num_heads_q": Hq, "num_heads_kv": Hkv,
+                   "head_dim": D,
                    "cp": cp, "merge_mode": args.merge, "parallelism": f"cp{cp} zig-zag ring",
                    "l2": "flushed before every timed step (256 MiB write, untimed)"},
         "per_gpu_tflops": round(value / world, 2),
@@ -327,7 +408,7 @@ def gpu_main(args, rank, world, local_rank):
         "exposed_comm_pct": None if exposed is None else round(exposed, 2),
         "roofline": {"bound": "tensor", "kernel": "fa4cp attn_fwd (tcgen05)",
                      "achieved": None if achieved is None else round(achieved, 1),
-                     "peak": peak, "peak_kind": f"{peaks_kind} bf16 dense (burst)",
+                     "peak": peak, "peak_kind": peak_kind,
                      "unit": "TFLOP/s",
                      "frac": None if achieved is None else round(achieved / peak, 4),
                      "launches_per_step": n_attn_local // max(args.steps, 1),
@@ -347,19 +428,20 @@ def gpu_main(args, rank, world, local_rank):
             "sample": "oracle (numpy restatement of the reference's CPU ring simulation) on "
                       "rank 0 of cfg2 at cp=8: all 8 ring steps, 32 heads, T=4096 local "
                       f"tokens; {flops_cpu:.3e} FLOP in {secs_cpu:.1f} s"}
-    traffic = _traffic_from_profile(world)
+    traffic = _traffic_from_profile(args.config, world)
     if traffic is not None:
         line["roofline"]["traffic"] = traffic
     return line
 
 
-def _traffic_from_profile(world):
-    """DRAM bytes per attention launch from the committed ncu summary, if present."""
+def _traffic_from_profile(config, world):
+    """DRAM bytes per attention launch recorded from an ncu capture of this workload
+    (profiles/attn_fwd_traffic.json), or None when none was captured."""
     path = os.path.join(ROOT, "profiles", "attn_fwd_traffic.json")
     try:
         with open(path) as f:
             t = json.load(f)
-        return t.get(f"cp{world}")
+        return t.get(f"{config}_cp{world}")
     except (OSError, ValueError):
         return None
 
@@ -400,8 +482,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--merge", choices=["incremental", "batched"], default="incremental")
-    ap.add_argument("--seq-len", type=int, default=CFG2["N"],
-                    help="total tokens (the cfg2 workload is 32768; smaller only for profiling)")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="cfg2",
+                    help="BASELINE workload (cfg2 is the headline metric's configuration)")
+    ap.add_argument("--seq-len", type=int, default=None,
+                    help="override the single-sequence length (smaller only for profiling)")
     ap.add_argument("--quick", action="store_true",
                     help="profiling run: timed loop only (no e2e, no CPU baseline)")
     args = ap.parse_args()

@@ -86,6 +86,34 @@ struct Geometry {
   int q_start, q_len, k_start, k_len;
 };
 
+// CTA order (blockIdx.x, one sequence per blockIdx.z): q-tiles are taken in chunks of
+// kQtileChunk, heaviest (latest, under causal masking) chunk first; inside a chunk all
+// CTAs of one kv head run before the next kv head's, q-tile major, q head minor.  The
+// CTAs resident at any time then read the K/V of only a few kv heads, which stay in L2
+// instead of every kv head's K/V streaming through it.
+constexpr int kQtileChunk = 16;
+
+__device__ __forceinline__ bool cta_tile(const Params& p, int& head, int& qtile) {
+  const int ch = min(kQtileChunk, p.n_qtiles);
+  const int per_chunk = p.Hkv * ch * p.group;
+  const int L = int(blockIdx.x);
+  const int chunk = L / per_chunk;
+  const int r = L - chunk * per_chunk;
+  const int kvh = r / (ch * p.group);
+  const int r2 = r - kvh * (ch * p.group);
+  const int qt_desc = chunk * ch + r2 / p.group;
+  if (qt_desc >= p.n_qtiles) return false;  // padding of the last chunk
+  head = kvh * p.group + (r2 % p.group);
+  qtile = p.n_qtiles - 1 - qt_desc;
+  return true;
+}
+
+inline unsigned cta_grid_x(int n_qtiles, int Hq) {
+  const int ch = n_qtiles < kQtileChunk ? n_qtiles : kQtileChunk;
+  const int chunks = (n_qtiles + ch - 1) / ch;
+  return unsigned(chunks * ch * Hq);
+}
+
 __device__ __forceinline__ Geometry seq_geometry(const Params& p, int seq) {
   Geometry g;
   const int a = p.cu_q[seq], b = p.cu_q[seq + 1];
@@ -114,8 +142,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int head = blockIdx.x;
-  const int qtile = p.n_qtiles - 1 - int(blockIdx.y);  // heaviest causal tiles first
+  int head, qtile;
+  if (!cta_tile(p, head, qtile)) return;  // uniform for the whole CTA
   const int seq = blockIdx.z;
 
   const Geometry g = seq_geometry(p, seq);
@@ -546,8 +574,8 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int head = blockIdx.x;
-  const int qtile = p.n_qtiles - 1 - int(blockIdx.y);  // heaviest causal tiles first
+  int head, qtile;
+  if (!cta_tile(p, head, qtile)) return;  // uniform for the whole CTA
   const int seq = blockIdx.z;
 
   const Geometry g = seq_geometry(p, seq);
@@ -1041,8 +1069,9 @@ int launch(const void* q, const void* k, const void* v, int64_t total_q, int64_t
   Params p = p0;
   p.n_qtiles = (max_seqlen_q + BM - 1) / BM;
   if (p.n_qtiles <= 0) return FA4CP_OK;
-  FA4CP_CHECK_ARG(p.n_qtiles <= 65535 && p.nseq <= 65535, "grid too large");
-  dim3 grid(unsigned(p.Hq), unsigned(p.n_qtiles), unsigned(p.nseq));
+  FA4CP_CHECK_ARG(int64_t(p.n_qtiles + kQtileChunk) * p.Hq < (int64_t(1) << 31) && p.nseq <= 65535,
+                  "grid too large");
+  dim3 grid(cta_grid_x(p.n_qtiles, p.Hq), 1u, unsigned(p.nseq));
   attn_fwd_kernel<TR><<<grid, kThreads, TR::SMEM_BYTES, stream>>>(mq, mk, mv, p);
   return check_launch("attn_fwd");
 }
@@ -1070,8 +1099,9 @@ int launch2(const void* q, const void* k, const void* v, int64_t total_q, int64_
   Params p = p0;
   p.n_qtiles = (max_seqlen_q + 2 * BM - 1) / (2 * BM);
   if (p.n_qtiles <= 0) return FA4CP_OK;
-  FA4CP_CHECK_ARG(p.n_qtiles <= 65535 && p.nseq <= 65535, "grid too large");
-  dim3 grid(unsigned(p.Hq), unsigned(p.n_qtiles), unsigned(p.nseq));
+  FA4CP_CHECK_ARG(int64_t(p.n_qtiles + kQtileChunk) * p.Hq < (int64_t(1) << 31) && p.nseq <= 65535,
+                  "grid too large");
+  dim3 grid(cta_grid_x(p.n_qtiles, p.Hq), 1u, unsigned(p.nseq));
   attn_fwd_2q_kernel<TR><<<grid, TR::THREADS, TR::SMEM_BYTES, stream>>>(mq, mk, mv, p);
   return check_launch("attn_fwd_2q");
 }
