@@ -273,11 +273,14 @@ def gpu_main(args, rank, world, local_rank):
     barrier()
     torch.cuda.synchronize()
     n_launch0 = _lib.launch_count
+    host_s = 0.0
     with ClockSampler(local_rank) as clk:
         for i in range(args.steps):
             flush.zero_()
             ev[i][0].record()
+            h0 = time.perf_counter()
             run()
+            host_s += time.perf_counter() - h0
             ev[i][1].record()
         torch.cuda.synchronize()
         barrier()
@@ -417,6 +420,7 @@ def gpu_main(args, rank, world, local_rank):
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": round(e2e_ms, 3)},
         "gpu_launches": gpu_launches,
+        "host_issue_ms_per_step": round(host_s * 1e3 / args.steps, 3),
         "clocks": clocks,
         "device_status": int(status_max),
     }
@@ -486,6 +490,8 @@ def main():
                     help="BASELINE workload (cfg2 is the headline metric's configuration)")
     ap.add_argument("--seq-len", type=int, default=None,
                     help="override the single-sequence length (smaller only for profiling)")
+    ap.add_argument("--nccl-cta-policy", choices=["default", "zero"], default="default",
+                    help="NCCL CTA policy of the ring's process group (zero: no SM CTAs)")
     ap.add_argument("--quick", action="store_true",
                     help="profiling run: timed loop only (no e2e, no CPU baseline)")
     args = ap.parse_args()
@@ -502,8 +508,10 @@ def main():
 
     torch.cuda.set_device(local_rank)
     if world > 1:
+        from fa4_ring.comm import nccl_pg_options
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=torch.device("cuda", local_rank))
+                                device_id=torch.device("cuda", local_rank),
+                                pg_options=nccl_pg_options(args.nccl_cta_policy))
     try:
         line = gpu_main(args, rank, world, local_rank)
     finally:

@@ -48,6 +48,7 @@ struct Params {
   int in_fmt;    // kind::f16 operand format: 0 f16, 1 bf16 (unused for e4m3)
   int out_bf16;  // 1 -> bf16 output, 0 -> f16 output
   float scale_log2;
+  int n_tiles;  // persistent kernel: tiles of the whole schedule (tile_work decodes them)
   // self-test only (fa4cp_selftest_wait_expiry): index of the KV tile whose K copy the
   // producer never issues, so the consumer's bounded wait must expire; -1 otherwise
   int debug_withhold_kv;
@@ -504,7 +505,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 //   warp  8    TMA producer                      warp  9    TMEM allocator + MMA issuer
 //   warps 10-11 idle (complete the producer warpgroup for the register re-split)
 // Registers: launched at 168/thread (384 x 168 = 64512); the producer warpgroup drops to
-// 72 and each softmax warpgroup rises to 216: 128 x (216 + 216 + 72) = 64512.
+// 72 (104 when persistent) and each softmax warpgroup rises to 216 (200):
+// 128 x (216 + 216 + 72) = 128 x (200 + 200 + 104) = 64512.
 // TMEM: S0 | S1 (BN fp32 columns each) | O0 | O1 (D columns each).  One S buffer per
 // tile: S_t(j+1) is issued after PV_t(j), so the completion of S_t(j+1) also proves
 // PV_t(j) finished -- a softmax warpgroup may rescale O_t right after its s_full wait.
@@ -540,13 +542,18 @@ struct Traits2 {
   static constexpr int OFF_V = OFF_K + STAGES * KV_BYTES;
   static constexpr int OFF_BAR = OFF_V + STAGES * KV_BYTES;
   // q_full, k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], o_done[2], teardown,
-  // p_full[2][P_SPLIT]
-  static constexpr int NUM_BARS = 1 + 4 * STAGES + 2 + 2 + 1 + 2 * FA4CP_P_SPLIT;
+  // q_empty, o_free[2], p_full[2][P_SPLIT]
+  static constexpr int NUM_BARS = 1 + 4 * STAGES + 2 + 2 + 1 + 1 + 2 + 2 * FA4CP_P_SPLIT;
   static constexpr int SMEM_BYTES = OFF_BAR + NUM_BARS * 8 + 16 + 1024;
   static constexpr int TM_COLS = 512;
   static constexpr int THREADS = 384;
-  static constexpr int REGS_SOFTMAX = 216;
-  static constexpr int REGS_PRODUCER = 72;
+  // FP8 runs persistently (one CTA per SM walking the tile schedule: its MMAs take half the
+  // time, so per-CTA set-up and epilogue weigh twice as much); f16/bf16 measured faster with
+  // one CTA per tile, where the tile loop has a single trip and its cross-tile state folds
+  // away, leaving the softmax warpgroups 216 registers.
+  static constexpr bool PERSISTENT = FP8;
+  static constexpr int REGS_SOFTMAX = PERSISTENT ? 200 : 216;
+  static constexpr int REGS_PRODUCER = PERSISTENT ? 104 : 72;
   static_assert(128 * (2 * REGS_SOFTMAX + REGS_PRODUCER) <= THREADS * 168,
                 "register re-split exceeds the launch allocation");
   __host__ __device__ static constexpr int tm_s(int t) { return t * BN; }
@@ -556,6 +563,53 @@ struct Traits2 {
   static_assert(BN == 128, "softmax register layout assumes 128 keys per tile");
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 };
+
+// One unit of work of the persistent kernel: 2 x 128 query rows of one (head, sequence).
+struct TileWork {
+  Geometry g;
+  int head, kvh, q0, diag, nmax;
+  int rows_t[2], n_t[2];
+};
+
+// Tile `tile` of the persistent schedule.  Order: chunks of kQtileChunk query-tile pairs,
+// heaviest (latest) chunk first across all sequences; inside a chunk, sequence, then kv
+// head, then query-tile pair, then query head of the GQA group -- so the tiles in flight
+// at any time touch the K/V of few kv heads (which then stay in L2) and heavy causal tiles
+// are scheduled before light ones.  Returns false for padding / past-the-end tiles.
+__device__ __forceinline__ bool tile_work(const Params& p, int tile, int BN, TileWork& w) {
+  const int ch = min(kQtileChunk, p.n_qtiles);
+  const int per_seq = ch * p.Hq;
+  const int per_chunk = per_seq * p.nseq;
+  const int chunk = tile / per_chunk;
+  int r = tile - chunk * per_chunk;
+  const int seq = r / per_seq;
+  r -= seq * per_seq;
+  const int kvh = r / (ch * p.group);
+  const int r2 = r - kvh * (ch * p.group);
+  const int qt_desc = chunk * ch + r2 / p.group;
+  if (qt_desc >= p.n_qtiles) return false;
+  w.head = kvh * p.group + r2 % p.group;
+  w.kvh = kvh;
+  w.g = seq_geometry(p, seq);
+  w.q0 = (p.n_qtiles - 1 - qt_desc) * 2 * BM;
+  if (w.q0 >= w.g.q_len) return false;
+  w.diag = w.g.k_len - w.g.q_len;
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    const int first = w.q0 + t * BM;
+    w.rows_t[t] = max(0, min(BM, w.g.q_len - first));
+    int kv_end = w.g.k_len;
+    if (p.causal) kv_end = min(w.g.k_len, first + w.rows_t[t] + w.diag);
+    w.n_t[t] = (w.rows_t[t] > 0 && kv_end > 0) ? (kv_end + BN - 1) / BN : 0;
+  }
+  w.nmax = max(w.n_t[0], w.n_t[1]);
+  return true;
+}
+
+inline int persistent_tiles(int n_qtiles, int Hq, int nseq) {
+  const int ch = n_qtiles < kQtileChunk ? n_qtiles : kQtileChunk;
+  return (n_qtiles + ch - 1) / ch * ch * Hq * nseq;
+}
 
 // exp2 of one element pair: the pair index decides, at compile time, which pipe does it
 template <class TR>
@@ -574,25 +628,6 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  int head, qtile;
-  if (!cta_tile(p, head, qtile)) return;  // uniform for the whole CTA
-  const int seq = blockIdx.z;
-
-  const Geometry g = seq_geometry(p, seq);
-  const int q0 = qtile * 2 * BM;
-  if (q0 >= g.q_len) return;  // uniform for the whole CTA, before any setup
-  const int diag = g.k_len - g.q_len;
-  int rows_t[2], n_t[2];
-#pragma unroll
-  for (int t = 0; t < 2; ++t) {
-    const int first = q0 + t * BM;
-    rows_t[t] = max(0, min(BM, g.q_len - first));
-    int kv_end = g.k_len;
-    if (p.causal) kv_end = min(g.k_len, first + rows_t[t] + diag);
-    n_t[t] = (rows_t[t] > 0 && kv_end > 0) ? (kv_end + BN - 1) / BN : 0;
-  }
-  const int nmax = max(n_t[0], n_t[1]);
-  const int kvh = head / p.group;
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TR::OFF_BAR);
   const uint32_t bar0 = smem_u32(bars);
@@ -605,13 +640,16 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
   auto s_full = [&](int t) { return BAR(1 + 4 * ST + t); };
   auto o_done = [&](int t) { return BAR(3 + 4 * ST + t); };
   const uint32_t td_bar = BAR(5 + 4 * ST);
-  auto p_full = [&](int t, int h) { return BAR(6 + 4 * ST + t * TR::P_SPLIT + h); };
+  const uint32_t q_empty = BAR(6 + 4 * ST);
+  auto o_free = [&](int t) { return BAR(7 + 4 * ST + t); };
+  auto p_full = [&](int t, int h) { return BAR(9 + 4 * ST + t * TR::P_SPLIT + h); };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + TR::NUM_BARS);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* status = &g_attn_status;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
     for (int s = 0; s < ST; ++s) {
       mbar_init(k_full(s), 1);
       mbar_init(k_empty(s), 1);
@@ -622,6 +660,7 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
       mbar_init(s_full(t), 1);
       for (int h = 0; h < TR::P_SPLIT; ++h) mbar_init(p_full(t, h), 128);
       mbar_init(o_done(t), 1);
+      mbar_init(o_free(t), 128);
     }
     mbar_init(td_bar, 1);
     *abort = 0;
@@ -640,6 +679,14 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  const int n_tiles = p.n_tiles;
+  // static boustrophedon schedule: round k takes tiles [k*G, (k+1)*G), forward on even
+  // rounds and backward on odd ones, so with heaviest-first tiles every CTA pairs heavy
+  // and light tiles (the same sequence for all roles of the CTA)
+  const int G = int(gridDim.x);
+  auto snake_tile = [&](int k) -> int {
+    return k * G + ((k & 1) ? G - 1 - int(blockIdx.x) : int(blockIdx.x));
+  };
 
   if (warp >= 8) {
    setmaxnreg_dec<TR::REGS_PRODUCER>();
@@ -649,41 +696,48 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
       const uint64_t pol_kv = policy_evict_last();
       int last_k[ST], last_v[ST];
       for (int s = 0; s < ST; ++s) last_k[s] = last_v[s] = -1;
-      mbar_arrive_expect_tx(q_full, 2 * TR::Q_TILE_BYTES);
+      int kv_it = 0, tile_it = 0;
+      bool ok = true;
+      for (int it_tile = 0, tile = snake_tile(0); (TR::PERSISTENT || it_tile == 0) && ok && tile < n_tiles; tile = snake_tile(++it_tile)) {
+        TileWork w;
+        if (!tile_work(p, tile, BN, w)) continue;
+        // the Q buffers are free once every S MMA of the previous tile has completed
+        if (tile_it > 0 && !mbar_wait(q_empty, (tile_it - 1) & 1, abort, kErrQ, status)) break;
+        mbar_arrive_expect_tx(q_full, 2 * TR::Q_TILE_BYTES);
 #pragma unroll
-      for (int t = 0; t < 2; ++t)
-#pragma unroll
-        for (int c = 0; c < TR::NCH; ++c)
-          tma_load_3d(smem_u32(smem + TR::OFF_Q + t * TR::Q_TILE_BYTES + c * TR::Q_CHUNK_BYTES),
-                      &tmQ, c * TR::CHUNK, head, g.q_start + q0 + t * BM, q_full);
-      for (int j = 0; j < nmax; ++j) {
-        const int s = j % ST, ph = (j / ST) & 1;
-        const int row = g.k_start + j * BN;
-        if (j >= ST && !mbar_wait(k_empty(s), ph ^ 1, abort, kErrKEmpty, status)) break;
-        if (j != p.debug_withhold_kv) {
-          mbar_arrive_expect_tx(k_full(s), TR::KV_BYTES);
+        for (int t = 0; t < 2; ++t)
 #pragma unroll
           for (int c = 0; c < TR::NCH; ++c)
-            tma_load_3d_hint(smem_u32(smem + TR::OFF_K + s * TR::KV_BYTES + c * TR::KV_CHUNK_BYTES),
-                             &tmK, c * TR::CHUNK, kvh, row, k_full(s), pol_kv);
-          last_k[s] = j;
-        }
-        if (j >= ST && !mbar_wait(v_empty(s), ph ^ 1, abort, kErrVEmpty, status)) break;
-        mbar_arrive_expect_tx(v_full(s), TR::KV_BYTES);
+            tma_load_3d(smem_u32(smem + TR::OFF_Q + t * TR::Q_TILE_BYTES + c * TR::Q_CHUNK_BYTES),
+                        &tmQ, c * TR::CHUNK, w.head, w.g.q_start + w.q0 + t * BM, q_full);
+        for (int j = 0; j < w.nmax; ++j, ++kv_it) {
+          const int s = kv_it % ST, ph = (kv_it / ST) & 1;
+          const int row = w.g.k_start + j * BN;
+          if (kv_it >= ST && !mbar_wait(k_empty(s), ph ^ 1, abort, kErrKEmpty, status)) { ok = false; break; }
+          if (kv_it != p.debug_withhold_kv) {
+            mbar_arrive_expect_tx(k_full(s), TR::KV_BYTES);
 #pragma unroll
-        for (int c = 0; c < TR::NCH; ++c)
-          tma_load_3d_hint(smem_u32(smem + TR::OFF_V + s * TR::KV_BYTES + c * TR::KV_CHUNK_BYTES),
-                           &tmV, c * TR::CHUNK, kvh, row, v_full(s), pol_kv);
-        last_v[s] = j;
-      }
-      {
-        // every copy this thread issued has landed before it leaves its role (on the
-        // normal path the consumers already waited for them, so this returns at once)
-        mbar_wait_drain(q_full, 0, kErrDrain, status);
-        for (int s = 0; s < ST; ++s) {
-          if (last_k[s] >= 0) mbar_wait_drain(k_full(s), (last_k[s] / ST) & 1, kErrDrain, status);
-          if (last_v[s] >= 0) mbar_wait_drain(v_full(s), (last_v[s] / ST) & 1, kErrDrain, status);
+            for (int c = 0; c < TR::NCH; ++c)
+              tma_load_3d_hint(smem_u32(smem + TR::OFF_K + s * TR::KV_BYTES + c * TR::KV_CHUNK_BYTES),
+                               &tmK, c * TR::CHUNK, w.kvh, row, k_full(s), pol_kv);
+            last_k[s] = kv_it;
+          }
+          if (kv_it >= ST && !mbar_wait(v_empty(s), ph ^ 1, abort, kErrVEmpty, status)) { ok = false; break; }
+          mbar_arrive_expect_tx(v_full(s), TR::KV_BYTES);
+#pragma unroll
+          for (int c = 0; c < TR::NCH; ++c)
+            tma_load_3d_hint(smem_u32(smem + TR::OFF_V + s * TR::KV_BYTES + c * TR::KV_CHUNK_BYTES),
+                             &tmV, c * TR::CHUNK, w.kvh, row, v_full(s), pol_kv);
+          last_v[s] = kv_it;
         }
+        ++tile_it;
+      }
+      // every copy this thread issued has landed before it leaves its role (on the
+      // normal path the consumers already waited for them, so this returns at once)
+      if (tile_it > 0) mbar_wait_drain(q_full, (tile_it - 1) & 1, kErrDrain, status);
+      for (int s = 0; s < ST; ++s) {
+        if (last_k[s] >= 0) mbar_wait_drain(k_full(s), (last_k[s] / ST) & 1, kErrDrain, status);
+        if (last_v[s] >= 0) mbar_wait_drain(v_full(s), (last_v[s] / ST) & 1, kErrDrain, status);
       }
     }
    } else if (warp == 9) {
@@ -692,9 +746,9 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
       const int fmt = TR::FP8 ? 0 : p.in_fmt;
       const uint32_t idesc_qk = make_idesc(BM, BN, fmt, fmt, 0, 0);
       const uint32_t idesc_pv = make_idesc(BM, D, fmt, fmt, 0, 1);
-      auto issue_s = [&](int t, int j) {
+      auto issue_s = [&](int t, int stage) {
         const uint32_t sQ = smem_u32(smem + TR::OFF_Q + t * TR::Q_TILE_BYTES);
-        const uint32_t sK = smem_u32(smem + TR::OFF_K + (j % ST) * TR::KV_BYTES);
+        const uint32_t sK = smem_u32(smem + TR::OFF_K + stage * TR::KV_BYTES);
 #pragma unroll
         for (int kk = 0; kk < D / TR::MMA_K; ++kk) {
           const int off = kk * 32;  // bytes along D of this K-step
@@ -710,65 +764,87 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
         tc_commit(s_full(t));
       };
       // PV of one key slice (the caller has waited for that slice of P)
-      auto issue_pv_slice = [&](int t, int j, int h) {
-        const uint32_t sV = smem_u32(smem + TR::OFF_V + (j % ST) * TR::KV_BYTES);
+      auto issue_pv_slice = [&](int t, int stage, bool first, int h) {
+        const uint32_t sV = smem_u32(smem + TR::OFF_V + stage * TR::KV_BYTES);
         constexpr int KS = BN / TR::MMA_K / TR::P_SPLIT;  // K-steps per slice
 #pragma unroll
         for (int k2 = 0; k2 < KS; ++k2) {
           const int kk = h * KS + k2;
           const uint64_t bdesc = make_desc_sw128(sV + kk * TR::MMA_K * 128, TR::KV_CHUNK_BYTES, 1024);
           const uint32_t a_tmem = tmem + uint32_t(TR::tm_s(t) + kk * 8);
-          const uint32_t acc = (j > 0 || kk > 0) ? 1u : 0u;
+          const uint32_t acc = (!first || kk > 0) ? 1u : 0u;
           if constexpr (TR::FP8)
             mma_f8_ts(tmem + uint32_t(TR::tm_o(t)), a_tmem, bdesc, idesc_pv, acc);
           else
             mma_f16_ts(tmem + uint32_t(TR::tm_o(t)), a_tmem, bdesc, idesc_pv, acc);
         }
       };
-      bool ok = mbar_wait(q_full, 0, abort, kErrQ, status);
-      if (ok && nmax > 0) {
-        ok = mbar_wait(k_full(0), 0, abort, kErrKFull, status);
+      int kv_it = 0, tile_it = 0;
+      int p_cnt[2] = {0, 0};          // P hand-offs consumed per query tile (p_full phases)
+      int ofree_cnt[2] = {0, 0};      // epilogues that read O_t (o_free phases) ...
+      int ofree_seen[2] = {0, 0};     // ... and how many of them this thread has waited for
+      bool ok = true;
+      for (int it_tile = 0, tile = snake_tile(0); (TR::PERSISTENT || it_tile == 0) && ok && tile < n_tiles; tile = snake_tile(++it_tile)) {
+        TileWork w;
+        if (!tile_work(p, tile, BN, w)) continue;
+        if (!mbar_wait(q_full, tile_it & 1, abort, kErrQ, status)) { ok = false; break; }
         tc_fence_after();
-        if (ok) {
-          if (n_t[0] > 0) issue_s(0, 0);
-          if (n_t[1] > 0) issue_s(1, 0);
-          tc_commit(k_empty(0));
+        if (w.nmax > 0) {
+          const int s0 = kv_it % ST;
+          if (!mbar_wait(k_full(s0), (kv_it / ST) & 1, abort, kErrKFull, status)) { ok = false; break; }
+          tc_fence_after();
+          if (w.n_t[0] > 0) issue_s(0, s0);
+          if (w.n_t[1] > 0) issue_s(1, s0);
+          tc_commit(k_empty(s0));
         }
-      }
-      for (int j = 0; ok && j < nmax; ++j) {
-        const int s = j % ST;
-        bool v_ready = false, k_next_ready = false;
+        for (int j = 0; ok && j < w.nmax; ++j) {
+          const int it = kv_it + j, s = it % ST;
+          bool v_ready = false, k_next_ready = false;
 #pragma unroll
-        for (int t = 0; t < 2; ++t) {
-          if (j >= n_t[t]) continue;
-          if (!v_ready) {
-            if (!mbar_wait(v_full(s), (j / ST) & 1, abort, kErrVFull, status)) { ok = false; break; }
-            v_ready = true;
-          }
+          for (int t = 0; t < 2; ++t) {
+            if (j >= w.n_t[t]) continue;
+            if (j == 0 && ofree_seen[t] < ofree_cnt[t]) {
+              // PV_t(0) overwrites O_t: the previous tile's epilogue must have read it
+              if (!mbar_wait(o_free(t), ofree_seen[t] & 1, abort, kErrODone, status)) { ok = false; break; }
+              ++ofree_seen[t];
+            }
+            if (!v_ready) {
+              if (!mbar_wait(v_full(s), (it / ST) & 1, abort, kErrVFull, status)) { ok = false; break; }
+              v_ready = true;
+            }
 #pragma unroll
-          for (int h = 0; h < TR::P_SPLIT; ++h) {
-            if (!mbar_wait(p_full(t, h), j & 1, abort, kErrPFull, status)) { ok = false; break; }
-            tc_fence_after();
-            issue_pv_slice(t, j, h);
+            for (int h = 0; h < TR::P_SPLIT; ++h) {
+              if (!mbar_wait(p_full(t, h), p_cnt[t] & 1, abort, kErrPFull, status)) { ok = false; break; }
+              tc_fence_after();
+              issue_pv_slice(t, s, j == 0, h);
+            }
+            if (!ok) break;
+            ++p_cnt[t];
+            tc_commit(o_done(t));
+            if (j + 1 < w.n_t[t]) {
+              const int s1 = (it + 1) % ST;
+              if (!k_next_ready) {
+                if (!mbar_wait(k_full(s1), ((it + 1) / ST) & 1, abort, kErrKFull, status)) {
+                  ok = false;
+                  break;
+                }
+                k_next_ready = true;
+                tc_fence_after();
+              }
+              issue_s(t, s1);
+            }
           }
           if (!ok) break;
-          tc_commit(o_done(t));
-          if (j + 1 < n_t[t]) {
-            if (!k_next_ready) {
-              const int s1 = (j + 1) % ST;
-              if (!mbar_wait(k_full(s1), ((j + 1) / ST) & 1, abort, kErrKFull, status)) {
-                ok = false;
-                break;
-              }
-              k_next_ready = true;
-              tc_fence_after();
-            }
-            issue_s(t, j + 1);
-          }
+          tc_commit(v_empty(s));
+          if (k_next_ready) tc_commit(k_empty((it + 1) % ST));
         }
         if (!ok) break;
-        tc_commit(v_empty(s));
-        if (k_next_ready) tc_commit(k_empty((j + 1) % ST));
+        // every S MMA of this tile is issued: its Q buffers are free once they complete
+        tc_commit(q_empty);
+        for (int t = 0; t < 2; ++t)
+          if (w.n_t[t] > 0) ++ofree_cnt[t];
+        kv_it += w.nmax;
+        ++tile_it;
       }
       // every MMA issued above has completed before TMEM is released
       tc_commit(td_bar);
@@ -778,156 +854,168 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
   } else {
     setmaxnreg_inc<TR::REGS_SOFTMAX>();
     // ------------------------------------------------------------ softmax + epilogue
-    const int t = warp >> 2;  // query tile of this warpgroup
+    const int t = warp >> 2;  // query tile slot of this warpgroup
     const int wq = warp & 3;
     const int r = wq * 32 + lane;
     const uint32_t t_lane = tmem + (uint32_t(wq * 32) << 16);
-    const int first = q0 + t * BM;
-    const int key_lim = first + r + diag;
-    const int n = n_t[t];
-    float scale = p.scale_log2;
-    float vscale = 1.0f;
-    if (p.q_descale) scale *= p.q_descale[kvh];
-    if (p.k_descale) scale *= p.k_descale[kvh];
-    if (p.v_descale) vscale = p.v_descale[kvh];
-    const uint64_t scale2 = f2pack(scale, scale);
-    float m = kNegInf, l = 0.f;
+    int s_cnt = 0;   // S_t completions consumed (s_full phases)
+    int pv_cnt = 0;  // PV_t MMAs issued for this slot so far (o_done phases)
     bool aborted = false;
 
-    for (int j = 0; j < n; ++j) {
-      bool ok = mbar_wait(s_full(t), j & 1, abort, kErrSFull, status);
-      if (!__all_sync(0xffffffffu, ok)) { aborted = true; break; }
-      tc_fence_after();
-      uint32_t sr[BN / 32][32];
-#pragma unroll
-      for (int c = 0; c < BN / 32; ++c) tmem_ld32(t_lane + uint32_t(TR::tm_s(t) + c * 32), sr[c]);
-      tmem_wait_ld();
-#pragma unroll
-      for (int c = 0; c < BN / 32; ++c) reg_fence32(sr[c]);
+    for (int it_tile = 0, tile = snake_tile(0); (TR::PERSISTENT || it_tile == 0) && !aborted && tile < n_tiles; tile = snake_tile(++it_tile)) {
+      TileWork w;
+      if (!tile_work(p, tile, BN, w)) continue;
+      if (w.rows_t[t] <= 0) continue;  // this query tile lies past the sequence end
+      const int first = w.q0 + t * BM;
+      const int key_lim = first + r + w.diag;
+      const int n = w.n_t[t];
+      float scale = p.scale_log2;
+      float vscale = 1.0f;
+      if (p.q_descale) scale *= p.q_descale[w.kvh];
+      if (p.k_descale) scale *= p.k_descale[w.kvh];
+      if (p.v_descale) vscale = p.v_descale[w.kvh];
+      const uint64_t scale2 = f2pack(scale, scale);
+      float m = kNegInf, l = 0.f;
 
-      const int kbase = j * BN;
-      const bool need_mask = (kbase + BN > g.k_len) || (p.causal && kbase + BN - 1 > first + diag);
-      if (need_mask) {
+      for (int j = 0; j < n; ++j) {
+        bool ok = mbar_wait(s_full(t), s_cnt & 1, abort, kErrSFull, status);
+        if (!__all_sync(0xffffffffu, ok)) { aborted = true; break; }
+        ++s_cnt;
+        tc_fence_after();
+        uint32_t sr[BN / 32][32];
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c) tmem_ld32(t_lane + uint32_t(TR::tm_s(t) + c * 32), sr[c]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c) reg_fence32(sr[c]);
+
+        const int kbase = j * BN;
+        const bool need_mask =
+            (kbase + BN > w.g.k_len) || (p.causal && kbase + BN - 1 > first + w.diag);
+        if (need_mask) {
+#pragma unroll
+          for (int c = 0; c < BN / 32; ++c)
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              const int key = kbase + c * 32 + e;
+              if (key >= w.g.k_len || (p.causal && key > key_lim)) sr[c][e] = __float_as_uint(kNegInf);
+            }
+        }
+        float mx4[4] = {kNegInf, kNegInf, kNegInf, kNegInf};
 #pragma unroll
         for (int c = 0; c < BN / 32; ++c)
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const int key = kbase + c * 32 + e;
-            if (key >= g.k_len || (p.causal && key > key_lim)) sr[c][e] = __float_as_uint(kNegInf);
-          }
-      }
-      float mx4[4] = {kNegInf, kNegInf, kNegInf, kNegInf};
-#pragma unroll
-      for (int c = 0; c < BN / 32; ++c)
-#pragma unroll
-        for (int e = 0; e < 32; e += 2)
-          mx4[c] = fmax3(mx4[c], __uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1]));
-      const float mx = fmax3(fmaxf(mx4[0], mx4[1]), mx4[2], mx4[3]);
-      const float m_new = fmaxf(m, mx);
-      if (j == 0) {
-        m = m_new;
-      } else {
-        const bool need = (m_new - m) * scale > kRescaleThreshold;
-        if (__any_sync(0xffffffffu, need)) {
-          // PV_t(j-1) is complete: S_t(j) was issued after it and has completed.
-          const float f = need ? ex2_approx((m - m_new) * scale) : 1.0f;
-          if (need) { l *= f; m = m_new; }
-          const uint64_t f2 = f2pack(f, f);
+          for (int e = 0; e < 32; e += 2)
+            mx4[c] = fmax3(mx4[c], __uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1]));
+        const float mx = fmax3(fmaxf(mx4[0], mx4[1]), mx4[2], mx4[3]);
+        const float m_new = fmaxf(m, mx);
+        if (j == 0) {
+          m = m_new;
+        } else {
+          const bool need = (m_new - m) * scale > kRescaleThreshold;
+          if (__any_sync(0xffffffffu, need)) {
+            // PV_t(j-1) is complete: S_t(j) was issued after it and has completed.
+            const float f = need ? ex2_approx((m - m_new) * scale) : 1.0f;
+            if (need) { l *= f; m = m_new; }
+            const uint64_t f2 = f2pack(f, f);
 #pragma unroll 1
-          for (int c = 0; c < D / 32; ++c) {
-            uint32_t o[32];
-            tmem_ld32(t_lane + uint32_t(TR::tm_o(t) + c * 32), o);
-            tmem_wait_ld();
-            reg_fence32(o);
+            for (int c = 0; c < D / 32; ++c) {
+              uint32_t o[32];
+              tmem_ld32(t_lane + uint32_t(TR::tm_o(t) + c * 32), o);
+              tmem_wait_ld();
+              reg_fence32(o);
 #pragma unroll
-            for (int e = 0; e < 32; e += 2) {
-              const uint64_t v = fmul2(f2pack(__uint_as_float(o[e]), __uint_as_float(o[e + 1])), f2);
-              o[e] = __float_as_uint(f2lo(v));
-              o[e + 1] = __float_as_uint(f2hi(v));
+              for (int e = 0; e < 32; e += 2) {
+                const uint64_t v = fmul2(f2pack(__uint_as_float(o[e]), __uint_as_float(o[e + 1])), f2);
+                o[e] = __float_as_uint(f2lo(v));
+                o[e + 1] = __float_as_uint(f2hi(v));
+              }
+              tmem_st32(t_lane + uint32_t(TR::tm_o(t) + c * 32), o);
             }
-            tmem_st32(t_lane + uint32_t(TR::tm_o(t) + c * 32), o);
-          }
-          tmem_wait_st();
-        }
-      }
-      const float neg_m = (m == kNegInf) ? 0.f : -m * scale;
-      const uint64_t negm2 = f2pack(neg_m, neg_m);
-      uint64_t rs2[2] = {0ull, 0ull};
-      if constexpr (TR::FP8) {
-        uint32_t pw[32];
-#pragma unroll
-        for (int c = 0; c < BN / 32; ++c) {
-#pragma unroll
-          for (int e = 0; e < 32; e += 4) {
-            const uint64_t a = ffma2(f2pack(__uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1])), scale2, negm2);
-            const uint64_t b = ffma2(f2pack(__uint_as_float(sr[c][e + 2]), __uint_as_float(sr[c][e + 3])), scale2, negm2);
-            const uint64_t ea = exp2_pair<TR>((c * 32 + e) / 2, a);
-            const uint64_t eb = exp2_pair<TR>((c * 32 + e) / 2 + 1, b);
-            rs2[0] = fadd2(rs2[0], ea);
-            rs2[1] = fadd2(rs2[1], eb);
-            pw[(c * 32 + e) / 4] = pack_e4m3x4(f2lo(ea), f2hi(ea), f2lo(eb), f2hi(eb));
+            tmem_wait_st();
           }
         }
-        tmem_st32(t_lane + uint32_t(TR::tm_s(t)), pw);
-        tmem_wait_st();
-        tc_fence_before();
-#pragma unroll
-        for (int h = 0; h < TR::P_SPLIT; ++h) mbar_arrive(p_full(t, h));
-      } else {
-        // P in 64-key halves: exps of a half are kept (as fp32 bits, in place of S) for
-        // the row sum, which is added up after P has been handed to the MMA warp
-        static_assert(TR::FP8 || BN / 64 == 2, "bf16 path assumes two 64-key halves");
-#pragma unroll
-        for (int half = 0; half < BN / 64; ++half) {
+        const float neg_m = (m == kNegInf) ? 0.f : -m * scale;
+        const uint64_t negm2 = f2pack(neg_m, neg_m);
+        uint64_t rs2[2] = {0ull, 0ull};
+        if constexpr (TR::FP8) {
           uint32_t pw[32];
 #pragma unroll
-          for (int e = 0; e < 64; e += 2) {
-            const int c = half * 2 + (e >> 5), ee = e & 31;
-            const uint64_t a = ffma2(f2pack(__uint_as_float(sr[c][ee]), __uint_as_float(sr[c][ee + 1])), scale2, negm2);
-            const uint64_t ex = exp2_pair<TR>(half * 32 + (e >> 1), a);
-            const float x0 = f2lo(ex), x1 = f2hi(ex);
-            sr[c][ee] = __float_as_uint(x0);
-            sr[c][ee + 1] = __float_as_uint(x1);
-            pw[e >> 1] = p.in_fmt ? pack_bf16x2(x0, x1) : pack_f16x2(x0, x1);
-          }
-          tmem_st32(t_lane + uint32_t(TR::tm_s(t) + half * 32), pw);
-          if (TR::P_SPLIT == 2 || half == BN / 64 - 1) {
-            tmem_wait_st();
-            tc_fence_before();
-            if (TR::P_SPLIT == 2) {
-              mbar_arrive(p_full(t, half));
-            } else {
+          for (int c = 0; c < BN / 32; ++c) {
 #pragma unroll
-              for (int h = 0; h < TR::P_SPLIT; ++h) mbar_arrive(p_full(t, h));
+            for (int e = 0; e < 32; e += 4) {
+              const uint64_t a = ffma2(f2pack(__uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1])), scale2, negm2);
+              const uint64_t b = ffma2(f2pack(__uint_as_float(sr[c][e + 2]), __uint_as_float(sr[c][e + 3])), scale2, negm2);
+              const uint64_t ea = exp2_pair<TR>((c * 32 + e) / 2, a);
+              const uint64_t eb = exp2_pair<TR>((c * 32 + e) / 2 + 1, b);
+              rs2[0] = fadd2(rs2[0], ea);
+              rs2[1] = fadd2(rs2[1], eb);
+              pw[(c * 32 + e) / 4] = pack_e4m3x4(f2lo(ea), f2hi(ea), f2lo(eb), f2hi(eb));
             }
           }
-        }
+          static_assert(!TR::FP8 || BN == 128, "FP8 P store assumes 128 keys (32 columns)");
+          tmem_st32(t_lane + uint32_t(TR::tm_s(t)), pw);
+          tmem_wait_st();
+          tc_fence_before();
 #pragma unroll
-        for (int c = 0; c < BN / 32; ++c)
+          for (int h = 0; h < TR::P_SPLIT; ++h) mbar_arrive(p_full(t, h));
+        } else {
+          // P in 64-key halves: exps of a half are kept (as fp32 bits, in place of S) for
+          // the row sum, which is added up after P has been handed to the MMA warp
+          static_assert(TR::FP8 || BN / 64 == 2, "bf16 path assumes two 64-key halves");
 #pragma unroll
-          for (int e = 0; e < 32; e += 4) {
-            rs2[0] = fadd2(rs2[0], f2pack(__uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1])));
-            rs2[1] = fadd2(rs2[1], f2pack(__uint_as_float(sr[c][e + 2]), __uint_as_float(sr[c][e + 3])));
+          for (int half = 0; half < BN / 64; ++half) {
+            uint32_t pw[32];
+#pragma unroll
+            for (int e = 0; e < 64; e += 2) {
+              const int c = half * 2 + (e >> 5), ee = e & 31;
+              const uint64_t a = ffma2(f2pack(__uint_as_float(sr[c][ee]), __uint_as_float(sr[c][ee + 1])), scale2, negm2);
+              const uint64_t ex = exp2_pair<TR>(half * 32 + (e >> 1), a);
+              const float x0 = f2lo(ex), x1 = f2hi(ex);
+              sr[c][ee] = __float_as_uint(x0);
+              sr[c][ee + 1] = __float_as_uint(x1);
+              pw[e >> 1] = p.in_fmt ? pack_bf16x2(x0, x1) : pack_f16x2(x0, x1);
+            }
+            tmem_st32(t_lane + uint32_t(TR::tm_s(t) + half * 32), pw);
+            if (TR::P_SPLIT == 2 || half == BN / 64 - 1) {
+              tmem_wait_st();
+              tc_fence_before();
+              if (TR::P_SPLIT == 2) {
+                mbar_arrive(p_full(t, half));
+              } else {
+#pragma unroll
+                for (int h = 0; h < TR::P_SPLIT; ++h) mbar_arrive(p_full(t, h));
+              }
+            }
           }
+#pragma unroll
+          for (int c = 0; c < BN / 32; ++c)
+#pragma unroll
+            for (int e = 0; e < 32; e += 4) {
+              rs2[0] = fadd2(rs2[0], f2pack(__uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1])));
+              rs2[1] = fadd2(rs2[1], f2pack(__uint_as_float(sr[c][e + 2]), __uint_as_float(sr[c][e + 3])));
+            }
+        }
+        const uint64_t rs = fadd2(rs2[0], rs2[1]);
+        l += f2lo(rs) + f2hi(rs);
       }
-      const uint64_t rs = fadd2(rs2[0], rs2[1]);
-      l += f2lo(rs) + f2hi(rs);
-    }
+      if (aborted) break;
 
-    // ------------------------------------------------------------ epilogue
-    if (!aborted && n > 0) {
-      bool ok = mbar_wait(o_done(t), (n - 1) & 1, abort, kErrODone, status);
-      if (!__all_sync(0xffffffffu, ok)) aborted = true;
-      tc_fence_after();
-    }
-    if (!aborted && rows_t[t] > 0) {
-      const bool valid = r < rows_t[t];
-      const int64_t grow = int64_t(g.q_start) + first + r;
+      // ---------------------------------------------------------- epilogue of this tile
+      if (n > 0) {
+        // the last PV_t of this tile; PV_t of the next tile waits for o_free below
+        pv_cnt += n;
+        bool ok = mbar_wait(o_done(t), (pv_cnt - 1) & 1, abort, kErrODone, status);
+        if (!__all_sync(0xffffffffu, ok)) { aborted = true; break; }
+        tc_fence_after();
+      }
+      const bool valid = r < w.rows_t[t];
+      const int64_t grow = int64_t(w.g.q_start) + first + r;
       // a row that saw no key has m = -inf (the emulated exp2 maps -inf to ~1e-38, not 0,
       // so l alone cannot tell)
       const bool any_key = (m != kNegInf) && (l > 0.f);
       const float lse_new = any_key ? (m * scale + lg2_approx(l)) * kLn2 : kNegInf;
-      float* lse_ptr = p.lse + grow * p.Hq + head;
+      float* lse_ptr = p.lse + grow * p.Hq + w.head;
       float ca = 0.f, cb = any_key ? vscale / l : 0.f, lse_out = lse_new;
       bool write = valid;
       bool read_acc = false;
@@ -946,7 +1034,7 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
           read_acc = true;
         }
       }
-      uint8_t* orow = static_cast<uint8_t*>(p.out) + (grow * p.Hq + head) * int64_t(D) * 2;
+      uint8_t* orow = static_cast<uint8_t*>(p.out) + (grow * p.Hq + w.head) * int64_t(D) * 2;
       const bool has_o = n > 0;  // warpgroup-uniform
 #pragma unroll 1
       for (int c = 0; c < D / 32; ++c) {
@@ -955,6 +1043,11 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
           tmem_ld32(t_lane + uint32_t(TR::tm_o(t) + c * 32), o);
           tmem_wait_ld();
           reg_fence32(o);
+          if (c == D / 32 - 1) {
+            // all of O_t has been read: the next tile's PV_t may overwrite it
+            tc_fence_before();
+            mbar_arrive(o_free(t));
+          }
         } else {
 #pragma unroll
           for (int e = 0; e < 32; ++e) o[e] = 0u;
@@ -968,15 +1061,15 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
 #pragma unroll
             for (int v4 = 0; v4 < 4; ++v4) {
               const uint4 a = dst[v4];
-              const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+              const uint32_t wd[4] = {a.x, a.y, a.z, a.w};
 #pragma unroll
               for (int i = 0; i < 4; ++i) {
                 float lo, hi;
                 if (p.out_bf16) {
-                  lo = __uint_as_float(w[i] << 16);
-                  hi = __uint_as_float(w[i] & 0xFFFF0000u);
+                  lo = __uint_as_float(wd[i] << 16);
+                  hi = __uint_as_float(wd[i] & 0xFFFF0000u);
                 } else {
-                  const float2 tt = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+                  const float2 tt = __half22float2(*reinterpret_cast<const __half2*>(&wd[i]));
                   lo = tt.x; hi = tt.y;
                 }
                 f[v4 * 8 + 2 * i] = fmaf(lo, ca, f[v4 * 8 + 2 * i]);
@@ -986,12 +1079,12 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
           }
 #pragma unroll
           for (int v4 = 0; v4 < 4; ++v4) {
-            uint32_t w[4];
+            uint32_t wd[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i)
-              w[i] = p.out_bf16 ? pack_bf16x2(f[v4 * 8 + 2 * i], f[v4 * 8 + 2 * i + 1])
-                                : pack_f16x2(f[v4 * 8 + 2 * i], f[v4 * 8 + 2 * i + 1]);
-            dst[v4] = make_uint4(w[0], w[1], w[2], w[3]);
+              wd[i] = p.out_bf16 ? pack_bf16x2(f[v4 * 8 + 2 * i], f[v4 * 8 + 2 * i + 1])
+                                 : pack_f16x2(f[v4 * 8 + 2 * i], f[v4 * 8 + 2 * i + 1]);
+            dst[v4] = make_uint4(wd[0], wd[1], wd[2], wd[3]);
           }
         }
       }
@@ -1099,9 +1192,17 @@ int launch2(const void* q, const void* k, const void* v, int64_t total_q, int64_
   Params p = p0;
   p.n_qtiles = (max_seqlen_q + 2 * BM - 1) / (2 * BM);
   if (p.n_qtiles <= 0) return FA4CP_OK;
-  FA4CP_CHECK_ARG(int64_t(p.n_qtiles + kQtileChunk) * p.Hq < (int64_t(1) << 31) && p.nseq <= 65535,
-                  "grid too large");
-  dim3 grid(cta_grid_x(p.n_qtiles, p.Hq), 1u, unsigned(p.nseq));
+  FA4CP_CHECK_ARG(int64_t(p.n_qtiles + kQtileChunk) * p.Hq * p.nseq < (int64_t(1) << 31),
+                  "too many tiles");
+  p.n_tiles = persistent_tiles(p.n_qtiles, p.Hq, p.nseq);
+  // persistent: one CTA per SM, each walking the tile schedule with a stride of the grid
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0;
+    FA4CP_CHECK_CUDA(cudaGetDevice(&dev));
+    FA4CP_CHECK_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  }
+  const int grid = (TR::PERSISTENT && p.n_tiles > sms) ? sms : p.n_tiles;
   attn_fwd_2q_kernel<TR><<<grid, TR::THREADS, TR::SMEM_BYTES, stream>>>(mq, mk, mv, p);
   return check_launch("attn_fwd_2q");
 }

@@ -39,6 +39,26 @@ def comm_stream(device: torch.device) -> torch.cuda.Stream:
     return st
 
 
+def nccl_pg_options(cta_policy: str = "default"):
+    """Options for the NCCL process group the ring runs on: high-priority NCCL streams.
+
+    The attention kernel fills every SM (one CTA holds an SM's whole register file), so
+    the KV hop's NCCL kernel only gets SMs as attention CTAs retire; on a high-priority
+    stream its CTAs are placed ahead of the queued attention CTAs, so the transfer overlaps
+    the step instead of waiting for the end of the attention grid.  Use as
+    ``dist.init_process_group("nccl", pg_options=nccl_pg_options(), ...)`` or for the
+    ``group`` passed to ``ring_flash_attn``.
+    """
+    opts = dist.ProcessGroupNCCL.Options()
+    opts.is_high_priority_stream = True
+    if cta_policy == "zero":
+        # NCCL 2.28+: communicate without SM CTAs where NCCL supports it (copy engines)
+        opts.config.cta_policy = dist.ProcessGroupNCCL.NCCL_CTA_POLICY_ZERO
+    elif cta_policy != "default":
+        raise ValueError(f"unknown cta_policy {cta_policy!r}")
+    return opts
+
+
 def _global_rank(group, r: int) -> int:
     if group is None:
         return r

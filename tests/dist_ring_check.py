@@ -23,7 +23,9 @@ def main():
     rank = int(os.environ["RANK"])
     world = int(os.environ["WORLD_SIZE"])
     torch.cuda.set_device(int(os.environ["LOCAL_RANK"]))
-    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    from fa4_ring.comm import nccl_pg_options
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                            pg_options=nccl_pg_options())
     dev = torch.device("cuda")
     ok = True
     try:

@@ -206,3 +206,33 @@ def test_quantize_and_dequantize_e4m3():
     z8, zs = quantize_e4m3(torch.zeros(64, device="cuda", dtype=torch.bfloat16))
     assert float(zs) == 1.0 and torch.all(z8.float() == 0)
     assert_device_ok()
+
+
+PERSISTENT_CASES = [
+    # more tiles than SMs: every CTA of the persistent kernel walks several tiles
+    ([4096], [4096], 40, 8, 128, True, torch.bfloat16),
+    ([2048], [2048], 64, 8, 64, False, torch.float16),
+    # ragged packed batch with empty sequences: padding tiles interleaved in the schedule
+    ([300, 0, 2000, 17, 1024, 129], [300, 0, 2000, 17, 1024, 129], 32, 4, 128, True,
+     torch.bfloat16),
+]
+
+
+@pytest.mark.parametrize("case", PERSISTENT_CASES, ids=[str(i) for i in range(len(PERSISTENT_CASES))])
+def test_attn_persistent_many_tiles_per_cta(case):
+    _run_case(*case)
+
+
+def test_attn_fp8_many_tiles_per_cta():
+    from fa4_ring.attn_backend import b200_attn
+    g = torch.Generator().manual_seed(12)
+    T, H, Hkv, D = 2048, 48, 8, 128
+    q32, k32, v32 = (torch.randn(T, h, D, generator=g) for h in (H, Hkv, Hkv))
+    (q8, qs), (k8, ks), (v8, vs) = quant_e4m3(q32), quant_e4m3(k32), quant_e4m3(v32)
+    scale = 1.0 / math.sqrt(D)
+    out, lse = b200_attn(q8.cuda(), k8.cuda(), v8.cuda(), causal=True, softmax_scale=scale,
+                         q_descale=qs.cuda(), k_descale=ks.cuda(), v_descale=vs.cuda())
+    wo, wl = orc.attn(dequant(q8, qs), dequant(k8, ks), dequant(v8, vs), True, scale)
+    np.testing.assert_allclose(to_np(out), wo, atol=OUT_TOL[torch.float8_e4m3fn], rtol=0)
+    np.testing.assert_allclose(to_np(lse), wl, atol=1e-2, rtol=0)
+    assert_device_ok()
