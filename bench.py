@@ -205,8 +205,8 @@ def cpu_sample(rank_steps=None, threads=None):
 # --------------------------------------------------------------------------- GPU arm
 def gpu_main(args, rank, world, local_rank):
     from fa4_ring import RingConfig, ring_flash_attn, zigzag_shard
-    from fa4_ring import _lib, attn_backend
-    from fa4_ring.ring_attention import ring_forward, _single_cu
+    from fa4_ring import _lib, attn_backend, ring_attention
+    from fa4_ring.comm import native_ring
 
     from fa4_ring import Descales
     from fa4_ring.fp8 import allgather_descales, quantize_e4m3
@@ -269,7 +269,11 @@ def gpu_main(args, rank, world, local_rank):
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
           for _ in range(args.steps)]
     launches = []
-    attn_backend.launch_timer = launches
+    attn_backend.launch_timer = launches  # attention launches issued from Python
+    nring = None
+    if world > 1 and ring_attention.use_native_executor() and args.merge == "incremental":
+        nring = native_ring(rank, cp, dev)  # created during warm-up; times its own launches
+        nring.start_timing(args.steps * cp)
     barrier()
     torch.cuda.synchronize()
     n_launch0 = _lib.launch_count
@@ -288,37 +292,20 @@ def gpu_main(args, rank, world, local_rank):
     gpu_launches = _lib.launch_count - n_launch0
     clocks = clk.summary()
     ms_local = sum(a.elapsed_time(b) for a, b in ev)
-    attn_ms_local = sum(a.elapsed_time(b) for a, b, _ in launches)
-    n_attn_local = len(launches)
-    status = _lib.device_status()
-
-    # ---- exposed communication: same schedule with the transfers skipped
-    exposed = None
-    if world > 1 and not args.quick:
-        cu = lcu if varlen else _single_cu(lq.shape[0], dev)
-
-        def run_nocomm():
-            return ring_forward(lq, lambda s: (lk, lv), lambda s: None, cfg, cu=cu,
-                                nseq=cu.numel() - 1, max_seqlen=max_local, descales=desc)
-        for _ in range(2):
-            run_nocomm()
-        torch.cuda.synchronize()
-        ev2 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-               for _ in range(args.steps)]
-        barrier()
-        for i in range(args.steps):
-            flush.zero_()
-            ev2[i][0].record()
-            run_nocomm()
-            ev2[i][1].record()
-        torch.cuda.synchronize()
-        barrier()
-        ms_nocomm_local = sum(a.elapsed_time(b) for a, b in ev2)
+    if nring is not None:
+        attn_ms_local, n_attn_local = nring.read_timing()
+        nring.start_timing(0)
     else:
-        ms_nocomm_local = ms_local
+        attn_ms_local = sum(a.elapsed_time(b) for a, b, _ in launches)
+        n_attn_local = len(launches)
+    status = _lib.device_status()
+    # exposed communication: the share of the step in which no attention kernel ran
+    # (K/V hops not hidden under attention, plus launch gaps), this rank; max over ranks
+    exposed_local = max(0.0, (ms_local - attn_ms_local) / ms_local * 100.0) if world > 1 else 0.0
 
     if args.quick:  # profiling runs: timed loop only
-        vals = torch.tensor([ms_local, attn_ms_local], dtype=torch.float64, device=dev)
+        vals = torch.tensor([ms_local, attn_ms_local, exposed_local], dtype=torch.float64,
+                            device=dev)
         if world > 1:
             dist.all_reduce(vals, op=dist.ReduceOp.MAX)
         if rank == 0:
@@ -327,6 +314,8 @@ def gpu_main(args, rank, world, local_rank):
                     "ms_per_step": round(ms_step, 4),
                     "value": round(step_flops / (ms_step * 1e-3) / 1e12, 2),
                     "attn_ms": round(vals[1].item() / args.steps, 4), "gpu_launches": gpu_launches,
+                    "exposed_comm_pct": round(vals[2].item(), 2),
+                    "host_issue_ms_per_step": round(host_s * 1e3 / args.steps, 3),
                     "device_status": status}
         return None
 
@@ -363,13 +352,11 @@ def gpu_main(args, rank, world, local_rank):
     d2h = hout.numel() * hout.element_size()
 
     # ---- reduce over ranks (max)
-    vals = torch.tensor([ms_local, attn_ms_local, e2e_ms_local, ms_nocomm_local, float(status)],
+    vals = torch.tensor([ms_local, attn_ms_local, e2e_ms_local, exposed_local, float(status)],
                         dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
-    ms_total, attn_ms, e2e_ms, ms_nocomm, status_max = vals.tolist()
-    if world > 1 and ms_total > 0:
-        exposed = max(0.0, (ms_total - ms_nocomm) / ms_total * 100.0)
+    ms_total, attn_ms, e2e_ms, exposed, status_max = vals.tolist()
 
     if rank != 0:
         return None
@@ -408,7 +395,10 @@ def gpu_main(args, rank, world, local_rank):
                    "l2": "flushed before every timed step (256 MiB write, untimed)"},
         "per_gpu_tflops": round(value / world, 2),
         "pct_tensor_peak": round(value / world / peak * 100.0, 2),
-        "exposed_comm_pct": None if exposed is None else round(exposed, 2),
+        "exposed_comm_pct": round(exposed, 2) if world > 1 else None,
+        "exposed_comm_def": "100 * (step time - summed attention-kernel time) / step time, "
+                            "max over ranks",
+        "executor": "native (fa4cp_ring_attn_fwd)" if nring is not None else "python step loop",
         "roofline": {"bound": "tensor", "kernel": "fa4cp attn_fwd (tcgen05)",
                      "achieved": None if achieved is None else round(achieved, 1),
                      "peak": peak, "peak_kind": peak_kind,
@@ -516,6 +506,8 @@ def main():
         line = gpu_main(args, rank, world, local_rank)
     finally:
         if world > 1:
+            from fa4_ring.comm import close_native_rings
+            close_native_rings()
             dist.destroy_process_group()
     if line is not None:
         print(json.dumps(line), flush=True)

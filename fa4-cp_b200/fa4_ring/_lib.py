@@ -64,6 +64,13 @@ _SIGNATURES = {
     "fa4cp_zigzag_unshard": [ctypes.POINTER(_vp), _vp, _vp, _i32, _i64, _i32, _i64, _vp],
     "fa4cp_half_index": [_vp, _i32, _i64, _i32, _vp, _vp],
     "fa4cp_local_cu": [_vp, _i32, _i32, _vp, _vp],
+    "fa4cp_ring_unique_id": [_vp],
+    "fa4cp_ring_comm_init": [_vp, _i32, _i32, ctypes.POINTER(_i64)],
+    "fa4cp_ring_comm_destroy": [_i64],
+    "fa4cp_ring_timing": [_i64, _i32],
+    "fa4cp_ring_timing_read": [_i64, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(_i32)],
+    "fa4cp_ring_attn_fwd": [_i64, _vp, _vp, _vp, _vp, _i64, _vp, _vp, _vp, _i32, _i32, _i64, _i32,
+                            _i32, _i32, _i32, _i32, _f32, _vp, _vp, _vp, _vp, _i64, _vp],
 }
 _RESTYPE = {"fa4cp_last_error": ctypes.c_char_p, "fa4cp_attn_kv8_workspace_bytes": _i64}
 

@@ -137,3 +137,101 @@ class KVRing:
             ev = torch.cuda.Event()
             ev.record(torch.cuda.current_stream(self.kv[0][0].device))
             self.consumed[s] = ev
+
+
+class NativeRing:
+    """The library's native ring executor (``fa4cp_ring_*``) for one cp group on one GPU.
+
+    It owns an NCCL communicator over the cp group (NCCL rank = cp rank), created
+    collectively on first use from a unique id that cp rank 0 makes and broadcasts over
+    ``group``, plus a high-priority comm stream and CUDA events.  One
+    :meth:`forward` call issues a rank's whole ring forward (all hops and all attention
+    steps) from C++, so the per-step cost on the host is a few CUDA API calls instead of a
+    Python loop over ``torch.distributed`` P2P ops.  Call :func:`close_native_rings` on
+    every rank before ``destroy_process_group``.
+    """
+
+    def __init__(self, cp_rank: int, cp_size: int, device: torch.device,
+                 group: Optional["dist.ProcessGroup"] = None):
+        import ctypes
+
+        from . import _lib
+
+        self.lib = _lib.load()
+        self.rank, self.size, self.device = cp_rank, cp_size, device
+        uid = (ctypes.c_uint8 * 128)()
+        if cp_rank == 0:
+            _lib.check(self.lib.fa4cp_ring_unique_id(uid), "ring_unique_id")
+        on_gpu = dist.get_backend(group) == "nccl"
+        t = torch.tensor(list(uid), dtype=torch.uint8,
+                         device=device if on_gpu else torch.device("cpu"))
+        dist.broadcast(t, src=_global_rank(group, 0), group=group)
+        uid = (ctypes.c_uint8 * 128)(*t.cpu().tolist())
+        h = ctypes.c_int64(0)
+        with torch.cuda.device(device):
+            _lib.check(self.lib.fa4cp_ring_comm_init(uid, cp_size, cp_rank, ctypes.byref(h)),
+                       "ring_comm_init")
+        self.handle = h.value
+
+    def forward(self, q, k, v, out, lse, cu, *, nseq: int, max_seqlen: int, softmax_scale: float,
+                q_descale=None, k_descales=None, v_descales=None, kv_bufs=None,
+                workspace=None) -> None:
+        """Run the ring forward on the current stream into ``out``/``lse`` (see
+        ``fa4cp_ring_attn_fwd``).  ``k_descales``/``v_descales``: ``[cp_size, H_kv]`` fp32."""
+        from . import _lib
+
+        T, Hq, D = q.shape
+        Hkv = k.shape[1]
+        rc = self.lib.fa4cp_ring_attn_fwd(
+            self.handle, q.data_ptr(), k.data_ptr(), v.data_ptr(), _lib.ptr(kv_bufs),
+            0 if kv_bufs is None else kv_bufs.numel() * kv_bufs.element_size(), out.data_ptr(),
+            lse.data_ptr(), cu.data_ptr(), nseq, max_seqlen, T, Hq, Hkv, D,
+            _lib.dtype_code(q.dtype), _lib.dtype_code(k.dtype), float(softmax_scale),
+            _lib.ptr(q_descale), _lib.ptr(k_descales), _lib.ptr(v_descales), _lib.ptr(workspace),
+            0 if workspace is None else workspace.numel(), _lib.stream_of(q))
+        _lib.check(rc, "ring_attn_fwd")
+
+    def start_timing(self, max_launches: int) -> None:
+        """Time the next ``max_launches`` attention launches with CUDA events."""
+        from . import _lib
+
+        _lib.check(self.lib.fa4cp_ring_timing(self.handle, int(max_launches)), "ring_timing")
+
+    def read_timing(self):
+        """``(summed ms, launches)`` of the launches timed since :meth:`start_timing`."""
+        import ctypes
+
+        from . import _lib
+
+        ms, n = ctypes.c_double(0.0), ctypes.c_int32(0)
+        _lib.check(self.lib.fa4cp_ring_timing_read(self.handle, ctypes.byref(ms), ctypes.byref(n)),
+                   "ring_timing_read")
+        return ms.value, n.value
+
+    def close(self) -> None:
+        if self.handle:
+            self.lib.fa4cp_ring_comm_destroy(self.handle)
+            self.handle = 0
+
+
+_NATIVE_RINGS: Dict[Tuple, Tuple[object, NativeRing]] = {}
+
+
+def native_ring(cp_rank: int, cp_size: int, device: torch.device,
+                group: Optional["dist.ProcessGroup"] = None) -> NativeRing:
+    """The :class:`NativeRing` of ``group`` on ``device`` (created collectively on first use)."""
+    g = group if group is not None else dist.group.WORLD
+    key = (id(g), device.index, cp_rank, cp_size)
+    hit = _NATIVE_RINGS.get(key)
+    if hit is not None and hit[0] is g:
+        return hit[1]
+    ring = NativeRing(cp_rank, cp_size, device, group)
+    _NATIVE_RINGS[key] = (g, ring)  # holds the group so its id stays unique
+    return ring
+
+
+def close_native_rings() -> None:
+    """Free every native ring's NCCL communicator (all ranks, before the process group)."""
+    for _, ring in list(_NATIVE_RINGS.values()):
+        ring.close()
+    _NATIVE_RINGS.clear()

@@ -12,8 +12,11 @@ Per step, one launch of the sm_100a attention kernel does the step's attention o
 the rows the pattern selects, in place (no ``index_select`` / ``index_copy_``
 staging), and in ``incremental`` mode merges the partial into the running
 ``(out, lse)`` in its epilogue.  ``batched`` mode keeps every partial and runs one
-k-way merge kernel at the end.  The K/V rotation (:class:`.comm.KVRing`) overlaps
-each step's attention with the next hop's transfer.
+k-way merge kernel at the end.  The K/V rotation overlaps each step's attention with
+the next hop's transfer.  Over an NCCL group, ``incremental`` mode runs as one call of
+the library's native ring executor (:class:`.comm.NativeRing`: NCCL hops and attention
+steps issued from C++); ``batched`` mode, and any other group, runs the Python step
+loop over :class:`.comm.KVRing`, which follows the same schedule.
 """
 
 import math
@@ -25,8 +28,8 @@ import torch.distributed as dist
 
 from . import _lib
 from .attn_backend import (PATTERN_BACK_Q, PATTERN_FRONT_KV, PATTERN_VARLEN, _check_qkv,
-                           attn_into, norm_descale, out_dtype_for)
-from .comm import KVRing
+                           attn_into, is_mixed, norm_descale, out_dtype_for)
+from .comm import KVRing, native_ring
 from .config import RingConfig
 from .merge import merge_states
 
@@ -110,6 +113,9 @@ def ring_flash_attn(
 
     k0 = local_k.contiguous()
     v0 = local_v.contiguous()
+    if S > 1 and cfg.merge_mode == "incremental" and use_native_executor(group):
+        return _native_forward(local_q.contiguous(), k0, v0, cfg, group, cu=cu, nseq=nseq,
+                               max_seqlen=max_seqlen, descales=descales)
     ring = KVRing(k0, v0, rank, S, group) if S > 1 else None
     if ring is not None:
         ring.start()  # hop 1 overlaps the local step
@@ -123,6 +129,51 @@ def ring_flash_attn(
 
     return ring_forward(local_q, kv_at, step_done, cfg, cu=cu, nseq=nseq, max_seqlen=max_seqlen,
                         descales=descales)
+
+
+# Run incremental-mode rings over an NCCL group through the native executor
+# (fa4cp_ring_attn_fwd); False keeps the Python step loop over KVRing.
+NATIVE_EXECUTOR = True
+
+
+def use_native_executor(group=None) -> bool:
+    return (NATIVE_EXECUTOR and dist.is_available() and dist.is_initialized()
+            and dist.get_backend(group) == "nccl")
+
+
+def _native_forward(q, k, v, cfg: RingConfig, group, *, cu, nseq, max_seqlen,
+                    descales: Optional[Descales]) -> torch.Tensor:
+    """The whole ring forward in one native call (NCCL hops + attention steps in C++)."""
+    S, rank = cfg.cp_size, cfg.cp_rank
+    T, Hq, D = q.shape
+    Hkv = k.shape[1]
+    dev = q.device
+    assert dist.get_rank(group) == rank, "cp_rank must be this process's rank in the cp group"
+    assert dist.get_world_size(group) == S, "cp_size must be the size of the cp group"
+    scale = cfg.softmax_scale if cfg.softmax_scale is not None else 1.0 / math.sqrt(D)
+    fp8 = q.dtype == torch.float8_e4m3fn
+    kv8 = k.dtype == torch.float8_e4m3fn
+    qd = norm_descale(descales.q, Hkv, dev) if (fp8 and descales and descales.q is not None) else None
+    kds = vds = None
+    if kv8 and descales and descales.k:
+        assert len(descales.k) == S, "one k descale per source rank"
+        kds = torch.stack([norm_descale(d, Hkv, dev) for d in descales.k])
+    if kv8 and descales and descales.v:
+        assert len(descales.v) == S, "one v descale per source rank"
+        vds = torch.stack([norm_descale(d, Hkv, dev) for d in descales.v])
+    out = torch.empty((T, Hq, D), dtype=out_dtype_for(q.dtype), device=dev)
+    lse = torch.empty((T, Hq), dtype=torch.float32, device=dev)
+    kv_bytes = k.numel() * k.element_size()
+    bufs = torch.empty(4 * kv_bytes, dtype=torch.uint8, device=dev)  # two [K | V] slots
+    ws = None
+    if is_mixed(q, k):
+        nbytes = _lib.load().fa4cp_attn_kv8_workspace_bytes(T, Hkv, D)
+        ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=dev)
+    native_ring(rank, S, dev, group).forward(
+        q, k, v, out, lse, cu, nseq=nseq, max_seqlen=max_seqlen, softmax_scale=scale,
+        q_descale=qd, k_descales=kds, v_descales=vds, kv_bufs=bufs, workspace=ws)
+    _lib.count_launches(S * (3 if ws is not None else 1))
+    return out
 
 
 def ring_forward(local_q, kv_at, step_done, cfg: RingConfig, *, cu: torch.Tensor, nseq: int,

@@ -239,6 +239,52 @@ FA4CP_API int fa4cp_half_index(const int32_t* cu, int32_t nseq, int64_t total, i
 FA4CP_API int fa4cp_local_cu(const int32_t* full_cu, int32_t nseq, int32_t cp_size, int32_t* local_cu,
                    void* stream);
 
+/*
+ * Native ring executor (incremental merge mode): one call runs a rank's whole zig-zag ring
+ * forward, every K/V hop as NCCL send/recv on the executor's high-priority comm stream and
+ * every step's attention (fa4cp_attn_fwd / fa4cp_attn_fwd_kv8, with the in-epilogue merge) on
+ * `stream`, ordered by CUDA events; the host never blocks.
+ * Replaces: the per-step loop of fa4_ring/ring_attention.py:121-172 (torch.distributed
+ * P2P + `_attn` + `merge_state_in_place` per step) with the reference's step schedule.
+ *
+ * Unlike the rest of this header, the ring handle owns resources: an NCCL communicator
+ * (ncclCommInitRank; libnccl.so.2 found with dlopen), a comm stream and CUDA events.
+ *
+ * fa4cp_ring_unique_id: writes the 128-byte NCCL unique id (HOST buffer) that rank 0 makes
+ *   and the caller broadcasts to the cp group.
+ * fa4cp_ring_comm_init: collective over the cp group (every rank calls it with the same id,
+ *   on the device it will run on); NCCL rank = cp rank; 1 <= nranks <= 64.
+ *   handle_out HOST int64.
+ * fa4cp_ring_comm_destroy: waits for the comm stream and frees the communicator; call it on
+ *   every rank before the process group is torn down.
+ * fa4cp_ring_timing: time the next `max_launches` attention launches (0 = off) with CUDA
+ *   events; fa4cp_ring_timing_read waits for them and returns their summed duration (HOST
+ *   double, ms) and count (HOST int32), then starts over.
+ * fa4cp_ring_attn_fwd:
+ *   q [total, Hq, D], k/v [total, Hkv, D] this rank's zig-zag shards; out/lse [total, Hq(, D)]
+ *   receive the merged result (out dtype: q's, bf16 for e4m3 q);
+ *   kv_bufs >= 4 * total*Hkv*D*elem bytes, 16-byte aligned (two receive slots of K and V);
+ *   cu int32 [nseq+1] local boundaries (even lengths), max_seqlen the longest local length;
+ *   q_dtype/kv_dtype: equal (f16 | bf16 | e4m3), or bf16 q with e4m3 k/v (then `workspace`
+ *   of fa4cp_attn_kv8_workspace_bytes(total, Hkv, D) bytes is required);
+ *   k_descales/v_descales float32 [cp_size, Hkv] indexed by SOURCE rank (NULL for 16-bit
+ *   k/v), q_descale float32 [Hkv] for e4m3 q.
+ */
+FA4CP_API int fa4cp_ring_unique_id(uint8_t* id_out);
+FA4CP_API int fa4cp_ring_comm_init(const uint8_t* id, int32_t nranks, int32_t rank,
+                                   int64_t* handle_out);
+FA4CP_API int fa4cp_ring_comm_destroy(int64_t handle);
+FA4CP_API int fa4cp_ring_timing(int64_t handle, int32_t max_launches);
+FA4CP_API int fa4cp_ring_timing_read(int64_t handle, double* total_ms, int32_t* launches);
+FA4CP_API int fa4cp_ring_attn_fwd(int64_t handle, const void* q, const void* k, const void* v,
+                                  void* kv_bufs, int64_t kv_bufs_bytes, void* out, float* lse,
+                                  const int32_t* cu, int32_t nseq, int32_t max_seqlen,
+                                  int64_t total, int32_t num_heads_q, int32_t num_heads_kv,
+                                  int32_t head_dim, int32_t q_dtype, int32_t kv_dtype,
+                                  float softmax_scale, const float* q_descale,
+                                  const float* k_descales, const float* v_descales,
+                                  void* workspace, int64_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

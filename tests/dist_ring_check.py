@@ -1,6 +1,13 @@
 """torchrun worker of test_gpu_ring.test_nccl_ring_multi_gpu: the real NCCL ring
 (``ring_flash_attn``) on every rank, outputs gathered and checked on rank 0 against the
-oracle's dense causal attention, for both merge modes, single and packed sequences."""
+oracle's dense causal attention.
+
+Cases: bf16 single and packed sequences in ``incremental`` mode through both executors
+(the native C++ one, ``fa4cp_ring_attn_fwd``, and the Python step loop over ``KVRing``)
+and in ``batched`` mode; FP8 e4m3 Q/K/V and bf16 Q with e4m3 K/V (quantised per rank,
+descales all-gathered by source rank) through the native executor, checked against the
+dense attention of the dequantised tensors.  Tolerances: bf16 2e-2, FP8 6e-2.
+"""
 
 import datetime
 import math
@@ -14,16 +21,27 @@ import torch.distributed as dist
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 sys.path[:0] = [ROOT, os.path.join(ROOT, "fa4-cp_b200")]
 
-from fa4_ring import RingConfig, ring_flash_attn, zigzag_shard  # noqa: E402
+from fa4_ring import Descales, RingConfig, ring_flash_attn, zigzag_shard  # noqa: E402
+from fa4_ring import ring_attention  # noqa: E402
+from fa4_ring.comm import close_native_rings, nccl_pg_options  # noqa: E402
+from fa4_ring.fp8 import allgather_descales, quantize_e4m3  # noqa: E402
 from fa4_ring.zigzag import zigzag_shard_varlen, zigzag_unshard, zigzag_unshard_varlen  # noqa: E402
 from oracle import ring_oracle as orc  # noqa: E402
+
+
+def gather_full(t, world, cu, num_seqs):
+    parts = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(parts, t.contiguous())
+    if dist.get_rank() != 0:
+        return None
+    full = zigzag_unshard(parts, world) if num_seqs == 1 else zigzag_unshard_varlen(parts, cu, world)
+    return full.float().cpu().numpy()
 
 
 def main():
     rank = int(os.environ["RANK"])
     world = int(os.environ["WORLD_SIZE"])
     torch.cuda.set_device(int(os.environ["LOCAL_RANK"]))
-    from fa4_ring.comm import nccl_pg_options
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                             pg_options=nccl_pg_options())
     dev = torch.device("cuda")
@@ -31,39 +49,57 @@ def main():
     try:
         H, Hkv, D = 8, 2, 128
         scale = 1.0 / math.sqrt(D)
+        runs = [("bf16", "incremental", True), ("bf16", "incremental", False),
+                ("bf16", "batched", False), ("e4m3", "incremental", True),
+                ("mixed", "incremental", True)]
         for num_seqs in (1, 3):
             g = torch.Generator().manual_seed(1234)
             lens = [2 * world * 96] if num_seqs == 1 else [2 * world * n for n in (64, 16, 80)]
             cu = [0] + list(np.cumsum(lens))
-            N = cu[-1]
-            q, k, v = (torch.randn(N, h, D, generator=g).bfloat16().to(dev) for h in (H, Hkv, Hkv))
-            for mode in ("incremental", "batched"):
+            q, k, v = (torch.randn(cu[-1], h, D, generator=g).bfloat16().to(dev)
+                       for h in (H, Hkv, Hkv))
+            if num_seqs == 1:
+                lq, lk, lv = (zigzag_shard(t, rank, world) for t in (q, k, v))
+                kw = {}
+            else:
+                lq, lcu = zigzag_shard_varlen(q, cu, rank, world)
+                lk, _ = zigzag_shard_varlen(k, cu, rank, world)
+                lv, _ = zigzag_shard_varlen(v, cu, rank, world)
+                kw = {"cu_seqlens": lcu, "max_seqlen": max(lens) // world}
+            for kind, mode, native in runs:
+                ring_attention.NATIVE_EXECUTOR = native
                 cfg = RingConfig(cp_size=world, cp_rank=rank, merge_mode=mode)
-                if num_seqs == 1:
-                    lq, lk, lv = (zigzag_shard(t, rank, world) for t in (q, k, v))
-                    out = ring_flash_attn(lq, lk, lv, cfg)
-                else:
-                    lq, lcu = zigzag_shard_varlen(q, cu, rank, world)
-                    lk, _ = zigzag_shard_varlen(k, cu, rank, world)
-                    lv, _ = zigzag_shard_varlen(v, cu, rank, world)
-                    out = ring_flash_attn(lq, lk, lv, cfg, cu_seqlens=lcu,
-                                          max_seqlen=max(lens) // world)
-                gathered = [torch.empty_like(out) for _ in range(world)]
-                dist.all_gather(gathered, out.contiguous())
+                tq, tk, tv, desc = lq, lk, lv, None
+                if kind != "bf16":
+                    tk, ks = quantize_e4m3(lk)
+                    tv, vs = quantize_e4m3(lv)
+                    qs = None
+                    if kind == "e4m3":
+                        tq, qs = quantize_e4m3(lq)
+                    desc = Descales(q=qs, k=allgather_descales(ks), v=allgather_descales(vs))
+                out = ring_flash_attn(tq, tk, tv, cfg, descales=desc, **kw)
+                full = gather_full(out, world, cu, num_seqs)
+                # the inputs the ring actually attended (dequantised for FP8)
+                ins = []
+                for t8, t16, name in ((tq, lq, "q"), (tk, lk, "k"), (tv, lv, "v")):
+                    if t8.dtype == torch.float8_e4m3fn:
+                        sc = {"q": desc.q, "k": desc.k[rank], "v": desc.v[rank]}[name]
+                        t16 = (t8.float() * sc).bfloat16()
+                    ins.append(gather_full(t16, world, cu, num_seqs))
                 if rank == 0:
-                    full = (zigzag_unshard(gathered, world) if num_seqs == 1
-                            else zigzag_unshard_varlen(gathered, cu, world))
-                    full = full.float().cpu().numpy()
-                    qn, kn, vn = (t.float().cpu().numpy() for t in (q, k, v))
+                    qn, kn, vn = ins
+                    tol = 2e-2 if kind == "bf16" else 6e-2
                     for j in range(len(lens)):
                         a, b = cu[j], cu[j + 1]
                         ref, _ = orc.dense_causal(qn[a:b], kn[a:b], vn[a:b], scale)
                         err = float(np.abs(full[a:b] - ref).max())
-                        print(f"world={world} seqs={num_seqs} mode={mode} seq{j} max_err={err:.3e}")
-                        ok &= err <= 2e-2
+                        print(f"world={world} seqs={num_seqs} {kind} mode={mode} "
+                              f"native={native} seq{j} max_err={err:.3e}")
+                        ok &= err <= tol
         torch.cuda.synchronize()
         dist.barrier()
     finally:
+        close_native_rings()
         dist.destroy_process_group()
     if rank == 0:
         print("RING_OK" if ok else "RING_FAIL")
