@@ -272,7 +272,11 @@ def gpu_main(args, rank, world, local_rank):
     attn_backend.launch_timer = launches  # attention launches issued from Python
     nring = None
     if world > 1 and ring_attention.use_native_executor() and args.merge == "incremental":
-        nring = native_ring(rank, cp, dev)  # created during warm-up; times its own launches
+        nring = native_ring(rank, cp, dev, transport=ring_attention.RING_TRANSPORT)  # from warm-up
+        if args.sm_reserve is not None:
+            nring.set_sm_reserve(args.sm_reserve)
+            for _ in range(2):
+                run()
         nring.start_timing(args.steps * cp)
     barrier()
     torch.cuda.synchronize()
@@ -292,7 +296,16 @@ def gpu_main(args, rank, world, local_rank):
     gpu_launches = _lib.launch_count - n_launch0
     clocks = clk.summary()
     ms_local = sum(a.elapsed_time(b) for a, b in ev)
+    timeline = None
     if nring is not None:
+        if args.timeline:
+            a, h = nring.timeline()
+            last = (args.steps - 1) * cp  # the last timed forward
+            t0 = a[last][0]
+            timeline = {"rank": rank,
+                        "attn": [[round(x - t0, 3), round(y - t0, 3)] for x, y in a[last:]],
+                        "hops": [[round(x - t0, 3), round(y - t0, 3)]
+                                 for x, y in h[(args.steps - 1) * (cp - 1):]]}
         attn_ms_local, n_attn_local = nring.read_timing()
         nring.start_timing(0)
     else:
@@ -308,6 +321,12 @@ def gpu_main(args, rank, world, local_rank):
                             device=dev)
         if world > 1:
             dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+        if timeline is not None:
+            tls = [None] * world
+            dist.all_gather_object(tls, timeline)
+            if rank == 0:
+                for t in tls:
+                    print(json.dumps(t), file=sys.stderr, flush=True)
         if rank == 0:
             ms_step = vals[0].item() / args.steps
             return {"quick": True, "config": args.config, "seq_len": N, "cp": cp,
@@ -398,7 +417,8 @@ def gpu_main(args, rank, world, local_rank):
         "exposed_comm_pct": round(exposed, 2) if world > 1 else None,
         "exposed_comm_def": "100 * (step time - summed attention-kernel time) / step time, "
                             "max over ranks",
-        "executor": "native (fa4cp_ring_attn_fwd)" if nring is not None else "python step loop",
+        "executor": (f"native (fa4cp_ring_attn_fwd), {nring.transport} transport"
+                     if nring is not None else "python step loop"),
         "roofline": {"bound": "tensor", "kernel": "fa4cp attn_fwd (tcgen05)",
                      "achieved": None if achieved is None else round(achieved, 1),
                      "peak": peak, "peak_kind": peak_kind,
@@ -482,6 +502,14 @@ def main():
                     help="override the single-sequence length (smaller only for profiling)")
     ap.add_argument("--nccl-cta-policy", choices=["default", "zero"], default="default",
                     help="NCCL CTA policy of the ring's process group (zero: no SM CTAs)")
+    ap.add_argument("--transport", choices=["copy_engine", "nccl"], default="copy_engine",
+                    help="K/V transport of the native ring executor (N > 1)")
+    ap.add_argument("--sm-reserve", type=int, default=None,
+                    help="SMs the persistent attention grid leaves to NCCL during a ring call "
+                         "(native executor; default: the library's)")
+    ap.add_argument("--timeline", action="store_true",
+                    help="with --quick: print each rank's launch/hop timeline of the last "
+                         "forward to stderr")
     ap.add_argument("--quick", action="store_true",
                     help="profiling run: timed loop only (no e2e, no CPU baseline)")
     args = ap.parse_args()
@@ -502,6 +530,8 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank),
                                 pg_options=nccl_pg_options(args.nccl_cta_policy))
+    from fa4_ring import ring_attention
+    ring_attention.RING_TRANSPORT = args.transport
     try:
         line = gpu_main(args, rank, world, local_rank)
     finally:

@@ -22,6 +22,11 @@ namespace fa4cp {
 
 __device__ int g_attn_status = 0;
 
+// SMs the persistent kernel leaves free on this host thread (set by the ring executor around
+// its launches, so the K/V hop's NCCL kernel finds SMs while the attention grid runs)
+thread_local int t_sm_reserve = 0;
+void set_sm_reserve(int n) { t_sm_reserve = n > 0 ? n : 0; }
+
 namespace {
 
 constexpr int BM = 128;
@@ -1202,7 +1207,8 @@ int launch2(const void* q, const void* k, const void* v, int64_t total_q, int64_
     FA4CP_CHECK_CUDA(cudaGetDevice(&dev));
     FA4CP_CHECK_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   }
-  const int grid = (TR::PERSISTENT && p.n_tiles > sms) ? sms : p.n_tiles;
+  const int ctas = sms - (t_sm_reserve < sms / 2 ? t_sm_reserve : sms / 2);
+  const int grid = (TR::PERSISTENT && p.n_tiles > ctas) ? ctas : p.n_tiles;
   attn_fwd_2q_kernel<TR><<<grid, TR::THREADS, TR::SMEM_BYTES, stream>>>(mq, mk, mv, p);
   return check_launch("attn_fwd_2q");
 }

@@ -48,6 +48,10 @@ inline int check_launch(const char* what) {
 int launch_dequant_e4m3(const void* x, const float* descale, void* out, int64_t rows, int heads,
                         int dim, cudaStream_t st);
 
+// SMs the persistent attention grid leaves free for concurrent kernels, for launches made by
+// the calling host thread (attn_fwd_sm100.cu); 0 = use every SM
+void set_sm_reserve(int n);
+
 inline int elem_bytes(int dtype) {
   switch (dtype) {
     case FA4CP_DTYPE_F16: return 2;

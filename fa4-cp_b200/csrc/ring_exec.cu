@@ -12,10 +12,19 @@
 // Hop s+1 is issued right after step s's wait, before step s's attention, so the transfer
 // overlaps that attention.
 //
-// The NCCL communicator is this library's own (ncclCommInitRank over the cp group, NCCL
-// rank = cp rank), created once per group by fa4cp_ring_comm_init from a unique id that
-// the caller broadcasts.  libnccl.so.2 is opened with dlopen, so the process's already
-// loaded NCCL (PyTorch's) is the one used.
+// Two transports move the K/V:
+//   * copy engine (preferred): each rank pushes the K/V it attended at step s-1 straight
+//     into its right neighbour's receive slot with cudaMemcpyAsync over NVLink (a CUDA IPC
+//     mapping of the neighbour's receive area), so the rotation takes no SM from the
+//     attention kernel.  Arrival and slot release are 32-bit hop counters in the receive
+//     areas, written into the peer's memory with cuStreamWriteValue32 (which fences the
+//     stream's earlier writes first) and waited on locally with cuStreamWaitValue32.  The
+//     order of operations is a plan (build_ce_plan) that a CPU test runs against a
+//     multi-rank simulator for deadlocks and slot hazards;
+//   * NCCL: send/recv on the executor's own communicator (ncclCommInitRank over the cp
+//     group, NCCL rank = cp rank, unique id broadcast by the caller) into caller-provided
+//     ping-pong buffers.  libnccl.so.2 is opened with dlopen, so the process's already
+//     loaded NCCL (PyTorch's) is the one used.
 #include <dlfcn.h>
 #include <nccl.h>
 #include <string.h>
@@ -67,6 +76,9 @@ NcclApi* nccl_api() {
 }
 
 constexpr int kMaxRing = 64;
+constexpr int kDefaultSmReserve = 8;
+// streams of the copy-engine plan: the caller's, the K and V copies, the slot releases
+enum { ST_COMPUTE = 0, ST_COPY_K = 1, ST_COPY_V = 2, ST_RELEASE = 3, ST_COUNT = 4 };
 
 struct RingComm {
   ncclComm_t comm = nullptr;
@@ -75,20 +87,53 @@ struct RingComm {
   cudaEvent_t ev_start = nullptr;      // the caller's stream reached the call
   cudaEvent_t ev_hop[kMaxRing] = {};   // hop s landed
   cudaEvent_t ev_step[kMaxRing] = {};  // attention of step s done (its K/V slot is free)
-  // optional launch timing: 2 timing events per attention launch, filled in call order
-  std::vector<cudaEvent_t> tev;
-  int t_used = 0;
+  int sm_reserve = kDefaultSmReserve;  // SMs the persistent attention grid leaves to NCCL
+  // optional timing: 2 timing events per attention launch and per hop, filled in call order
+  std::vector<cudaEvent_t> tev, hev;
+  int t_used = 0, h_used = 0;
+  // copy-engine transport
+  bool ce = false;                       // transport: copy engine (else NCCL)
+  uint8_t* area = nullptr;               // own receive area (cudaMalloc)
+  uint8_t* right = nullptr;              // right neighbour's area (IPC mapping)
+  uint8_t* left = nullptr;               // left neighbour's area (== right when nranks == 2)
+  int64_t kv_cap = 0;                    // bytes of one K (or V) part of a slot
+  uint64_t hops = 0;                     // hops issued since the area was (re)allocated
+  cudaStream_t cstream[4] = {};          // [1] K copy, [2] V copy, [3] release ([0]: caller's)
+  std::vector<cudaEvent_t> cev;          // plan events
+};
+
+// restores the calling thread's SM reserve when a ring call returns
+struct SmReserveScope {
+  explicit SmReserveScope(int n) { set_sm_reserve(n); }
+  ~SmReserveScope() { set_sm_reserve(0); }
 };
 
 void destroy_timing(RingComm* rc) {
   for (cudaEvent_t e : rc->tev)
     if (e) cudaEventDestroy(e);
+  for (cudaEvent_t e : rc->hev)
+    if (e) cudaEventDestroy(e);
   rc->tev.clear();
-  rc->t_used = 0;
+  rc->hev.clear();
+  rc->t_used = rc->h_used = 0;
+}
+
+void close_peers(RingComm* rc) {
+  if (rc->right) cudaIpcCloseMemHandle(rc->right);
+  if (rc->left && rc->left != rc->right) cudaIpcCloseMemHandle(rc->left);
+  rc->right = rc->left = nullptr;
+  rc->ce = false;
 }
 
 void destroy_ring(RingComm* rc) {
   destroy_timing(rc);
+  if (rc->area || rc->right) cudaDeviceSynchronize();
+  close_peers(rc);
+  if (rc->area) cudaFree(rc->area);
+  for (int i = 1; i < ST_COUNT; ++i)
+    if (rc->cstream[i]) cudaStreamDestroy(rc->cstream[i]);
+  for (cudaEvent_t e : rc->cev)
+    if (e) cudaEventDestroy(e);
   if (rc->ev_start) cudaEventDestroy(rc->ev_start);
   for (int i = 0; i < kMaxRing; ++i) {
     if (rc->ev_hop[i]) cudaEventDestroy(rc->ev_hop[i]);
@@ -103,10 +148,128 @@ int nccl_fail(NcclApi* api, const char* what, ncclResult_t r) {
   return FA4CP_ERR_CUDA;
 }
 
+// ---------------------------------------------------------------------------------------
+// copy-engine transport: the plan
+//
+// Hop g (a counter over all hops of all calls, from 1) carries one K/V shard into the
+// receiver's slot g & 1.  A call with hops g0+1 .. g0+S-1 issues, in this host order:
+//   RECORD start on the compute stream, push(1);
+//   for s = 0 .. S-1:
+//     s > 0:     compute waits ARRIVED >= g0+s;  push(s+1) if s+1 < S
+//     attention of step s on the compute stream (K/V: the caller's for s = 0, else slot g0+s);
+//     RECORD step(s);  s > 0: release(s)
+//   the compute stream joins the copy and release streams.
+// push(s) (K on copy stream 1, V on copy stream 2): wait for the data (the caller's stream
+// for s = 1, else ARRIVED >= g0+s-1), wait FREED >= g0+s-2 (the right neighbour released
+// the previous use of the slot), copy into the right neighbour's slot g0+s, then write its
+// ARRIVED = g0+s.  release(s) (release stream): after attention s and push(s+1), write
+// the left neighbour's FREED = g0+s.  Every wait depends only on neighbours' earlier
+// iterations, so the plan cannot deadlock even if every stream of a rank ran in host
+// order on one hardware queue.
+// ---------------------------------------------------------------------------------------
+enum { FLAG_ARRIVED = 0, FLAG_FREED = 1 };
+enum { PEER_RIGHT = 0, PEER_LEFT = 1 };
+constexpr int EV_START = 0;
+constexpr int ev_step(int s) { return 1 + s; }
+constexpr int ev_vdone(int s) { return 1 + kMaxRing + s; }
+constexpr int ev_push(int s) { return 1 + 2 * kMaxRing + s; }
+constexpr int EV_COPY_END = 1 + 3 * kMaxRing;
+constexpr int EV_REL_END = 2 + 3 * kMaxRing;
+constexpr int EV_COUNT = 3 + 3 * kMaxRing;
+constexpr int64_t kFlagOffset[2] = {0, 128};  // ARRIVED, FREED (own 128-byte lines)
+constexpr int64_t kSlotBase = 4096;           // receive slots start here in the area
+
+using RingOp = fa4cp_ring_op;
+
+void build_ce_plan(int S, int rank, uint64_t g0, std::vector<RingOp>& ops) {
+  (void)rank;  // the plan is the same on every rank; peers are implied (left / right)
+  ops.clear();
+  auto op = [&](int st, int kind, int64_t a = 0, int64_t b = 0, int64_t c = 0) {
+    ops.push_back(RingOp{st, kind, a, b, c});
+  };
+  auto G = [&](int s) { return int64_t(uint32_t(g0 + uint64_t(s))); };  // flag value of hop
+  auto push = [&](int s) {
+    for (int st : {ST_COPY_K, ST_COPY_V}) {
+      if (s == 1)
+        op(st, FA4CP_RING_OP_WAIT_EVENT, EV_START);
+      else
+        op(st, FA4CP_RING_OP_WAIT_FLAG, FLAG_ARRIVED, G(s - 1));
+      if (g0 + uint64_t(s) >= 3)  // the slot's previous use, hop g-2, must be released
+        op(st, FA4CP_RING_OP_WAIT_FLAG, FLAG_FREED, int64_t(uint32_t(G(s) - 2)));
+      op(st, FA4CP_RING_OP_COPY, st == ST_COPY_K ? 0 : 1, s == 1 ? -1 : G(s - 1), G(s));
+    }
+    op(ST_COPY_V, FA4CP_RING_OP_RECORD, ev_vdone(s));
+    op(ST_COPY_K, FA4CP_RING_OP_WAIT_EVENT, ev_vdone(s));
+    op(ST_COPY_K, FA4CP_RING_OP_WRITE_FLAG, PEER_RIGHT, FLAG_ARRIVED, G(s));
+    op(ST_COPY_K, FA4CP_RING_OP_RECORD, ev_push(s));
+  };
+  if (S > 1) {
+    op(ST_COMPUTE, FA4CP_RING_OP_RECORD, EV_START);
+    push(1);
+  }
+  for (int s = 0; s < S; ++s) {
+    if (s > 0) {
+      op(ST_COMPUTE, FA4CP_RING_OP_WAIT_FLAG, FLAG_ARRIVED, G(s));
+      if (s + 1 < S) push(s + 1);
+    }
+    op(ST_COMPUTE, FA4CP_RING_OP_ATTN, s, s == 0 ? -1 : G(s));
+    op(ST_COMPUTE, FA4CP_RING_OP_RECORD, ev_step(s));
+    if (s > 0) {
+      op(ST_RELEASE, FA4CP_RING_OP_WAIT_EVENT, ev_step(s));
+      if (s + 1 < S) op(ST_RELEASE, FA4CP_RING_OP_WAIT_EVENT, ev_push(s + 1));
+      op(ST_RELEASE, FA4CP_RING_OP_WRITE_FLAG, PEER_LEFT, FLAG_FREED, G(s));
+    }
+  }
+  if (S > 1) {
+    op(ST_COPY_K, FA4CP_RING_OP_RECORD, EV_COPY_END);
+    op(ST_RELEASE, FA4CP_RING_OP_RECORD, EV_REL_END);
+    op(ST_COMPUTE, FA4CP_RING_OP_WAIT_EVENT, EV_COPY_END);
+    op(ST_COMPUTE, FA4CP_RING_OP_WAIT_EVENT, EV_REL_END);
+  }
+}
+
+using StreamWaitValue32Fn = CUresult (*)(CUstream, CUdeviceptr, cuuint32_t, unsigned int);
+using StreamWriteValue32Fn = CUresult (*)(CUstream, CUdeviceptr, cuuint32_t, unsigned int);
+
+struct StreamMemOps {
+  StreamWaitValue32Fn wait = nullptr;
+  StreamWriteValue32Fn write = nullptr;
+};
+
+StreamMemOps* stream_mem_ops() {
+  static StreamMemOps ops;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuStreamWaitValue32", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      ops.wait = reinterpret_cast<StreamWaitValue32Fn>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuStreamWriteValue32", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      ops.write = reinterpret_cast<StreamWriteValue32Fn>(p);
+  });
+  return (ops.wait && ops.write) ? &ops : nullptr;
+}
+
 }  // namespace
 }  // namespace fa4cp
 
 using namespace fa4cp;
+
+extern "C" int fa4cp_ring_ce_plan(int32_t nranks, int32_t rank, int64_t g0, fa4cp_ring_op* ops,
+                                  int32_t capacity) {
+  FA4CP_CHECK_ARG(g0 >= 0, "negative hop count");
+  FA4CP_CHECK_ARG(nranks >= 1 && nranks <= kMaxRing && rank >= 0 && rank < nranks,
+                  "bad ring size %d / rank %d", nranks, rank);
+  std::vector<RingOp> plan;
+  build_ce_plan(nranks, rank, uint64_t(g0), plan);
+  FA4CP_CHECK_ARG(ops == nullptr || capacity >= int32_t(plan.size()),
+                  "capacity %d < %d plan entries", capacity, int(plan.size()));
+  if (ops != nullptr) memcpy(ops, plan.data(), plan.size() * sizeof(RingOp));
+  return int32_t(plan.size());
+}
 
 #define FA4CP_CHECK_NCCL(expr)                               \
   do {                                                       \
@@ -126,11 +289,11 @@ extern "C" int fa4cp_ring_unique_id(uint8_t* id_out) {
 
 extern "C" int fa4cp_ring_comm_init(const uint8_t* id, int32_t nranks, int32_t rank,
                                     int64_t* handle_out) {
-  FA4CP_CHECK_ARG(id != nullptr && handle_out != nullptr, "null argument");
+  FA4CP_CHECK_ARG(handle_out != nullptr, "null argument");
   FA4CP_CHECK_ARG(nranks >= 1 && nranks <= kMaxRing && rank >= 0 && rank < nranks,
                   "bad ring size %d / rank %d (at most %d ranks)", nranks, rank, kMaxRing);
   NcclApi* api = nccl_api();
-  FA4CP_CHECK_ARG(api != nullptr, "libnccl.so.2 could not be loaded");
+  FA4CP_CHECK_ARG(id == nullptr || api != nullptr, "libnccl.so.2 could not be loaded");
   RingComm* rc = new RingComm();
   rc->nranks = nranks;
   rc->rank = rank;
@@ -143,12 +306,17 @@ extern "C" int fa4cp_ring_comm_init(const uint8_t* id, int32_t nranks, int32_t r
     ce = cudaEventCreateWithFlags(&rc->ev_hop[i], cudaEventDisableTiming);
     if (ce == cudaSuccess) ce = cudaEventCreateWithFlags(&rc->ev_step[i], cudaEventDisableTiming);
   }
+  for (int i = 1; ce == cudaSuccess && i < ST_COUNT; ++i)
+    ce = cudaStreamCreateWithPriority(&rc->cstream[i], cudaStreamNonBlocking, hi);
+  rc->cev.assign(EV_COUNT, nullptr);
+  for (int i = 0; ce == cudaSuccess && i < EV_COUNT; ++i)
+    ce = cudaEventCreateWithFlags(&rc->cev[i], cudaEventDisableTiming);
   if (ce != cudaSuccess) {
     set_last_error("ring stream/event creation failed: %s", cudaGetErrorString(ce));
     destroy_ring(rc);
     return FA4CP_ERR_CUDA;
   }
-  if (nranks > 1) {
+  if (nranks > 1 && id != nullptr) {
     ncclUniqueId uid;
     memcpy(&uid, id, sizeof(uid));
     ncclResult_t r = api->CommInitRank(&rc->comm, nranks, uid, rank);
@@ -172,6 +340,70 @@ extern "C" int fa4cp_ring_comm_destroy(int64_t handle) {
   return FA4CP_OK;
 }
 
+extern "C" int fa4cp_ring_ipc_alloc(int64_t handle, int64_t kv_capacity, uint8_t* ipc_out) {
+  FA4CP_CHECK_ARG(handle != 0 && ipc_out != nullptr, "null argument");
+  FA4CP_CHECK_ARG(kv_capacity > 0 && kv_capacity <= (int64_t(1) << 40), "bad kv_capacity");
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "CUDA IPC handles are 64 bytes");
+  RingComm* rc = reinterpret_cast<RingComm*>(handle);
+  FA4CP_CHECK_CUDA(cudaDeviceSynchronize());
+  close_peers(rc);
+  if (rc->area) {
+    FA4CP_CHECK_CUDA(cudaFree(rc->area));
+    rc->area = nullptr;
+  }
+  const int64_t cap = (kv_capacity + 255) / 256 * 256;
+  void* p = nullptr;
+  FA4CP_CHECK_CUDA(cudaMalloc(&p, size_t(kSlotBase + 4 * cap)));
+  rc->area = static_cast<uint8_t*>(p);
+  rc->kv_cap = cap;
+  rc->hops = 0;
+  FA4CP_CHECK_CUDA(cudaMemset(rc->area, 0, size_t(kSlotBase)));
+  FA4CP_CHECK_CUDA(cudaDeviceSynchronize());
+  cudaIpcMemHandle_t h;
+  FA4CP_CHECK_CUDA(cudaIpcGetMemHandle(&h, rc->area));
+  memcpy(ipc_out, &h, sizeof(h));
+  return FA4CP_OK;
+}
+
+extern "C" int fa4cp_ring_ipc_open(int64_t handle, const uint8_t* left_ipc,
+                                   const uint8_t* right_ipc) {
+  FA4CP_CHECK_ARG(handle != 0 && left_ipc != nullptr && right_ipc != nullptr, "null argument");
+  RingComm* rc = reinterpret_cast<RingComm*>(handle);
+  FA4CP_CHECK_ARG(rc->nranks > 1, "a ring of one rank has no neighbours");
+  FA4CP_CHECK_ARG(rc->area != nullptr, "fa4cp_ring_ipc_alloc must come first");
+  FA4CP_CHECK_ARG(stream_mem_ops() != nullptr,
+                  "cuStreamWaitValue32/cuStreamWriteValue32 are not available");
+  close_peers(rc);
+  cudaIpcMemHandle_t hr, hl;
+  memcpy(&hr, right_ipc, sizeof(hr));
+  memcpy(&hl, left_ipc, sizeof(hl));
+  void* pr = nullptr;
+  FA4CP_CHECK_CUDA(cudaIpcOpenMemHandle(&pr, hr, cudaIpcMemLazyEnablePeerAccess));
+  rc->right = static_cast<uint8_t*>(pr);
+  if (memcmp(&hr, &hl, sizeof(hr)) == 0) {
+    rc->left = rc->right;
+  } else {
+    void* pl = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&pl, hl, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      close_peers(rc);
+      set_last_error("cudaIpcOpenMemHandle(left) failed: %s", cudaGetErrorString(e));
+      return FA4CP_ERR_CUDA;
+    }
+    rc->left = static_cast<uint8_t*>(pl);
+  }
+  rc->ce = true;
+  return FA4CP_OK;
+}
+
+extern "C" int fa4cp_ring_ipc_close(int64_t handle) {
+  FA4CP_CHECK_ARG(handle != 0, "null ring handle");
+  RingComm* rc = reinterpret_cast<RingComm*>(handle);
+  FA4CP_CHECK_CUDA(cudaDeviceSynchronize());
+  close_peers(rc);
+  return FA4CP_OK;
+}
+
 extern "C" int fa4cp_ring_timing(int64_t handle, int32_t max_launches) {
   FA4CP_CHECK_ARG(handle != 0, "null ring handle");
   FA4CP_CHECK_ARG(max_launches >= 0 && max_launches <= (1 << 16), "bad max_launches %d",
@@ -179,14 +411,51 @@ extern "C" int fa4cp_ring_timing(int64_t handle, int32_t max_launches) {
   RingComm* rc = reinterpret_cast<RingComm*>(handle);
   destroy_timing(rc);
   rc->tev.assign(2 * size_t(max_launches), nullptr);
-  for (auto& e : rc->tev) {
-    cudaError_t ce = cudaEventCreate(&e);
-    if (ce != cudaSuccess) {
-      set_last_error("cudaEventCreate failed: %s", cudaGetErrorString(ce));
-      destroy_timing(rc);
-      return FA4CP_ERR_CUDA;
+  rc->hev.assign(2 * size_t(max_launches), nullptr);
+  for (auto* vec : {&rc->tev, &rc->hev}) {
+    for (auto& e : *vec) {
+      cudaError_t ce = cudaEventCreate(&e);
+      if (ce != cudaSuccess) {
+        set_last_error("cudaEventCreate failed: %s", cudaGetErrorString(ce));
+        destroy_timing(rc);
+        return FA4CP_ERR_CUDA;
+      }
     }
   }
+  return FA4CP_OK;
+}
+
+extern "C" int fa4cp_ring_set_sm_reserve(int64_t handle, int32_t sm_reserve) {
+  FA4CP_CHECK_ARG(handle != 0, "null ring handle");
+  FA4CP_CHECK_ARG(sm_reserve >= 0 && sm_reserve <= 64, "sm_reserve %d out of [0, 64]", sm_reserve);
+  reinterpret_cast<RingComm*>(handle)->sm_reserve = sm_reserve;
+  return FA4CP_OK;
+}
+
+extern "C" int fa4cp_ring_timeline(int64_t handle, float* attn_ms, int32_t max_attn,
+                                   float* hop_ms, int32_t max_hops, int32_t* n_attn,
+                                   int32_t* n_hops) {
+  FA4CP_CHECK_ARG(handle != 0 && n_attn != nullptr && n_hops != nullptr, "null argument");
+  RingComm* rc = reinterpret_cast<RingComm*>(handle);
+  *n_attn = *n_hops = 0;
+  if (rc->t_used == 0) return FA4CP_OK;
+  cudaEvent_t t0 = rc->tev[0];
+  auto rel = [&](cudaEvent_t e, float* dst) -> int {
+    FA4CP_CHECK_CUDA(cudaEventSynchronize(e));
+    FA4CP_CHECK_CUDA(cudaEventElapsedTime(dst, t0, e));
+    return FA4CP_OK;
+  };
+  int r;
+  const int na = rc->t_used < max_attn ? rc->t_used : max_attn;
+  for (int i = 0; i < na && attn_ms != nullptr; ++i)
+    if ((r = rel(rc->tev[2 * i], attn_ms + 2 * i)) || (r = rel(rc->tev[2 * i + 1], attn_ms + 2 * i + 1)))
+      return r;
+  const int nh = rc->h_used < max_hops ? rc->h_used : max_hops;
+  for (int i = 0; i < nh && hop_ms != nullptr; ++i)
+    if ((r = rel(rc->hev[2 * i], hop_ms + 2 * i)) || (r = rel(rc->hev[2 * i + 1], hop_ms + 2 * i + 1)))
+      return r;
+  *n_attn = attn_ms != nullptr ? na : 0;
+  *n_hops = hop_ms != nullptr ? nh : 0;
   return FA4CP_OK;
 }
 
@@ -202,9 +471,80 @@ extern "C" int fa4cp_ring_timing_read(int64_t handle, double* total_ms, int32_t*
   }
   *total_ms = sum;
   *launches = rc->t_used;
-  rc->t_used = 0;
+  rc->t_used = rc->h_used = 0;
   return FA4CP_OK;
 }
+
+namespace {
+
+// Issues the copy-engine plan of one call (build_ce_plan) on the caller's stream `st` and
+// the ring's copy / release streams.
+template <class AttnStep>
+int run_ce(RingComm* rc, AttnStep& attn_step, const void* k, const void* v, int64_t kv_bytes,
+           cudaStream_t st) {
+  FA4CP_CHECK_ARG(kv_bytes <= rc->kv_cap, "K/V shard of %lld bytes exceeds the receive slots "
+                  "(%lld bytes; reallocate with fa4cp_ring_ipc_alloc)",
+                  static_cast<long long>(kv_bytes), static_cast<long long>(rc->kv_cap));
+  StreamMemOps* mem = stream_mem_ops();
+  FA4CP_CHECK_ARG(mem != nullptr, "stream memory operations are not available");
+  std::vector<RingOp> plan;
+  build_ce_plan(rc->nranks, rc->rank, rc->hops, plan);
+  cudaStream_t streams[ST_COUNT] = {st, rc->cstream[1], rc->cstream[2], rc->cstream[3]};
+  auto slot = [&](uint8_t* area, int64_t hop, int64_t part) {
+    return area + kSlotBase + (hop & 1) * 2 * rc->kv_cap + part * rc->kv_cap;
+  };
+  auto flag = [&](uint8_t* area, int64_t which) {
+    return reinterpret_cast<CUdeviceptr>(area + kFlagOffset[which]);
+  };
+  for (const RingOp& o : plan) {
+    cudaStream_t cs = streams[o.stream];
+    switch (o.kind) {
+      case FA4CP_RING_OP_RECORD: {
+        FA4CP_CHECK_CUDA(cudaEventRecord(rc->cev[o.a], cs));
+        const bool push_end = o.a >= ev_push(0) && o.a < ev_push(kMaxRing);
+        if (push_end && rc->h_used < int(rc->hev.size() / 2))
+          FA4CP_CHECK_CUDA(cudaEventRecord(rc->hev[2 * rc->h_used++ + 1], cs));
+        break;
+      }
+      case FA4CP_RING_OP_WAIT_EVENT:
+        FA4CP_CHECK_CUDA(cudaStreamWaitEvent(cs, rc->cev[o.a], 0));
+        break;
+      case FA4CP_RING_OP_WAIT_FLAG: {
+        CUresult e = mem->wait(cs, flag(rc->area, o.a), cuuint32_t(o.b), CU_STREAM_WAIT_VALUE_GEQ);
+        FA4CP_CHECK_ARG(e == CUDA_SUCCESS, "cuStreamWaitValue32 failed (CUresult %d)", int(e));
+        break;
+      }
+      case FA4CP_RING_OP_WRITE_FLAG: {
+        uint8_t* peer = o.a == PEER_RIGHT ? rc->right : rc->left;
+        CUresult e = mem->write(cs, flag(peer, o.b), cuuint32_t(o.c), CU_STREAM_WRITE_VALUE_DEFAULT);
+        FA4CP_CHECK_ARG(e == CUDA_SUCCESS, "cuStreamWriteValue32 failed (CUresult %d)", int(e));
+        break;
+      }
+      case FA4CP_RING_OP_COPY: {
+        const void* src = o.b < 0 ? (o.a == 0 ? k : v) : slot(rc->area, o.b, o.a);
+        if (o.a == 0 && rc->h_used < int(rc->hev.size() / 2))
+          FA4CP_CHECK_CUDA(cudaEventRecord(rc->hev[2 * rc->h_used], cs));
+        FA4CP_CHECK_CUDA(cudaMemcpyAsync(slot(rc->right, o.c, o.a), src, size_t(kv_bytes),
+                                         cudaMemcpyDeviceToDevice, cs));
+        break;
+      }
+      case FA4CP_RING_OP_ATTN: {
+        const void* kk = o.b < 0 ? k : slot(rc->area, o.b, 0);
+        const void* vv = o.b < 0 ? v : slot(rc->area, o.b, 1);
+        int r = attn_step(int(o.a), kk, vv);
+        if (r != FA4CP_OK) return r;
+        break;
+      }
+      default:
+        set_last_error("unknown ring plan operation %d", o.kind);
+        return FA4CP_ERR_INVALID;
+    }
+  }
+  rc->hops += uint64_t(rc->nranks - 1);
+  return FA4CP_OK;
+}
+
+}  // namespace
 
 extern "C" int fa4cp_ring_attn_fwd(int64_t handle, const void* q, const void* k, const void* v,
                                    void* kv_bufs, int64_t kv_bufs_bytes, void* out, float* lse,
@@ -226,17 +566,46 @@ extern "C" int fa4cp_ring_attn_fwd(int64_t handle, const void* q, const void* k,
   const int out_dtype = q_dtype == FA4CP_DTYPE_E4M3 ? FA4CP_DTYPE_BF16 : q_dtype;
   const int64_t kv_bytes = total * num_heads_kv * int64_t(head_dim) * elem_bytes(kv_dtype);
   FA4CP_CHECK_ARG(kv_bytes % 16 == 0, "K/V shard bytes must be a multiple of 16");
-  FA4CP_CHECK_ARG(S == 1 || (kv_bufs != nullptr && kv_bufs_bytes >= 4 * kv_bytes),
-                  "kv_bufs must hold two slots of K and V (%lld bytes)",
-                  static_cast<long long>(4 * kv_bytes));
-  FA4CP_CHECK_ARG(uintptr_t(kv_bufs) % 16 == 0, "kv_bufs must be 16-byte aligned");
   int dev = 0;
   FA4CP_CHECK_CUDA(cudaGetDevice(&dev));
   FA4CP_CHECK_ARG(dev == rc->device, "current device %d is not the ring's device %d", dev,
                   rc->device);
-  NcclApi* api = nccl_api();
-  FA4CP_CHECK_ARG(api != nullptr, "libnccl.so.2 could not be loaded");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+  // attention of step s on the given K/V, merged into (out, lse) for s > 0
+  auto attn_step = [&](int s, const void* kk, const void* vv) -> int {
+    const int src = (rank - s + S) % S;
+    const int pattern = s == 0 ? FA4CP_PATTERN_VARLEN
+                               : (s > rank ? FA4CP_PATTERN_BACK_Q : FA4CP_PATTERN_FRONT_KV);
+    const int q_rows = pattern == FA4CP_PATTERN_BACK_Q ? (max_seqlen + 1) / 2 : max_seqlen;
+    const float* kd = k_descales ? k_descales + int64_t(src) * num_heads_kv : nullptr;
+    const float* vd = v_descales ? v_descales + int64_t(src) * num_heads_kv : nullptr;
+    const bool timed = rc->t_used < int(rc->tev.size() / 2);
+    if (timed) FA4CP_CHECK_CUDA(cudaEventRecord(rc->tev[2 * rc->t_used], st));
+    int r;
+    if (mixed)
+      r = fa4cp_attn_fwd_kv8(q, kk, vv, out, lse, cu, cu, nseq, q_rows, total, total, num_heads_q,
+                             num_heads_kv, head_dim, q_dtype, pattern, s == 0, softmax_scale, kd,
+                             vd, s > 0, workspace, workspace_bytes, stream);
+    else
+      r = fa4cp_attn_fwd(q, kk, vv, out, lse, cu, cu, nseq, q_rows, total, total, num_heads_q,
+                         num_heads_kv, head_dim, q_dtype, out_dtype, pattern, s == 0,
+                         softmax_scale, q_descale, kd, vd, s > 0, stream);
+    if (r != FA4CP_OK) return r;
+    if (timed) FA4CP_CHECK_CUDA(cudaEventRecord(rc->tev[2 * rc->t_used++ + 1], st));
+    return FA4CP_OK;
+  };
+
+  if (S == 1) return attn_step(0, k, v);
+  if (rc->ce) return run_ce(rc, attn_step, k, v, kv_bytes, st);
+
+  // ---- NCCL transport
+  FA4CP_CHECK_ARG(kv_bufs != nullptr && kv_bufs_bytes >= 4 * kv_bytes,
+                  "kv_bufs must hold two slots of K and V (%lld bytes)",
+                  static_cast<long long>(4 * kv_bytes));
+  FA4CP_CHECK_ARG(uintptr_t(kv_bufs) % 16 == 0, "kv_bufs must be 16-byte aligned");
+  NcclApi* api = nccl_api();
+  FA4CP_CHECK_ARG(api != nullptr && rc->comm != nullptr, "the ring has no NCCL communicator");
   const int send_peer = (rank + 1) % S, recv_peer = (rank + S - 1) % S;
   uint8_t* bufs = static_cast<uint8_t*>(kv_bufs);
   // step s >= 1 reads slot s & 1, laid out [K | V], kv_bytes each
@@ -253,6 +622,8 @@ extern "C" int fa4cp_ring_attn_fwd(int64_t handle, const void* q, const void* k,
     } else if (s >= 3) {
       FA4CP_CHECK_CUDA(cudaStreamWaitEvent(rc->stream, rc->ev_step[s - 2], 0));
     }
+    const bool timed = rc->h_used < int(rc->hev.size() / 2);
+    if (timed) FA4CP_CHECK_CUDA(cudaEventRecord(rc->hev[2 * rc->h_used], rc->stream));
     FA4CP_CHECK_NCCL(api->GroupStart());
     FA4CP_CHECK_NCCL(api->Send(step_k(s - 1), size_t(kv_bytes), ncclUint8, send_peer, rc->comm,
                                rc->stream));
@@ -264,35 +635,19 @@ extern "C" int fa4cp_ring_attn_fwd(int64_t handle, const void* q, const void* k,
                                rc->stream));
     FA4CP_CHECK_NCCL(api->GroupEnd());
     FA4CP_CHECK_CUDA(cudaEventRecord(rc->ev_hop[s], rc->stream));
+    if (timed) FA4CP_CHECK_CUDA(cudaEventRecord(rc->hev[2 * rc->h_used++ + 1], rc->stream));
     return FA4CP_OK;
   };
 
   int r = FA4CP_OK;
-  if (S > 1 && (r = hop(1)) != FA4CP_OK) return r;  // hop 1 overlaps the local step
+  SmReserveScope reserve(rc->sm_reserve);
+  if ((r = hop(1)) != FA4CP_OK) return r;  // hop 1 overlaps the local step
   for (int s = 0; s < S; ++s) {
-    const int src = (rank - s + S) % S;
-    const int pattern = s == 0 ? FA4CP_PATTERN_VARLEN
-                               : (s > rank ? FA4CP_PATTERN_BACK_Q : FA4CP_PATTERN_FRONT_KV);
-    const int q_rows = pattern == FA4CP_PATTERN_BACK_Q ? (max_seqlen + 1) / 2 : max_seqlen;
     if (s > 0) {
       FA4CP_CHECK_CUDA(cudaStreamWaitEvent(st, rc->ev_hop[s], 0));
       if (s + 1 < S && (r = hop(s + 1)) != FA4CP_OK) return r;
     }
-    const float* kd = k_descales ? k_descales + int64_t(src) * num_heads_kv : nullptr;
-    const float* vd = v_descales ? v_descales + int64_t(src) * num_heads_kv : nullptr;
-    const bool timed = rc->t_used < int(rc->tev.size() / 2);
-    if (timed) FA4CP_CHECK_CUDA(cudaEventRecord(rc->tev[2 * rc->t_used], st));
-    if (mixed)
-      r = fa4cp_attn_fwd_kv8(q, step_k(s), step_v(s), out, lse, cu, cu, nseq, q_rows, total,
-                             total, num_heads_q, num_heads_kv, head_dim, q_dtype, pattern,
-                             s == 0, softmax_scale, kd, vd, s > 0, workspace, workspace_bytes,
-                             stream);
-    else
-      r = fa4cp_attn_fwd(q, step_k(s), step_v(s), out, lse, cu, cu, nseq, q_rows, total, total,
-                         num_heads_q, num_heads_kv, head_dim, q_dtype, out_dtype, pattern, s == 0,
-                         softmax_scale, q_descale, kd, vd, s > 0, stream);
-    if (r != FA4CP_OK) return r;
-    if (timed) FA4CP_CHECK_CUDA(cudaEventRecord(rc->tev[2 * rc->t_used++ + 1], st));
+    if ((r = attn_step(s, step_k(s), step_v(s))) != FA4CP_OK) return r;
     if (s + 2 < S) FA4CP_CHECK_CUDA(cudaEventRecord(rc->ev_step[s], st));
   }
   return FA4CP_OK;

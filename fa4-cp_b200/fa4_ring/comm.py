@@ -142,36 +142,75 @@ class KVRing:
 class NativeRing:
     """The library's native ring executor (``fa4cp_ring_*``) for one cp group on one GPU.
 
-    It owns an NCCL communicator over the cp group (NCCL rank = cp rank), created
-    collectively on first use from a unique id that cp rank 0 makes and broadcasts over
-    ``group``, plus a high-priority comm stream and CUDA events.  One
-    :meth:`forward` call issues a rank's whole ring forward (all hops and all attention
-    steps) from C++, so the per-step cost on the host is a few CUDA API calls instead of a
-    Python loop over ``torch.distributed`` P2P ops.  Call :func:`close_native_rings` on
-    every rank before ``destroy_process_group``.
+    One :meth:`forward` call issues a rank's whole ring forward (every K/V hop and every
+    attention step) from C++, so the host cost per step is a few CUDA API calls instead of
+    a Python loop over ``torch.distributed`` P2P ops.  Transports:
+
+    * ``"copy_engine"`` (default): each hop is a ``cudaMemcpyAsync`` straight into the right
+      neighbour's receive slot over NVLink (CUDA IPC mappings exchanged over ``group``), with
+      arrival / release hop counters written into the peers' memory and waited on by the
+      streams (``cuStreamWriteValue32`` / ``cuStreamWaitValue32``): the rotation uses no SM;
+    * ``"nccl"``: NCCL send/recv on the executor's own communicator (created collectively
+      from a unique id that cp rank 0 broadcasts over ``group``).
+
+    Call :func:`close_native_rings` on every rank before ``destroy_process_group``.
     """
 
+    TRANSPORTS = ("copy_engine", "nccl")
+
     def __init__(self, cp_rank: int, cp_size: int, device: torch.device,
-                 group: Optional["dist.ProcessGroup"] = None):
+                 group: Optional["dist.ProcessGroup"] = None, transport: str = "copy_engine"):
         import ctypes
 
         from . import _lib
 
+        if transport not in self.TRANSPORTS:
+            raise ValueError(f"unknown ring transport {transport!r}")
         self.lib = _lib.load()
-        self.rank, self.size, self.device = cp_rank, cp_size, device
-        uid = (ctypes.c_uint8 * 128)()
-        if cp_rank == 0:
-            _lib.check(self.lib.fa4cp_ring_unique_id(uid), "ring_unique_id")
-        on_gpu = dist.get_backend(group) == "nccl"
-        t = torch.tensor(list(uid), dtype=torch.uint8,
-                         device=device if on_gpu else torch.device("cpu"))
-        dist.broadcast(t, src=_global_rank(group, 0), group=group)
-        uid = (ctypes.c_uint8 * 128)(*t.cpu().tolist())
+        self.rank, self.size, self.device, self.group = cp_rank, cp_size, device, group
+        self.transport = transport
+        self.kv_capacity = 0
+        uid = None
+        if transport == "nccl" and cp_size > 1:
+            uid = (ctypes.c_uint8 * 128)()
+            if cp_rank == 0:
+                _lib.check(self.lib.fa4cp_ring_unique_id(uid), "ring_unique_id")
+            on_gpu = dist.get_backend(group) == "nccl"
+            t = torch.tensor(list(uid), dtype=torch.uint8,
+                             device=device if on_gpu else torch.device("cpu"))
+            dist.broadcast(t, src=_global_rank(group, 0), group=group)
+            uid = (ctypes.c_uint8 * 128)(*t.cpu().tolist())
         h = ctypes.c_int64(0)
         with torch.cuda.device(device):
             _lib.check(self.lib.fa4cp_ring_comm_init(uid, cp_size, cp_rank, ctypes.byref(h)),
                        "ring_comm_init")
         self.handle = h.value
+
+    def ensure_capacity(self, kv_bytes: int) -> None:
+        """Copy-engine transport: make the receive slots hold ``kv_bytes`` per K (and V).
+        Collective over the group when it grows (all ranks pass the same size)."""
+        import ctypes
+
+        from . import _lib
+
+        if self.transport != "copy_engine" or self.size < 2 or kv_bytes <= self.kv_capacity:
+            return
+        with torch.cuda.device(self.device):
+            torch.cuda.synchronize()
+            dist.barrier(group=self.group)  # no peer is still writing into the old areas
+            _lib.check(self.lib.fa4cp_ring_ipc_close(self.handle), "ring_ipc_close")
+            dist.barrier(group=self.group)  # nobody maps an area that is about to be freed
+            mine = (ctypes.c_uint8 * 64)()
+            _lib.check(self.lib.fa4cp_ring_ipc_alloc(self.handle, int(kv_bytes), mine),
+                       "ring_ipc_alloc")
+            handles = [None] * self.size
+            dist.all_gather_object(handles, (bytes(mine), int(kv_bytes)), group=self.group)
+            assert all(hb[1] == kv_bytes for hb in handles), "ranks disagree on the K/V size"
+            left = (ctypes.c_uint8 * 64)(*handles[(self.rank - 1) % self.size][0])
+            right = (ctypes.c_uint8 * 64)(*handles[(self.rank + 1) % self.size][0])
+            _lib.check(self.lib.fa4cp_ring_ipc_open(self.handle, left, right), "ring_ipc_open")
+            dist.barrier(group=self.group)  # every area is mapped before the first push
+        self.kv_capacity = int(kv_bytes)
 
     def forward(self, q, k, v, out, lse, cu, *, nseq: int, max_seqlen: int, softmax_scale: float,
                 q_descale=None, k_descales=None, v_descales=None, kv_bufs=None,
@@ -197,6 +236,29 @@ class NativeRing:
 
         _lib.check(self.lib.fa4cp_ring_timing(self.handle, int(max_launches)), "ring_timing")
 
+    def set_sm_reserve(self, n: int) -> None:
+        """SMs the persistent attention grid leaves free for the hop's NCCL kernel."""
+        from . import _lib
+
+        _lib.check(self.lib.fa4cp_ring_set_sm_reserve(self.handle, int(n)), "ring_set_sm_reserve")
+
+    def timeline(self, max_entries: int = 4096):
+        """``(attention, hops)``: lists of ``(start_ms, end_ms)`` of the timed launches and
+        hops in issue order, relative to the first timed launch (call before
+        :meth:`read_timing`, which starts over)."""
+        import ctypes
+
+        from . import _lib
+
+        a = (ctypes.c_float * (2 * max_entries))()
+        h = (ctypes.c_float * (2 * max_entries))()
+        na, nh = ctypes.c_int32(0), ctypes.c_int32(0)
+        _lib.check(self.lib.fa4cp_ring_timeline(self.handle, a, max_entries, h, max_entries,
+                                                ctypes.byref(na), ctypes.byref(nh)),
+                   "ring_timeline")
+        return ([(a[2 * i], a[2 * i + 1]) for i in range(na.value)],
+                [(h[2 * i], h[2 * i + 1]) for i in range(nh.value)])
+
     def read_timing(self):
         """``(summed ms, launches)`` of the launches timed since :meth:`start_timing`."""
         import ctypes
@@ -208,6 +270,14 @@ class NativeRing:
                    "ring_timing_read")
         return ms.value, n.value
 
+    def unmap_peers(self) -> None:
+        """Unmap the neighbours' receive areas (waits for this GPU's work)."""
+        from . import _lib
+
+        if self.handle and self.kv_capacity:
+            with torch.cuda.device(self.device):
+                _lib.check(self.lib.fa4cp_ring_ipc_close(self.handle), "ring_ipc_close")
+
     def close(self) -> None:
         if self.handle:
             self.lib.fa4cp_ring_comm_destroy(self.handle)
@@ -218,20 +288,29 @@ _NATIVE_RINGS: Dict[Tuple, Tuple[object, NativeRing]] = {}
 
 
 def native_ring(cp_rank: int, cp_size: int, device: torch.device,
-                group: Optional["dist.ProcessGroup"] = None) -> NativeRing:
+                group: Optional["dist.ProcessGroup"] = None,
+                transport: str = "copy_engine") -> NativeRing:
     """The :class:`NativeRing` of ``group`` on ``device`` (created collectively on first use)."""
     g = group if group is not None else dist.group.WORLD
-    key = (id(g), device.index, cp_rank, cp_size)
+    key = (id(g), device.index, cp_rank, cp_size, transport)
     hit = _NATIVE_RINGS.get(key)
     if hit is not None and hit[0] is g:
         return hit[1]
-    ring = NativeRing(cp_rank, cp_size, device, group)
+    ring = NativeRing(cp_rank, cp_size, device, group, transport)
     _NATIVE_RINGS[key] = (g, ring)  # holds the group so its id stays unique
     return ring
 
 
 def close_native_rings() -> None:
-    """Free every native ring's NCCL communicator (all ranks, before the process group)."""
-    for _, ring in list(_NATIVE_RINGS.values()):
+    """Free every native ring (its NCCL communicator or receive areas).  Collective: all
+    ranks call it, before the process group is destroyed.  Every rank unmaps its
+    neighbours' receive areas before any rank frees its own (freeing memory another
+    process still maps is undefined behaviour in CUDA IPC)."""
+    rings = [ring for _, ring in _NATIVE_RINGS.values()]
+    for ring in rings:
+        ring.unmap_peers()
+    if any(r.transport == "copy_engine" and r.size > 1 for r in rings) and dist.is_initialized():
+        dist.barrier()
+    for ring in rings:
         ring.close()
     _NATIVE_RINGS.clear()

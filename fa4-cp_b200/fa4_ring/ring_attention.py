@@ -134,6 +134,9 @@ def ring_flash_attn(
 # Run incremental-mode rings over an NCCL group through the native executor
 # (fa4cp_ring_attn_fwd); False keeps the Python step loop over KVRing.
 NATIVE_EXECUTOR = True
+# K/V transport of the native executor: "copy_engine" (NVLink copies + stream counters, no
+# SM used) or "nccl" (send/recv on the executor's own communicator)
+RING_TRANSPORT = "copy_engine"
 
 
 def use_native_executor(group=None) -> bool:
@@ -164,12 +167,17 @@ def _native_forward(q, k, v, cfg: RingConfig, group, *, cu, nseq, max_seqlen,
     out = torch.empty((T, Hq, D), dtype=out_dtype_for(q.dtype), device=dev)
     lse = torch.empty((T, Hq), dtype=torch.float32, device=dev)
     kv_bytes = k.numel() * k.element_size()
-    bufs = torch.empty(4 * kv_bytes, dtype=torch.uint8, device=dev)  # two [K | V] slots
+    ring = native_ring(rank, S, dev, group, RING_TRANSPORT)
+    bufs = None
+    if ring.transport == "nccl":
+        bufs = torch.empty(4 * kv_bytes, dtype=torch.uint8, device=dev)  # two [K | V] slots
+    else:
+        ring.ensure_capacity(kv_bytes)
     ws = None
     if is_mixed(q, k):
         nbytes = _lib.load().fa4cp_attn_kv8_workspace_bytes(T, Hkv, D)
         ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=dev)
-    native_ring(rank, S, dev, group).forward(
+    ring.forward(
         q, k, v, out, lse, cu, nseq=nseq, max_seqlen=max_seqlen, softmax_scale=scale,
         q_descale=qd, k_descales=kds, v_descales=vds, kv_bufs=bufs, workspace=ws)
     _lib.count_launches(S * (3 if ws is not None else 1))

@@ -253,28 +253,71 @@ FA4CP_API int fa4cp_local_cu(const int32_t* full_cu, int32_t nseq, int32_t cp_si
  * fa4cp_ring_unique_id: writes the 128-byte NCCL unique id (HOST buffer) that rank 0 makes
  *   and the caller broadcasts to the cp group.
  * fa4cp_ring_comm_init: collective over the cp group (every rank calls it with the same id,
- *   on the device it will run on); NCCL rank = cp rank; 1 <= nranks <= 64.
- *   handle_out HOST int64.
+ *   on the device it will run on); NCCL rank = cp rank; 1 <= nranks <= 64.  id NULL: no
+ *   NCCL communicator (copy-engine transport only; not collective).  handle_out HOST int64.
  * fa4cp_ring_comm_destroy: waits for the comm stream and frees the communicator; call it on
  *   every rank before the process group is torn down.
- * fa4cp_ring_timing: time the next `max_launches` attention launches (0 = off) with CUDA
- *   events; fa4cp_ring_timing_read waits for them and returns their summed duration (HOST
- *   double, ms) and count (HOST int32), then starts over.
+ * fa4cp_ring_set_sm_reserve: SMs (0..64, default 8) the persistent attention grid leaves
+ *   free during a ring call, so that the hop's NCCL kernel runs beside it.
+ * fa4cp_ring_timing: time the next `max_launches` attention launches and hops (0 = off) with
+ *   CUDA events; fa4cp_ring_timeline writes (start, end) pairs in ms relative to the first
+ *   timed launch's start into HOST float arrays (attention launches and hops, in issue order,
+ *   at most max_attn / max_hops pairs; counts to n_attn / n_hops); fa4cp_ring_timing_read
+ *   waits for them and returns the launches' summed duration (HOST double, ms) and count
+ *   (HOST int32), then starts over.
  * fa4cp_ring_attn_fwd:
  *   q [total, Hq, D], k/v [total, Hkv, D] this rank's zig-zag shards; out/lse [total, Hq(, D)]
  *   receive the merged result (out dtype: q's, bf16 for e4m3 q);
- *   kv_bufs >= 4 * total*Hkv*D*elem bytes, 16-byte aligned (two receive slots of K and V);
+ *   kv_bufs (NCCL transport; NULL with the copy engine) >= 4 * total*Hkv*D*elem bytes,
+ *   16-byte aligned (two receive slots of K and V); the copy engine needs
+ *   total*Hkv*D*elem <= the kv_capacity of fa4cp_ring_ipc_alloc;
  *   cu int32 [nseq+1] local boundaries (even lengths), max_seqlen the longest local length;
  *   q_dtype/kv_dtype: equal (f16 | bf16 | e4m3), or bf16 q with e4m3 k/v (then `workspace`
  *   of fa4cp_attn_kv8_workspace_bytes(total, Hkv, D) bytes is required);
  *   k_descales/v_descales float32 [cp_size, Hkv] indexed by SOURCE rank (NULL for 16-bit
  *   k/v), q_descale float32 [Hkv] for e4m3 q.
  */
+/*
+ * Copy-engine transport of the ring executor (used when fa4cp_ring_ipc_open has run):
+ * fa4cp_ring_ipc_alloc: (re)allocates this rank's receive area (two slots of K and V of
+ *   kv_capacity bytes each, plus hop counters) with cudaMalloc and writes its 64-byte CUDA
+ *   IPC handle to ipc_out (HOST).  Synchronises the device; resets the hop count.
+ * fa4cp_ring_ipc_open: maps the left and right neighbours' areas (HOST 64-byte handles; the
+ *   same handle for both when nranks == 2).  fa4cp_ring_ipc_close unmaps them.
+ * Every rank calls alloc, exchanges handles, and opens, with a barrier of the cp group
+ * before freeing (close, barrier, alloc) and after opening; all ranks use the same capacity.
+ * fa4cp_ring_ce_plan: the ordered operations one call issues (host only, no GPU needed),
+ *   for hops g0+1 .. g0+nranks-1; returns the count (ops may be NULL to ask for it).
+ */
+typedef struct {
+  int32_t stream; /* 0 caller's (compute), 1 K copy, 2 V copy, 3 release */
+  int32_t kind;   /* FA4CP_RING_OP_* */
+  int64_t a, b, c;
+} fa4cp_ring_op;
+#define FA4CP_RING_OP_RECORD 0     /* record event a */
+#define FA4CP_RING_OP_WAIT_EVENT 1 /* wait for event a's latest record */
+#define FA4CP_RING_OP_WAIT_FLAG 2  /* wait until own counter a (0 arrived, 1 freed) >= b (cyclic) */
+#define FA4CP_RING_OP_WRITE_FLAG 3 /* write counter b of peer a (0 right, 1 left) := c */
+#define FA4CP_RING_OP_COPY 4       /* part a (0 K, 1 V): src b (-1 caller's, else own slot of
+                                      hop b) -> right neighbour's slot of hop c */
+#define FA4CP_RING_OP_ATTN 5       /* attention of step a on K/V b (-1 caller's, else own slot
+                                      of hop b) */
+FA4CP_API int fa4cp_ring_ipc_alloc(int64_t handle, int64_t kv_capacity, uint8_t* ipc_out);
+FA4CP_API int fa4cp_ring_ipc_open(int64_t handle, const uint8_t* left_ipc,
+                                  const uint8_t* right_ipc);
+FA4CP_API int fa4cp_ring_ipc_close(int64_t handle);
+FA4CP_API int fa4cp_ring_ce_plan(int32_t nranks, int32_t rank, int64_t g0, fa4cp_ring_op* ops,
+                                 int32_t capacity);
+
 FA4CP_API int fa4cp_ring_unique_id(uint8_t* id_out);
 FA4CP_API int fa4cp_ring_comm_init(const uint8_t* id, int32_t nranks, int32_t rank,
                                    int64_t* handle_out);
 FA4CP_API int fa4cp_ring_comm_destroy(int64_t handle);
+FA4CP_API int fa4cp_ring_set_sm_reserve(int64_t handle, int32_t sm_reserve);
 FA4CP_API int fa4cp_ring_timing(int64_t handle, int32_t max_launches);
+FA4CP_API int fa4cp_ring_timeline(int64_t handle, float* attn_ms, int32_t max_attn,
+                                  float* hop_ms, int32_t max_hops, int32_t* n_attn,
+                                  int32_t* n_hops);
 FA4CP_API int fa4cp_ring_timing_read(int64_t handle, double* total_ms, int32_t* launches);
 FA4CP_API int fa4cp_ring_attn_fwd(int64_t handle, const void* q, const void* k, const void* v,
                                   void* kv_bufs, int64_t kv_bufs_bytes, void* out, float* lse,

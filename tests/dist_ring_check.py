@@ -2,11 +2,13 @@
 (``ring_flash_attn``) on every rank, outputs gathered and checked on rank 0 against the
 oracle's dense causal attention.
 
-Cases: bf16 single and packed sequences in ``incremental`` mode through both executors
-(the native C++ one, ``fa4cp_ring_attn_fwd``, and the Python step loop over ``KVRing``)
-and in ``batched`` mode; FP8 e4m3 Q/K/V and bf16 Q with e4m3 K/V (quantised per rank,
-descales all-gathered by source rank) through the native executor, checked against the
-dense attention of the dequantised tensors.  Tolerances: bf16 2e-2, FP8 6e-2.
+Cases: bf16 single and packed sequences in ``incremental`` mode through the native C++
+executor (``fa4cp_ring_attn_fwd``) with both transports (copy engine, NCCL) and through
+the Python step loop over ``KVRing``, and in ``batched`` mode; FP8 e4m3 Q/K/V and bf16 Q
+with e4m3 K/V (quantised per rank, descales all-gathered by source rank) through the
+native executor, checked against the dense attention of the dequantised tensors.  The
+copy-engine cases run twice in a row (the hop counters carry over between calls), and
+the packed case makes the receive slots grow.  Tolerances: bf16 2e-2, FP8 6e-2.
 """
 
 import datetime
@@ -49,9 +51,10 @@ def main():
     try:
         H, Hkv, D = 8, 2, 128
         scale = 1.0 / math.sqrt(D)
-        runs = [("bf16", "incremental", True), ("bf16", "incremental", False),
-                ("bf16", "batched", False), ("e4m3", "incremental", True),
-                ("mixed", "incremental", True)]
+        runs = [("bf16", "incremental", "copy_engine"), ("bf16", "incremental", "copy_engine"),
+                ("bf16", "incremental", "nccl"), ("bf16", "incremental", "python"),
+                ("bf16", "batched", "python"), ("e4m3", "incremental", "copy_engine"),
+                ("mixed", "incremental", "copy_engine"), ("e4m3", "incremental", "nccl")]
         for num_seqs in (1, 3):
             g = torch.Generator().manual_seed(1234)
             lens = [2 * world * 96] if num_seqs == 1 else [2 * world * n for n in (64, 16, 80)]
@@ -66,8 +69,10 @@ def main():
                 lk, _ = zigzag_shard_varlen(k, cu, rank, world)
                 lv, _ = zigzag_shard_varlen(v, cu, rank, world)
                 kw = {"cu_seqlens": lcu, "max_seqlen": max(lens) // world}
-            for kind, mode, native in runs:
-                ring_attention.NATIVE_EXECUTOR = native
+            for kind, mode, executor in runs:
+                ring_attention.NATIVE_EXECUTOR = executor != "python"
+                if executor != "python":
+                    ring_attention.RING_TRANSPORT = executor
                 cfg = RingConfig(cp_size=world, cp_rank=rank, merge_mode=mode)
                 tq, tk, tv, desc = lq, lk, lv, None
                 if kind != "bf16":
@@ -94,7 +99,7 @@ def main():
                         ref, _ = orc.dense_causal(qn[a:b], kn[a:b], vn[a:b], scale)
                         err = float(np.abs(full[a:b] - ref).max())
                         print(f"world={world} seqs={num_seqs} {kind} mode={mode} "
-                              f"native={native} seq{j} max_err={err:.3e}")
+                              f"executor={executor} seq{j} max_err={err:.3e}")
                         ok &= err <= tol
         torch.cuda.synchronize()
         dist.barrier()
