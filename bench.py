@@ -300,12 +300,12 @@ def gpu_main(args, rank, world, local_rank):
     if nring is not None:
         if args.timeline:
             a, h = nring.timeline()
-            last = (args.steps - 1) * cp  # the last timed forward
-            t0 = a[last][0]
+            na, nh = len(a) // args.steps, len(h) // args.steps  # per forward
+            a, h = a[(args.steps - 1) * na:], h[(args.steps - 1) * nh:]  # the last forward
+            t0 = a[0][0]
             timeline = {"rank": rank,
-                        "attn": [[round(x - t0, 3), round(y - t0, 3)] for x, y in a[last:]],
-                        "hops": [[round(x - t0, 3), round(y - t0, 3)]
-                                 for x, y in h[(args.steps - 1) * (cp - 1):]]}
+                        "attn": [[round(x - t0, 3), round(y - t0, 3)] for x, y in a],
+                        "hops": [[round(x - t0, 3), round(y - t0, 3)] for x, y in h]}
         attn_ms_local, n_attn_local = nring.read_timing()
         nring.start_timing(0)
     else:

@@ -1103,6 +1103,8 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
   if (warp == 9) tmem_dealloc(tmem, TR::TM_COLS);
 }
 
+#include "ring_fused.cuh"
+
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
@@ -1215,6 +1217,62 @@ int launch2(const void* q, const void* k, const void* v, int64_t total_q, int64_
 
 bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
 
+// 4-D view [slots, rows, heads, D] (slot stride in bytes) with a box of (128 bytes, 1 head,
+// box_rows, 1 slot): the receive slots of the ring, one per hop.
+int make_map4(CUtensorMap* map, const void* base, int64_t rows, int heads, int D, int elem,
+              int box_rows, int slots, int64_t slot_stride) {
+  EncodeTiledFn enc = get_encode_fn();
+  FA4CP_CHECK_ARG(enc != nullptr, "cuTensorMapEncodeTiled is unavailable");
+  const cuuint64_t dims[4] = {cuuint64_t(D), cuuint64_t(heads), cuuint64_t(rows), cuuint64_t(slots)};
+  const cuuint64_t strides[3] = {cuuint64_t(D) * elem, cuuint64_t(heads) * D * elem,
+                                 cuuint64_t(slot_stride)};
+  const cuuint32_t box[4] = {cuuint32_t(128 / elem), 1, cuuint32_t(box_rows), 1};
+  const cuuint32_t es[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, elem == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16,
+                   4, const_cast<void*>(base), dims, strides, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_last_error("cuTensorMapEncodeTiled (4-D) failed (%d)", int(r));
+    return FA4CP_ERR_CUDA;
+  }
+  return FA4CP_OK;
+}
+
+template <class TR>
+int launch_ring_fused(const void* q, const void* k, const void* v, const void* slots_k,
+                      const void* slots_v, int64_t slot_stride, int64_t total, int max_seqlen,
+                      const RingFusedParams& p0, cudaStream_t stream) {
+  static bool attr_set = false;
+  if (!attr_set) {
+    FA4CP_CHECK_CUDA(cudaFuncSetAttribute(ring_fused_kernel<TR>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          TR::SMEM_BYTES));
+    attr_set = true;
+  }
+  RingFusedParams p = p0;
+  p.n_pairs = (max_seqlen / 2 + 2 * BM - 1) / (2 * BM);
+  if (p.n_pairs <= 0 || total <= 0) return FA4CP_OK;
+  CUtensorMap mq, mk0, mv0, mks, mvs;
+  int rc;
+  if ((rc = make_map(&mq, q, total, p.Hq, TR::D, TR::ELEM, BM))) return rc;
+  if ((rc = make_map(&mk0, k, total, p.Hkv, TR::D, TR::ELEM, TR::BN))) return rc;
+  if ((rc = make_map(&mv0, v, total, p.Hkv, TR::D, TR::ELEM, TR::BN))) return rc;
+  if (p.S > 1) {
+    if ((rc = make_map4(&mks, slots_k, total, p.Hkv, TR::D, TR::ELEM, TR::BN, p.S - 1, slot_stride)))
+      return rc;
+    if ((rc = make_map4(&mvs, slots_v, total, p.Hkv, TR::D, TR::ELEM, TR::BN, p.S - 1, slot_stride)))
+      return rc;
+  } else {
+    mks = mk0;  // no step reads a slot
+    mvs = mv0;
+  }
+  FA4CP_CHECK_ARG(int64_t(ring_grid(p.n_pairs, p.Hq, p.nseq)) < (int64_t(1) << 31), "grid too large");
+  ring_fused_kernel<TR><<<ring_grid(p.n_pairs, p.Hq, p.nseq), TR::THREADS, TR::SMEM_BYTES, stream>>>(
+      mq, mk0, mv0, mks, mvs, p);
+  return check_launch("ring_fused");
+}
+
 }  // namespace
 }  // namespace fa4cp
 
@@ -1279,6 +1337,59 @@ extern "C" int fa4cp_attn_fwd(const void* q, const void* k, const void* v, void*
     if (head_dim == 256) return launch<Traits<256, 64, 2, false>>(q, k, v, total_q, total_k, max_seqlen_q, p, st);
   }
   set_last_error("head_dim %d with dtype %d is not supported", head_dim, in_dtype);
+  return FA4CP_ERR_UNSUPPORTED;
+}
+
+extern "C" int fa4cp_ring_attn_fused(const void* q, const void* k, const void* v,
+                                     const void* slots_k, const void* slots_v,
+                                     int64_t slot_stride, void* out, float* lse,
+                                     const int32_t* cu, int32_t nseq, int32_t max_seqlen,
+                                     int64_t total, int32_t num_heads_q, int32_t num_heads_kv,
+                                     int32_t head_dim, int32_t dtype, float softmax_scale,
+                                     int32_t nranks, int32_t rank, const uint32_t* arrived,
+                                     uint32_t arrived_base, void* stream) {
+  FA4CP_CHECK_ARG(nseq >= 1 && cu != nullptr, "cu_seqlens must describe >= 1 sequence");
+  FA4CP_CHECK_ARG(nranks >= 1 && nranks <= 64 && rank >= 0 && rank < nranks,
+                  "bad ring size %d / rank %d", nranks, rank);
+  FA4CP_CHECK_ARG(num_heads_q > 0 && num_heads_kv > 0 && num_heads_q % num_heads_kv == 0,
+                  "H_q=%d not a multiple of H_kv=%d", num_heads_q, num_heads_kv);
+  FA4CP_CHECK_ARG(total >= 0 && max_seqlen >= 0, "bad sizes");
+  FA4CP_CHECK_ARG(softmax_scale > 0.f, "softmax_scale must be positive");
+  if (dtype != FA4CP_DTYPE_BF16 && dtype != FA4CP_DTYPE_F16) {
+    set_last_error("the ring kernel takes f16 or bf16 (dtype %d)", dtype);
+    return FA4CP_ERR_UNSUPPORTED;
+  }
+  if (total == 0) return FA4CP_OK;
+  FA4CP_CHECK_ARG(q && k && v && out && lse, "null tensor pointer");
+  FA4CP_CHECK_ARG(nranks == 1 || (slots_k && slots_v), "slots are required for nranks > 1");
+  FA4CP_CHECK_ARG(aligned16(q) && aligned16(k) && aligned16(v) && aligned16(out) &&
+                      aligned16(slots_k) && aligned16(slots_v) && slot_stride % 16 == 0,
+                  "tensors, slots and the slot stride must be 16-byte aligned");
+  FA4CP_CHECK_ARG(nranks == 1 || slot_stride >= total * num_heads_kv * int64_t(head_dim) * 2,
+                  "slot stride smaller than one K/V shard");
+  RingFusedParams p{};
+  p.cu = cu;
+  p.out = out;
+  p.lse = lse;
+  p.arrived = arrived;
+  p.arrived_base = arrived_base;
+  p.nseq = nseq;
+  p.Hq = num_heads_q;
+  p.Hkv = num_heads_kv;
+  p.group = num_heads_q / num_heads_kv;
+  p.S = nranks;
+  p.rank = rank;
+  p.in_fmt = dtype == FA4CP_DTYPE_BF16 ? 1 : 0;
+  p.out_bf16 = p.in_fmt;
+  p.scale_log2 = softmax_scale * kLog2e;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (head_dim == 128)
+    return launch_ring_fused<Traits2<128, 128, 2, false>>(q, k, v, slots_k, slots_v, slot_stride,
+                                                          total, max_seqlen, p, st);
+  if (head_dim == 64)
+    return launch_ring_fused<Traits2<64, 128, 3, false>>(q, k, v, slots_k, slots_v, slot_stride,
+                                                         total, max_seqlen, p, st);
+  set_last_error("the ring kernel takes head_dim 64 or 128 (got %d)", head_dim);
   return FA4CP_ERR_UNSUPPORTED;
 }
 

@@ -176,7 +176,18 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, int 
       : "memory");
 }
 
-// Same, with an L2 cache-policy hint (createpolicy result).
+// 4-D form: coordinates (c0 innermost .. c3)
+__device__ __forceinline__ void tma_load_4d_hint(uint32_t dst, const void* tmap, int c0, int c1,
+                                                 int c2, int c3, uint32_t bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar),
+      "l"(policy)
+      : "memory");
+}
+
+// Same (3-D), with an L2 cache-policy hint (createpolicy result).
 __device__ __forceinline__ void tma_load_3d_hint(uint32_t dst, const void* tmap, int c0, int c1,
                                                  int c2, uint32_t bar, uint64_t policy) {
   asm volatile(

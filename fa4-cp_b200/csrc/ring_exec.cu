@@ -88,6 +88,7 @@ struct RingComm {
   cudaEvent_t ev_hop[kMaxRing] = {};   // hop s landed
   cudaEvent_t ev_step[kMaxRing] = {};  // attention of step s done (its K/V slot is free)
   int sm_reserve = kDefaultSmReserve;  // SMs the persistent attention grid leaves to NCCL
+  bool fused = true;                   // copy engine: persistent ring kernel where supported
   // optional timing: 2 timing events per attention launch and per hop, filled in call order
   std::vector<cudaEvent_t> tev, hev;
   int t_used = 0, h_used = 0;
@@ -151,81 +152,83 @@ int nccl_fail(NcclApi* api, const char* what, ncclResult_t r) {
 // ---------------------------------------------------------------------------------------
 // copy-engine transport: the plan
 //
-// Hop g (a counter over all hops of all calls, from 1) carries one K/V shard into the
-// receiver's slot g & 1.  A call with hops g0+1 .. g0+S-1 issues, in this host order:
-//   RECORD start on the compute stream, push(1);
-//   for s = 0 .. S-1:
-//     s > 0:     compute waits ARRIVED >= g0+s;  push(s+1) if s+1 < S
-//     attention of step s on the compute stream (K/V: the caller's for s = 0, else slot g0+s);
-//     RECORD step(s);  s > 0: release(s)
+// Hop g (a counter over all hops of all calls since the area was allocated, from 1) carries
+// one K/V shard; a call's hops g0+1 .. g0+S-1 land in the receiver's slots 0 .. S-2 (one
+// slot per hop, so nothing is reused inside a call).  One call issues, in this host order:
+//   RECORD start on the compute stream;
+//   push(1) .. push(S-1), where push(s) (K on copy stream 1, V on copy stream 2) waits for
+//     its data (the caller's stream for s = 1, else own ARRIVED >= g0+s-1), waits until the
+//     right neighbour released its slot s-1 from the previous call (own FREED >= g0+s-(S-1),
+//     once a previous call exists), copies into that slot, then writes the right neighbour's
+//     ARRIVED = g0+s;
+//   the attention: per-step launches (step s > 0 after own ARRIVED >= g0+s on the compute
+//     stream) or one persistent ring kernel that waits for ARRIVED >= g0+s itself before it
+//     reads slot s-1;
+//   RECORD done; the release stream waits for the attention and the last push (which read
+//     the own slots), then writes the left neighbour's FREED = g0+S-1;
 //   the compute stream joins the copy and release streams.
-// push(s) (K on copy stream 1, V on copy stream 2): wait for the data (the caller's stream
-// for s = 1, else ARRIVED >= g0+s-1), wait FREED >= g0+s-2 (the right neighbour released
-// the previous use of the slot), copy into the right neighbour's slot g0+s, then write its
-// ARRIVED = g0+s.  release(s) (release stream): after attention s and push(s+1), write
-// the left neighbour's FREED = g0+s.  Every wait depends only on neighbours' earlier
-// iterations, so the plan cannot deadlock even if every stream of a rank ran in host
-// order on one hardware queue.
+// The pushes depend only on the previous call's releases and on earlier hops, never on
+// this call's attention, so the whole rotation runs ahead of the compute, and no wait can
+// close a cycle even if every stream of a rank ran in host order on one hardware queue.
 // ---------------------------------------------------------------------------------------
 enum { FLAG_ARRIVED = 0, FLAG_FREED = 1 };
 enum { PEER_RIGHT = 0, PEER_LEFT = 1 };
 constexpr int EV_START = 0;
-constexpr int ev_step(int s) { return 1 + s; }
-constexpr int ev_vdone(int s) { return 1 + kMaxRing + s; }
-constexpr int ev_push(int s) { return 1 + 2 * kMaxRing + s; }
-constexpr int EV_COPY_END = 1 + 3 * kMaxRing;
-constexpr int EV_REL_END = 2 + 3 * kMaxRing;
-constexpr int EV_COUNT = 3 + 3 * kMaxRing;
+constexpr int EV_DONE = 1;
+constexpr int ev_vdone(int s) { return 2 + s; }
+constexpr int ev_push(int s) { return 2 + kMaxRing + s; }
+constexpr int EV_COPY_END = 2 + 2 * kMaxRing;
+constexpr int EV_REL_END = 3 + 2 * kMaxRing;
+constexpr int EV_COUNT = 4 + 2 * kMaxRing;
 constexpr int64_t kFlagOffset[2] = {0, 128};  // ARRIVED, FREED (own 128-byte lines)
 constexpr int64_t kSlotBase = 4096;           // receive slots start here in the area
 
 using RingOp = fa4cp_ring_op;
 
-void build_ce_plan(int S, int rank, uint64_t g0, std::vector<RingOp>& ops) {
+void build_ce_plan(int S, int rank, uint64_t g0, bool fused, std::vector<RingOp>& ops) {
   (void)rank;  // the plan is the same on every rank; peers are implied (left / right)
   ops.clear();
   auto op = [&](int st, int kind, int64_t a = 0, int64_t b = 0, int64_t c = 0) {
     ops.push_back(RingOp{st, kind, a, b, c});
   };
-  auto G = [&](int s) { return int64_t(uint32_t(g0 + uint64_t(s))); };  // flag value of hop
+  auto G = [&](int s) { return int64_t(uint32_t(g0 + uint64_t(s))); };  // counter value
   auto push = [&](int s) {
     for (int st : {ST_COPY_K, ST_COPY_V}) {
       if (s == 1)
         op(st, FA4CP_RING_OP_WAIT_EVENT, EV_START);
       else
         op(st, FA4CP_RING_OP_WAIT_FLAG, FLAG_ARRIVED, G(s - 1));
-      if (g0 + uint64_t(s) >= 3)  // the slot's previous use, hop g-2, must be released
-        op(st, FA4CP_RING_OP_WAIT_FLAG, FLAG_FREED, int64_t(uint32_t(G(s) - 2)));
-      op(st, FA4CP_RING_OP_COPY, st == ST_COPY_K ? 0 : 1, s == 1 ? -1 : G(s - 1), G(s));
+      if (g0 > 0)  // slot s-1 was last filled by the previous call's hop g0+s-(S-1)
+        op(st, FA4CP_RING_OP_WAIT_FLAG, FLAG_FREED, int64_t(uint32_t(G(s) - (S - 1))));
+      op(st, FA4CP_RING_OP_COPY, st == ST_COPY_K ? 0 : 1, s == 1 ? -1 : s - 2, s - 1);
     }
     op(ST_COPY_V, FA4CP_RING_OP_RECORD, ev_vdone(s));
     op(ST_COPY_K, FA4CP_RING_OP_WAIT_EVENT, ev_vdone(s));
     op(ST_COPY_K, FA4CP_RING_OP_WRITE_FLAG, PEER_RIGHT, FLAG_ARRIVED, G(s));
     op(ST_COPY_K, FA4CP_RING_OP_RECORD, ev_push(s));
   };
-  if (S > 1) {
-    op(ST_COMPUTE, FA4CP_RING_OP_RECORD, EV_START);
-    push(1);
+  if (S == 1) {
+    op(ST_COMPUTE, FA4CP_RING_OP_ATTN, 0, -1);
+    return;
   }
-  for (int s = 0; s < S; ++s) {
-    if (s > 0) {
-      op(ST_COMPUTE, FA4CP_RING_OP_WAIT_FLAG, FLAG_ARRIVED, G(s));
-      if (s + 1 < S) push(s + 1);
-    }
-    op(ST_COMPUTE, FA4CP_RING_OP_ATTN, s, s == 0 ? -1 : G(s));
-    op(ST_COMPUTE, FA4CP_RING_OP_RECORD, ev_step(s));
-    if (s > 0) {
-      op(ST_RELEASE, FA4CP_RING_OP_WAIT_EVENT, ev_step(s));
-      if (s + 1 < S) op(ST_RELEASE, FA4CP_RING_OP_WAIT_EVENT, ev_push(s + 1));
-      op(ST_RELEASE, FA4CP_RING_OP_WRITE_FLAG, PEER_LEFT, FLAG_FREED, G(s));
+  op(ST_COMPUTE, FA4CP_RING_OP_RECORD, EV_START);
+  for (int s = 1; s < S; ++s) push(s);
+  if (fused) {
+    op(ST_COMPUTE, FA4CP_RING_OP_ATTN_FUSED, S, G(0));
+  } else {
+    for (int s = 0; s < S; ++s) {
+      if (s > 0) op(ST_COMPUTE, FA4CP_RING_OP_WAIT_FLAG, FLAG_ARRIVED, G(s));
+      op(ST_COMPUTE, FA4CP_RING_OP_ATTN, s, s == 0 ? -1 : s - 1);
     }
   }
-  if (S > 1) {
-    op(ST_COPY_K, FA4CP_RING_OP_RECORD, EV_COPY_END);
-    op(ST_RELEASE, FA4CP_RING_OP_RECORD, EV_REL_END);
-    op(ST_COMPUTE, FA4CP_RING_OP_WAIT_EVENT, EV_COPY_END);
-    op(ST_COMPUTE, FA4CP_RING_OP_WAIT_EVENT, EV_REL_END);
-  }
+  op(ST_COMPUTE, FA4CP_RING_OP_RECORD, EV_DONE);
+  op(ST_RELEASE, FA4CP_RING_OP_WAIT_EVENT, EV_DONE);
+  op(ST_RELEASE, FA4CP_RING_OP_WAIT_EVENT, ev_push(S - 1));
+  op(ST_RELEASE, FA4CP_RING_OP_WRITE_FLAG, PEER_LEFT, FLAG_FREED, G(S - 1));
+  op(ST_COPY_K, FA4CP_RING_OP_RECORD, EV_COPY_END);
+  op(ST_RELEASE, FA4CP_RING_OP_RECORD, EV_REL_END);
+  op(ST_COMPUTE, FA4CP_RING_OP_WAIT_EVENT, EV_COPY_END);
+  op(ST_COMPUTE, FA4CP_RING_OP_WAIT_EVENT, EV_REL_END);
 }
 
 using StreamWaitValue32Fn = CUresult (*)(CUstream, CUdeviceptr, cuuint32_t, unsigned int);
@@ -258,13 +261,13 @@ StreamMemOps* stream_mem_ops() {
 
 using namespace fa4cp;
 
-extern "C" int fa4cp_ring_ce_plan(int32_t nranks, int32_t rank, int64_t g0, fa4cp_ring_op* ops,
-                                  int32_t capacity) {
+extern "C" int fa4cp_ring_ce_plan(int32_t nranks, int32_t rank, int64_t g0, int32_t fused,
+                                  fa4cp_ring_op* ops, int32_t capacity) {
   FA4CP_CHECK_ARG(g0 >= 0, "negative hop count");
   FA4CP_CHECK_ARG(nranks >= 1 && nranks <= kMaxRing && rank >= 0 && rank < nranks,
                   "bad ring size %d / rank %d", nranks, rank);
   std::vector<RingOp> plan;
-  build_ce_plan(nranks, rank, uint64_t(g0), plan);
+  build_ce_plan(nranks, rank, uint64_t(g0), fused != 0, plan);
   FA4CP_CHECK_ARG(ops == nullptr || capacity >= int32_t(plan.size()),
                   "capacity %d < %d plan entries", capacity, int(plan.size()));
   if (ops != nullptr) memcpy(ops, plan.data(), plan.size() * sizeof(RingOp));
@@ -353,7 +356,8 @@ extern "C" int fa4cp_ring_ipc_alloc(int64_t handle, int64_t kv_capacity, uint8_t
   }
   const int64_t cap = (kv_capacity + 255) / 256 * 256;
   void* p = nullptr;
-  FA4CP_CHECK_CUDA(cudaMalloc(&p, size_t(kSlotBase + 4 * cap)));
+  const int64_t nslots = rc->nranks > 1 ? rc->nranks - 1 : 1;
+  FA4CP_CHECK_CUDA(cudaMalloc(&p, size_t(kSlotBase + 2 * nslots * cap)));
   rc->area = static_cast<uint8_t*>(p);
   rc->kv_cap = cap;
   rc->hops = 0;
@@ -425,6 +429,12 @@ extern "C" int fa4cp_ring_timing(int64_t handle, int32_t max_launches) {
   return FA4CP_OK;
 }
 
+extern "C" int fa4cp_ring_set_fused(int64_t handle, int32_t fused) {
+  FA4CP_CHECK_ARG(handle != 0, "null ring handle");
+  reinterpret_cast<RingComm*>(handle)->fused = fused != 0;
+  return FA4CP_OK;
+}
+
 extern "C" int fa4cp_ring_set_sm_reserve(int64_t handle, int32_t sm_reserve) {
   FA4CP_CHECK_ARG(handle != 0, "null ring handle");
   FA4CP_CHECK_ARG(sm_reserve >= 0 && sm_reserve <= 64, "sm_reserve %d out of [0, 64]", sm_reserve);
@@ -479,19 +489,21 @@ namespace {
 
 // Issues the copy-engine plan of one call (build_ce_plan) on the caller's stream `st` and
 // the ring's copy / release streams.
-template <class AttnStep>
-int run_ce(RingComm* rc, AttnStep& attn_step, const void* k, const void* v, int64_t kv_bytes,
-           cudaStream_t st) {
+template <class AttnStep, class AttnFused>
+int run_ce(RingComm* rc, AttnStep& attn_step, AttnFused* attn_fused, const void* k,
+           const void* v, int64_t kv_bytes, cudaStream_t st) {
   FA4CP_CHECK_ARG(kv_bytes <= rc->kv_cap, "K/V shard of %lld bytes exceeds the receive slots "
                   "(%lld bytes; reallocate with fa4cp_ring_ipc_alloc)",
                   static_cast<long long>(kv_bytes), static_cast<long long>(rc->kv_cap));
   StreamMemOps* mem = stream_mem_ops();
   FA4CP_CHECK_ARG(mem != nullptr, "stream memory operations are not available");
   std::vector<RingOp> plan;
-  build_ce_plan(rc->nranks, rc->rank, rc->hops, plan);
+  build_ce_plan(rc->nranks, rc->rank, rc->hops, attn_fused != nullptr, plan);
   cudaStream_t streams[ST_COUNT] = {st, rc->cstream[1], rc->cstream[2], rc->cstream[3]};
-  auto slot = [&](uint8_t* area, int64_t hop, int64_t part) {
-    return area + kSlotBase + (hop & 1) * 2 * rc->kv_cap + part * rc->kv_cap;
+  const int64_t nslots = rc->nranks - 1;
+  // K slots 0 .. nslots-1, then V slots
+  auto slot = [&](uint8_t* area, int64_t idx, int64_t part) {
+    return area + kSlotBase + (part * nslots + idx) * rc->kv_cap;
   };
   auto flag = [&](uint8_t* area, int64_t which) {
     return reinterpret_cast<CUdeviceptr>(area + kFlagOffset[which]);
@@ -532,6 +544,13 @@ int run_ce(RingComm* rc, AttnStep& attn_step, const void* k, const void* v, int6
         const void* kk = o.b < 0 ? k : slot(rc->area, o.b, 0);
         const void* vv = o.b < 0 ? v : slot(rc->area, o.b, 1);
         int r = attn_step(int(o.a), kk, vv);
+        if (r != FA4CP_OK) return r;
+        break;
+      }
+      case FA4CP_RING_OP_ATTN_FUSED: {
+        int r = (*attn_fused)(slot(rc->area, 0, 0), slot(rc->area, 0, 1), rc->kv_cap,
+                              reinterpret_cast<const uint32_t*>(rc->area + kFlagOffset[FLAG_ARRIVED]),
+                              uint32_t(o.b));
         if (r != FA4CP_OK) return r;
         break;
       }
@@ -596,8 +615,24 @@ extern "C" int fa4cp_ring_attn_fwd(int64_t handle, const void* q, const void* k,
     return FA4CP_OK;
   };
 
-  if (S == 1) return attn_step(0, k, v);
-  if (rc->ce) return run_ce(rc, attn_step, k, v, kv_bytes, st);
+  // the persistent ring kernel: every step in one launch (f16 / bf16, D 64 or 128)
+  auto attn_fused = [&](const void* sk, const void* sv, int64_t stride, const uint32_t* arrived,
+                        uint32_t base) -> int {
+    const bool timed = rc->t_used < int(rc->tev.size() / 2);
+    if (timed) FA4CP_CHECK_CUDA(cudaEventRecord(rc->tev[2 * rc->t_used], st));
+    int r = fa4cp_ring_attn_fused(q, k, v, sk, sv, stride, out, lse, cu, nseq, max_seqlen, total,
+                                  num_heads_q, num_heads_kv, head_dim, q_dtype, softmax_scale, S,
+                                  rank, arrived, base, stream);
+    if (r != FA4CP_OK) return r;
+    if (timed) FA4CP_CHECK_CUDA(cudaEventRecord(rc->tev[2 * rc->t_used++ + 1], st));
+    return FA4CP_OK;
+  };
+  const bool fusable = rc->fused && q_dtype == kv_dtype &&
+                       (q_dtype == FA4CP_DTYPE_BF16 || q_dtype == FA4CP_DTYPE_F16) &&
+                       (head_dim == 64 || head_dim == 128);
+  if (S == 1) return fusable ? attn_fused(nullptr, nullptr, 0, nullptr, 0) : attn_step(0, k, v);
+  if (rc->ce)
+    return run_ce(rc, attn_step, fusable ? &attn_fused : nullptr, k, v, kv_bytes, st);
 
   // ---- NCCL transport
   FA4CP_CHECK_ARG(kv_bufs != nullptr && kv_bufs_bytes >= 4 * kv_bytes,

@@ -1,0 +1,501 @@
+// Persistent ring kernel: a rank's whole zig-zag ring forward in one launch.
+//
+// Included into attn_fwd_sm100.cu (inside its anonymous namespace): it shares the two-tile
+// traits, the barrier helpers, the error codes and the device status word of the per-step
+// kernel, whose warp roles, TMEM plan (S0 | S1 | O0 | O1) and softmax it follows.  What
+// changes is the K/V a CTA walks.  A CTA owns two 128-row query tiles of one half (early
+// or late) of one local sequence and one query head; its K/V sequence is the concatenation
+// of every ring step's K/V for those rows, in step order (reference
+// fa4_ring/ring_attention.py:109-166):
+//   step 0      the local K/V, causal (early half: keys [0, h); late half: keys [0, 2h));
+//   1 <= s <= rank   the front half [0, h) of the K/V of rank (rank - s) mod S (slot s-1);
+//   s > rank         all of it, [0, 2h), for late-half rows only.
+// The online softmax runs across the whole sequence, so out and lse are written once: no
+// per-step partial, merge or launch.  Both query tiles of a CTA walk the same number of K/V
+// tiles: at the end of step 0 the lower tile walks one tile past its diagonal, which the
+// causal mask zeroes.  Before the producer's first load of slot s-1 it waits (bounded) for
+// the rank's ARRIVED hop counter to reach arrived_base + s.
+#pragma once
+
+struct RingFusedParams {
+  const int32_t* cu;          // local cu [nseq + 1] (every length even)
+  void* out;                  // [total, Hq, D], q dtype
+  float* lse;                 // [total, Hq]
+  const uint32_t* arrived;    // this rank's ARRIVED counter, or nullptr (all slots present)
+  uint32_t arrived_base;      // slot s-1 is present once *arrived >= arrived_base + s
+  int nseq, Hq, Hkv, group, S, rank;
+  int n_pairs;                // query-tile pairs per half, max over sequences
+  int in_fmt, out_bf16;
+  float scale_log2;
+};
+
+constexpr int kErrArrived = kErrDrain + 1;
+// cross-rank waits allow for host skew between ranks; a dead peer still ends the wait
+constexpr long long kArriveWaitCycles = 20000000000LL;  // ~10 s at 1.9 GHz
+
+// Bounded wait of one thread for a hop counter written by a peer GPU (a stream write through
+// NVLink): acquire at system scope, then order the CTA's later async-proxy (TMA) reads of
+// the slot after it.
+__device__ __forceinline__ bool wait_arrived(const uint32_t* ctr, uint32_t target,
+                                             volatile int* abort, int* status) {
+  const long long t0 = clock64();
+  for (uint32_t it = 0;; ++it) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
+    if (int32_t(v - target) >= 0) {
+      asm volatile("fence.proxy.async.global;" ::: "memory");
+      return true;
+    }
+    if (*abort) return false;
+    if ((it & 15u) == 0 && *reinterpret_cast<volatile int*>(status) != 0) {
+      *abort = 1;
+      return false;
+    }
+    if (clock64() - t0 > kArriveWaitCycles) {
+      *abort = 1;
+      atomicCAS(status, 0, kErrArrived);
+      return false;
+    }
+    __nanosleep(256);
+  }
+}
+
+struct RingTile {
+  int seq, half, pair, head, kvh;
+};
+
+// CTA order: pair slots over both halves by decreasing work -- late-half pairs (latest
+// first), then early-half pairs -- in chunks of kQtileChunk; inside a chunk by sequence,
+// kv head, pair, query head of the GQA group (the kv-head grouping keeps the K/V of the CTAs
+// in flight in L2).
+__device__ __forceinline__ bool ring_tile(const RingFusedParams& p, RingTile& w) {
+  const int n_q = 2 * p.n_pairs;
+  const int ch = min(kQtileChunk, n_q);
+  const int per_seq = ch * p.Hq;
+  const int per_chunk = per_seq * p.nseq;
+  const int L = int(blockIdx.x);
+  const int chunk = L / per_chunk;
+  int r = L - chunk * per_chunk;
+  const int seq = r / per_seq;
+  r -= seq * per_seq;
+  const int kvh = r / (ch * p.group);
+  const int r2 = r - kvh * (ch * p.group);
+  const int qd = chunk * ch + r2 / p.group;
+  if (qd >= n_q) return false;
+  w.seq = seq;
+  w.half = qd < p.n_pairs ? 1 : 0;
+  w.pair = p.n_pairs - 1 - (qd % p.n_pairs);
+  w.head = kvh * p.group + r2 % p.group;
+  w.kvh = kvh;
+  return true;
+}
+
+inline unsigned ring_grid(int n_pairs, int Hq, int nseq) {
+  const int n_q = 2 * n_pairs;
+  const int ch = n_q < kQtileChunk ? n_q : kQtileChunk;
+  return unsigned((n_q + ch - 1) / ch * ch * Hq * nseq);
+}
+
+// K/V geometry of one CTA: step 0 (local, causal) then steps 1 .. S-1
+struct RingSegs {
+  int a, hh, half;      // sequence start, half length, 0 early / 1 late
+  int k0_len, diag;     // step 0: keys [0, k0_len), key j visible to row i iff j <= i + diag
+  int n0;               // K/V tiles of step 0 (up to the pair's last row)
+  int S, rank;
+  __device__ int len(int s) const {
+    if (s == 0) return k0_len;
+    return s <= rank ? hh : (half ? 2 * hh : 0);
+  }
+  __device__ int tiles(int s, int BN) const { return s == 0 ? n0 : (len(s) + BN - 1) / BN; }
+};
+
+// Walks the flat K/V tile index j through the steps (j only grows).
+struct SegCursor {
+  int s = 0, first = 0, count = 0;
+  __device__ void start(const RingSegs& g, int BN) { s = 0; first = 0; count = g.tiles(0, BN); }
+  __device__ void seek(const RingSegs& g, int j, int BN) {
+    while (j >= first + count) {
+      first += count;
+      ++s;
+      count = g.tiles(s, BN);
+    }
+  }
+};
+
+template <class TR>
+__global__ void __launch_bounds__(TR::THREADS, 1)
+    ring_fused_kernel(const __grid_constant__ CUtensorMap tmQ,
+                      const __grid_constant__ CUtensorMap tmK0,
+                      const __grid_constant__ CUtensorMap tmV0,
+                      const __grid_constant__ CUtensorMap tmKs,
+                      const __grid_constant__ CUtensorMap tmVs, const RingFusedParams p) {
+  static_assert(!TR::FP8 && !TR::PERSISTENT, "the ring kernel is the f16/bf16 one-tile form");
+  constexpr int D = TR::D, BN = TR::BN, ST = TR::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  RingTile w;
+  if (!ring_tile(p, w)) return;  // uniform for the whole CTA
+  RingSegs g;
+  g.a = p.cu[w.seq];
+  const int L = p.cu[w.seq + 1] - g.a;
+  g.hh = L / 2;
+  g.half = w.half;
+  g.S = p.S;
+  g.rank = p.rank;
+  const int q_start = g.a + w.half * g.hh;
+  const int q_len = w.half ? L - g.hh : g.hh;
+  const int q0 = w.pair * 2 * BM;
+  if (q0 >= q_len) return;  // uniform, before any set-up
+  int rows_t[2];
+#pragma unroll
+  for (int t = 0; t < 2; ++t) rows_t[t] = max(0, min(BM, q_len - (q0 + t * BM)));
+  g.k0_len = w.half ? L : g.hh;
+  g.diag = g.k0_len - q_len;
+  const int kv_end0 = min(g.k0_len, q0 + rows_t[0] + rows_t[1] + g.diag);
+  g.n0 = (kv_end0 + BN - 1) / BN;
+  int n = 0;
+  for (int s = 0; s < p.S; ++s) n += g.tiles(s, BN);
+  int n_t[2] = {rows_t[0] > 0 ? n : 0, rows_t[1] > 0 ? n : 0};
+
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TR::OFF_BAR);
+  const uint32_t bar0 = smem_u32(bars);
+  auto BAR = [&](int i) -> uint32_t { return bar0 + 8u * uint32_t(i); };
+  const uint32_t q_full = BAR(0);
+  auto k_full = [&](int s) { return BAR(1 + s); };
+  auto k_empty = [&](int s) { return BAR(1 + ST + s); };
+  auto v_full = [&](int s) { return BAR(1 + 2 * ST + s); };
+  auto v_empty = [&](int s) { return BAR(1 + 3 * ST + s); };
+  auto s_full = [&](int t) { return BAR(1 + 4 * ST + t); };
+  auto o_done = [&](int t) { return BAR(3 + 4 * ST + t); };
+  const uint32_t td_bar = BAR(5 + 4 * ST);
+  auto p_full = [&](int t) { return BAR(9 + 4 * ST + t * TR::P_SPLIT); };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + TR::NUM_BARS);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* status = &g_attn_status;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(k_full(s), 1);
+      mbar_init(k_empty(s), 1);
+      mbar_init(v_full(s), 1);
+      mbar_init(v_empty(s), 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(s_full(t), 1);
+      mbar_init(p_full(t), 128);
+      mbar_init(o_done(t), 1);
+    }
+    mbar_init(td_bar, 1);
+    *abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 8 && lane == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK0);
+    tma_prefetch_desc(&tmV0);
+    tma_prefetch_desc(&tmKs);
+    tma_prefetch_desc(&tmVs);
+  }
+  if (warp == 9) {
+    tmem_alloc(smem_u32(tmem_slot), TR::TM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp >= 8) {
+   setmaxnreg_dec<TR::REGS_PRODUCER>();
+   if (warp == 8) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      const uint64_t pol_kv = policy_evict_last();
+      int last_k[ST], last_v[ST];
+      for (int s = 0; s < ST; ++s) last_k[s] = last_v[s] = -1;
+      const int nmax = max(n_t[0], n_t[1]);
+      mbar_arrive_expect_tx(q_full, 2 * TR::Q_TILE_BYTES);
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int c = 0; c < TR::NCH; ++c)
+          tma_load_3d(smem_u32(smem + TR::OFF_Q + t * TR::Q_TILE_BYTES + c * TR::Q_CHUNK_BYTES),
+                      &tmQ, c * TR::CHUNK, w.head, q_start + q0 + t * BM, q_full);
+      SegCursor cur;
+      cur.start(g, BN);
+      int waited = 0;  // highest step whose slot is known present
+      for (int j = 0; j < nmax; ++j) {
+        cur.seek(g, j, BN);
+        const int s = j % ST, ph = (j / ST) & 1;
+        const int row = g.a + (j - cur.first) * BN;
+        if (cur.s > waited) {
+          if (p.arrived != nullptr &&
+              !wait_arrived(p.arrived, p.arrived_base + uint32_t(cur.s), abort, status))
+            break;
+          waited = cur.s;
+        }
+        if (j >= ST && !mbar_wait(k_empty(s), ph ^ 1, abort, kErrKEmpty, status)) break;
+        mbar_arrive_expect_tx(k_full(s), TR::KV_BYTES);
+#pragma unroll
+        for (int c = 0; c < TR::NCH; ++c) {
+          const uint32_t dst = smem_u32(smem + TR::OFF_K + s * TR::KV_BYTES + c * TR::KV_CHUNK_BYTES);
+          if (cur.s == 0)
+            tma_load_3d_hint(dst, &tmK0, c * TR::CHUNK, w.kvh, row, k_full(s), pol_kv);
+          else
+            tma_load_4d_hint(dst, &tmKs, c * TR::CHUNK, w.kvh, row, cur.s - 1, k_full(s), pol_kv);
+        }
+        last_k[s] = j;
+        if (j >= ST && !mbar_wait(v_empty(s), ph ^ 1, abort, kErrVEmpty, status)) break;
+        mbar_arrive_expect_tx(v_full(s), TR::KV_BYTES);
+#pragma unroll
+        for (int c = 0; c < TR::NCH; ++c) {
+          const uint32_t dst = smem_u32(smem + TR::OFF_V + s * TR::KV_BYTES + c * TR::KV_CHUNK_BYTES);
+          if (cur.s == 0)
+            tma_load_3d_hint(dst, &tmV0, c * TR::CHUNK, w.kvh, row, v_full(s), pol_kv);
+          else
+            tma_load_4d_hint(dst, &tmVs, c * TR::CHUNK, w.kvh, row, cur.s - 1, v_full(s), pol_kv);
+        }
+        last_v[s] = j;
+      }
+      // every copy this thread issued has landed before it leaves its role
+      mbar_wait_drain(q_full, 0, kErrDrain, status);
+      for (int s = 0; s < ST; ++s) {
+        if (last_k[s] >= 0) mbar_wait_drain(k_full(s), (last_k[s] / ST) & 1, kErrDrain, status);
+        if (last_v[s] >= 0) mbar_wait_drain(v_full(s), (last_v[s] / ST) & 1, kErrDrain, status);
+      }
+    }
+   } else if (warp == 9) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc_qk = make_idesc(BM, BN, p.in_fmt, p.in_fmt, 0, 0);
+      const uint32_t idesc_pv = make_idesc(BM, D, p.in_fmt, p.in_fmt, 0, 1);
+      auto issue_s = [&](int t, int stage) {
+        const uint32_t sQ = smem_u32(smem + TR::OFF_Q + t * TR::Q_TILE_BYTES);
+        const uint32_t sK = smem_u32(smem + TR::OFF_K + stage * TR::KV_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < D / TR::MMA_K; ++kk) {
+          const int off = kk * 32;  // bytes along D of this K-step
+          const uint32_t ca = (off / 128) * TR::Q_CHUNK_BYTES + (off % 128);
+          const uint32_t cb = (off / 128) * TR::KV_CHUNK_BYTES + (off % 128);
+          mma_f16_ss(tmem + uint32_t(TR::tm_s(t)), make_desc_sw128(sQ + ca, 16, 1024),
+                     make_desc_sw128(sK + cb, 16, 1024), idesc_qk, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(s_full(t));
+      };
+      auto issue_pv = [&](int t, int stage, bool first) {
+        const uint32_t sV = smem_u32(smem + TR::OFF_V + stage * TR::KV_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < BN / TR::MMA_K; ++kk) {
+          const uint64_t bdesc = make_desc_sw128(sV + kk * TR::MMA_K * 128, TR::KV_CHUNK_BYTES, 1024);
+          mma_f16_ts(tmem + uint32_t(TR::tm_o(t)), tmem + uint32_t(TR::tm_s(t) + kk * 8), bdesc,
+                     idesc_pv, (!first || kk > 0) ? 1u : 0u);
+        }
+      };
+      const int nmax = max(n_t[0], n_t[1]);
+      bool ok = mbar_wait(q_full, 0, abort, kErrQ, status);
+      if (ok) tc_fence_after();
+      if (ok && nmax > 0) {
+        ok = mbar_wait(k_full(0), 0, abort, kErrKFull, status);
+        if (ok) {
+          tc_fence_after();
+          if (n_t[0] > 0) issue_s(0, 0);
+          if (n_t[1] > 0) issue_s(1, 0);
+          tc_commit(k_empty(0));
+        }
+      }
+      for (int j = 0; ok && j < nmax; ++j) {
+        const int s = j % ST;
+        bool v_ready = false, k_next_ready = false;
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          if (j >= n_t[t]) continue;
+          if (!v_ready) {
+            if (!mbar_wait(v_full(s), (j / ST) & 1, abort, kErrVFull, status)) { ok = false; break; }
+            v_ready = true;
+          }
+          if (!mbar_wait(p_full(t), j & 1, abort, kErrPFull, status)) { ok = false; break; }
+          tc_fence_after();
+          issue_pv(t, s, j == 0);
+          tc_commit(o_done(t));
+          if (j + 1 < n_t[t]) {
+            const int s1 = (j + 1) % ST;
+            if (!k_next_ready) {
+              if (!mbar_wait(k_full(s1), ((j + 1) / ST) & 1, abort, kErrKFull, status)) {
+                ok = false;
+                break;
+              }
+              k_next_ready = true;
+              tc_fence_after();
+            }
+            issue_s(t, s1);
+          }
+        }
+        if (!ok) break;
+        tc_commit(v_empty(s));
+        if (k_next_ready) tc_commit(k_empty((j + 1) % ST));
+      }
+      // every MMA issued above has completed before TMEM is released
+      tc_commit(td_bar);
+      mbar_wait_drain(td_bar, 0, kErrDrain, status);
+    }
+   }
+  } else {
+    setmaxnreg_inc<TR::REGS_SOFTMAX>();
+    // ------------------------------------------------------------ softmax + epilogue
+    const int t = warp >> 2;  // query tile of this warpgroup
+    const int wq = warp & 3;
+    const int r = wq * 32 + lane;
+    const uint32_t t_lane = tmem + (uint32_t(wq * 32) << 16);
+    const int nn = n_t[t];
+    if (nn > 0) {
+      const int first = q0 + t * BM;
+      const int key_lim = first + r + g.diag;  // step 0 only
+      const float scale = p.scale_log2;
+      const uint64_t scale2 = f2pack(scale, scale);
+      float m = kNegInf, l = 0.f;
+      bool aborted = false;
+      SegCursor cur;
+      cur.start(g, BN);
+
+      for (int j = 0; j < nn; ++j) {
+        cur.seek(g, j, BN);
+        bool ok = mbar_wait(s_full(t), j & 1, abort, kErrSFull, status);
+        if (!__all_sync(0xffffffffu, ok)) { aborted = true; break; }
+        tc_fence_after();
+        uint32_t sr[BN / 32][32];
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c) tmem_ld32(t_lane + uint32_t(TR::tm_s(t) + c * 32), sr[c]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c) reg_fence32(sr[c]);
+
+        const int kbase = (j - cur.first) * BN;
+        const int seg_len = g.len(cur.s);
+        const bool causal = cur.s == 0;
+        const bool need_mask = (kbase + BN > seg_len) || (causal && kbase + BN - 1 > first + g.diag);
+        if (need_mask) {
+#pragma unroll
+          for (int c = 0; c < BN / 32; ++c)
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              const int key = kbase + c * 32 + e;
+              if (key >= seg_len || (causal && key > key_lim)) sr[c][e] = __float_as_uint(kNegInf);
+            }
+        }
+        float mx4[4] = {kNegInf, kNegInf, kNegInf, kNegInf};
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c)
+#pragma unroll
+          for (int e = 0; e < 32; e += 2)
+            mx4[c] = fmax3(mx4[c], __uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1]));
+        const float mx = fmax3(fmaxf(mx4[0], mx4[1]), mx4[2], mx4[3]);
+        const float m_new = fmaxf(m, mx);
+        if (j == 0) {
+          m = m_new;
+        } else {
+          const bool need = (m_new - m) * scale > kRescaleThreshold;
+          if (__any_sync(0xffffffffu, need)) {
+            // PV_t(j-1) is complete: S_t(j) was issued after it and has completed.
+            const float f = need ? ex2_approx((m - m_new) * scale) : 1.0f;
+            if (need) { l *= f; m = m_new; }
+            const uint64_t f2 = f2pack(f, f);
+#pragma unroll 1
+            for (int c = 0; c < D / 32; ++c) {
+              uint32_t o[32];
+              tmem_ld32(t_lane + uint32_t(TR::tm_o(t) + c * 32), o);
+              tmem_wait_ld();
+              reg_fence32(o);
+#pragma unroll
+              for (int e = 0; e < 32; e += 2) {
+                const uint64_t v = fmul2(f2pack(__uint_as_float(o[e]), __uint_as_float(o[e + 1])), f2);
+                o[e] = __float_as_uint(f2lo(v));
+                o[e + 1] = __float_as_uint(f2hi(v));
+              }
+              tmem_st32(t_lane + uint32_t(TR::tm_o(t) + c * 32), o);
+            }
+            tmem_wait_st();
+          }
+        }
+        const float neg_m = (m == kNegInf) ? 0.f : -m * scale;
+        const uint64_t negm2 = f2pack(neg_m, neg_m);
+        uint64_t rs2[2] = {0ull, 0ull};
+        // P in 64-key halves: exps of a half are kept (as fp32 bits, in place of S) for the
+        // row sum, which is added up after P has been handed to the MMA warp
+#pragma unroll
+        for (int half = 0; half < BN / 64; ++half) {
+          uint32_t pw[32];
+#pragma unroll
+          for (int e = 0; e < 64; e += 2) {
+            const int c = half * 2 + (e >> 5), ee = e & 31;
+            const uint64_t a = ffma2(f2pack(__uint_as_float(sr[c][ee]), __uint_as_float(sr[c][ee + 1])), scale2, negm2);
+            const uint64_t ex = exp2_pair<TR>(half * 32 + (e >> 1), a);
+            const float x0 = f2lo(ex), x1 = f2hi(ex);
+            sr[c][ee] = __float_as_uint(x0);
+            sr[c][ee + 1] = __float_as_uint(x1);
+            pw[e >> 1] = p.in_fmt ? pack_bf16x2(x0, x1) : pack_f16x2(x0, x1);
+          }
+          tmem_st32(t_lane + uint32_t(TR::tm_s(t) + half * 32), pw);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(p_full(t));
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c)
+#pragma unroll
+          for (int e = 0; e < 32; e += 4) {
+            rs2[0] = fadd2(rs2[0], f2pack(__uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1])));
+            rs2[1] = fadd2(rs2[1], f2pack(__uint_as_float(sr[c][e + 2]), __uint_as_float(sr[c][e + 3])));
+          }
+        const uint64_t rs = fadd2(rs2[0], rs2[1]);
+        l += f2lo(rs) + f2hi(rs);
+      }
+
+      // ---------------------------------------------------------- epilogue
+      if (!aborted) {
+        bool ok = mbar_wait(o_done(t), (nn - 1) & 1, abort, kErrODone, status);
+        aborted = !__all_sync(0xffffffffu, ok);
+      }
+      if (!aborted) {
+        tc_fence_after();
+        const bool valid = r < rows_t[t];
+        const int64_t grow = int64_t(q_start) + first + r;
+        const bool any_key = (m != kNegInf) && (l > 0.f);
+        const float inv_l = any_key ? 1.0f / l : 0.f;
+        uint8_t* orow = static_cast<uint8_t*>(p.out) + (grow * p.Hq + w.head) * int64_t(D) * 2;
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(t_lane + uint32_t(TR::tm_o(t) + c * 32), o);
+          tmem_wait_ld();
+          reg_fence32(o);
+          if (valid) {
+            uint4* dst = reinterpret_cast<uint4*>(orow + c * 64);
+#pragma unroll
+            for (int v4 = 0; v4 < 4; ++v4) {
+              uint32_t wd[4];
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const float f0 = __uint_as_float(o[v4 * 8 + 2 * i]) * inv_l;
+                const float f1 = __uint_as_float(o[v4 * 8 + 2 * i + 1]) * inv_l;
+                wd[i] = p.out_bf16 ? pack_bf16x2(f0, f1) : pack_f16x2(f0, f1);
+              }
+              dst[v4] = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+            }
+          }
+        }
+        if (valid)
+          p.lse[grow * p.Hq + w.head] =
+              any_key ? (m * scale + lg2_approx(l)) * kLn2 : kNegInf;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 9) tmem_dealloc(tmem, TR::TM_COLS);
+}

@@ -236,6 +236,15 @@ class NativeRing:
 
         _lib.check(self.lib.fa4cp_ring_timing(self.handle, int(max_launches)), "ring_timing")
 
+    def set_fused(self, fused: bool) -> None:
+        """Whole forward in one launch of the persistent ring kernel where it applies."""
+        from . import _lib
+
+        if getattr(self, "_fused", None) != bool(fused):
+            _lib.check(self.lib.fa4cp_ring_set_fused(self.handle, int(bool(fused))),
+                       "ring_set_fused")
+            self._fused = bool(fused)
+
     def set_sm_reserve(self, n: int) -> None:
         """SMs the persistent attention grid leaves free for the hop's NCCL kernel."""
         from . import _lib

@@ -137,6 +137,9 @@ NATIVE_EXECUTOR = True
 # K/V transport of the native executor: "copy_engine" (NVLink copies + stream counters, no
 # SM used) or "nccl" (send/recv on the executor's own communicator)
 RING_TRANSPORT = "copy_engine"
+# copy engine: run the whole forward as one launch of the persistent ring kernel where it
+# applies (f16 / bf16, D 64 or 128); False keeps one attention launch per step
+RING_FUSED = True
 
 
 def use_native_executor(group=None) -> bool:
@@ -173,6 +176,7 @@ def _native_forward(q, k, v, cfg: RingConfig, group, *, cu, nseq, max_seqlen,
         bufs = torch.empty(4 * kv_bytes, dtype=torch.uint8, device=dev)  # two [K | V] slots
     else:
         ring.ensure_capacity(kv_bytes)
+        ring.set_fused(RING_FUSED)
     ws = None
     if is_mixed(q, k):
         nbytes = _lib.load().fa4cp_attn_kv8_workspace_bytes(T, Hkv, D)
@@ -180,7 +184,9 @@ def _native_forward(q, k, v, cfg: RingConfig, group, *, cu, nseq, max_seqlen,
     ring.forward(
         q, k, v, out, lse, cu, nseq=nseq, max_seqlen=max_seqlen, softmax_scale=scale,
         q_descale=qd, k_descales=kds, v_descales=vds, kv_bufs=bufs, workspace=ws)
-    _lib.count_launches(S * (3 if ws is not None else 1))
+    fused = (ring.transport == "copy_engine" and RING_FUSED and q.dtype == k.dtype
+             and q.dtype in (torch.float16, torch.bfloat16) and D in (64, 128))
+    _lib.count_launches(1 if fused else S * (3 if ws is not None else 1))
     return out
 
 

@@ -259,6 +259,9 @@ FA4CP_API int fa4cp_local_cu(const int32_t* full_cu, int32_t nseq, int32_t cp_si
  *   every rank before the process group is torn down.
  * fa4cp_ring_set_sm_reserve: SMs (0..64, default 8) the persistent attention grid leaves
  *   free during a ring call, so that the hop's NCCL kernel runs beside it.
+ * fa4cp_ring_set_fused: 1 (default) runs the whole forward as one launch of the persistent
+ *   ring kernel (fa4cp_ring_attn_fused) where it applies (copy-engine transport or a single
+ *   rank; f16 / bf16; D 64 or 128); 0 keeps one attention launch per step.
  * fa4cp_ring_timing: time the next `max_launches` attention launches and hops (0 = off) with
  *   CUDA events; fa4cp_ring_timeline writes (start, end) pairs in ms relative to the first
  *   timed launch's start into HOST float arrays (attention launches and hops, in issue order,
@@ -279,15 +282,18 @@ FA4CP_API int fa4cp_local_cu(const int32_t* full_cu, int32_t nseq, int32_t cp_si
  */
 /*
  * Copy-engine transport of the ring executor (used when fa4cp_ring_ipc_open has run):
- * fa4cp_ring_ipc_alloc: (re)allocates this rank's receive area (two slots of K and V of
- *   kv_capacity bytes each, plus hop counters) with cudaMalloc and writes its 64-byte CUDA
- *   IPC handle to ipc_out (HOST).  Synchronises the device; resets the hop count.
+ * fa4cp_ring_ipc_alloc: (re)allocates this rank's receive area with cudaMalloc: a 4 KiB
+ *   header (32-bit hop counters ARRIVED at byte 0 and FREED at byte 128), then nranks-1 K
+ *   slots and nranks-1 V slots of kv_capacity bytes each (rounded up to 256; slot i of hop i+1
+ *   of a call); writes its 64-byte CUDA IPC handle to ipc_out (HOST).  Synchronises the
+ *   device; resets the hop count.
  * fa4cp_ring_ipc_open: maps the left and right neighbours' areas (HOST 64-byte handles; the
  *   same handle for both when nranks == 2).  fa4cp_ring_ipc_close unmaps them.
  * Every rank calls alloc, exchanges handles, and opens, with a barrier of the cp group
  * before freeing (close, barrier, alloc) and after opening; all ranks use the same capacity.
  * fa4cp_ring_ce_plan: the ordered operations one call issues (host only, no GPU needed),
- *   for hops g0+1 .. g0+nranks-1; returns the count (ops may be NULL to ask for it).
+ *   for hops g0+1 .. g0+nranks-1, with per-step attention launches (fused 0) or the
+ *   persistent ring kernel (fused 1); returns the count (ops may be NULL to ask for it).
  */
 typedef struct {
   int32_t stream; /* 0 caller's (compute), 1 K copy, 2 V copy, 3 release */
@@ -298,22 +304,49 @@ typedef struct {
 #define FA4CP_RING_OP_WAIT_EVENT 1 /* wait for event a's latest record */
 #define FA4CP_RING_OP_WAIT_FLAG 2  /* wait until own counter a (0 arrived, 1 freed) >= b (cyclic) */
 #define FA4CP_RING_OP_WRITE_FLAG 3 /* write counter b of peer a (0 right, 1 left) := c */
-#define FA4CP_RING_OP_COPY 4       /* part a (0 K, 1 V): src b (-1 caller's, else own slot of
-                                      hop b) -> right neighbour's slot of hop c */
-#define FA4CP_RING_OP_ATTN 5       /* attention of step a on K/V b (-1 caller's, else own slot
-                                      of hop b) */
+#define FA4CP_RING_OP_COPY 4       /* part a (0 K, 1 V): src b (-1 caller's, else own slot b)
+                                      -> right neighbour's slot c */
+#define FA4CP_RING_OP_ATTN 5       /* attention of step a on K/V b (-1 caller's, else own
+                                      slot b) */
+#define FA4CP_RING_OP_ATTN_FUSED 6 /* persistent ring kernel over a steps; before reading
+                                      slot s-1 it waits for own ARRIVED >= b + s */
 FA4CP_API int fa4cp_ring_ipc_alloc(int64_t handle, int64_t kv_capacity, uint8_t* ipc_out);
 FA4CP_API int fa4cp_ring_ipc_open(int64_t handle, const uint8_t* left_ipc,
                                   const uint8_t* right_ipc);
 FA4CP_API int fa4cp_ring_ipc_close(int64_t handle);
-FA4CP_API int fa4cp_ring_ce_plan(int32_t nranks, int32_t rank, int64_t g0, fa4cp_ring_op* ops,
-                                 int32_t capacity);
+FA4CP_API int fa4cp_ring_ce_plan(int32_t nranks, int32_t rank, int64_t g0, int32_t fused,
+                                 fa4cp_ring_op* ops, int32_t capacity);
+
+/*
+ * Persistent ring kernel: the whole zig-zag ring forward of one rank in ONE launch.  Each
+ * CTA owns two 128-row query tiles of one half (early / late) of one local sequence and one
+ * query head, and walks the K/V of every step in order -- step 0 the local K/V (causal),
+ * step s >= 1 the K/V of rank (rank - s) mod nranks in slot s-1 (front half when s <= rank;
+ * all of it, for late-half rows only, when s > rank) -- carrying the online softmax across
+ * steps, so out and lse are written once (no per-step merge).  Before its first read of
+ * slot s-1 a CTA waits (bounded, ~10 s) until *arrived >= arrived_base + s; arrived NULL:
+ * every slot is already filled.
+ * Replaces: the whole step loop of fa4_ring/ring_attention.py:121-172 (attention per step
+ * and the incremental merges of fa4_ring/merge.py:45-64).
+ *   q [total, Hq, D], k/v [total, Hkv, D] local; slots_k / slots_v: slot i at
+ *   slots_k + i * slot_stride bytes, each [total, Hkv, D] (the source's shard, same cu);
+ *   out [total, Hq, D] (q dtype); lse [total, Hq] float32.  f16 / bf16, D 64 or 128.
+ */
+FA4CP_API int fa4cp_ring_attn_fused(const void* q, const void* k, const void* v,
+                                    const void* slots_k, const void* slots_v,
+                                    int64_t slot_stride, void* out, float* lse,
+                                    const int32_t* cu, int32_t nseq, int32_t max_seqlen,
+                                    int64_t total, int32_t num_heads_q, int32_t num_heads_kv,
+                                    int32_t head_dim, int32_t dtype, float softmax_scale,
+                                    int32_t nranks, int32_t rank, const uint32_t* arrived,
+                                    uint32_t arrived_base, void* stream);
 
 FA4CP_API int fa4cp_ring_unique_id(uint8_t* id_out);
 FA4CP_API int fa4cp_ring_comm_init(const uint8_t* id, int32_t nranks, int32_t rank,
                                    int64_t* handle_out);
 FA4CP_API int fa4cp_ring_comm_destroy(int64_t handle);
 FA4CP_API int fa4cp_ring_set_sm_reserve(int64_t handle, int32_t sm_reserve);
+FA4CP_API int fa4cp_ring_set_fused(int64_t handle, int32_t fused);
 FA4CP_API int fa4cp_ring_timing(int64_t handle, int32_t max_launches);
 FA4CP_API int fa4cp_ring_timeline(int64_t handle, float* attn_ms, int32_t max_attn,
                                   float* hop_ms, int32_t max_hops, int32_t* n_attn,

@@ -21,9 +21,11 @@ import pytest
 
 from fa4_ring import _lib
 
-RECORD, WAIT_EVENT, WAIT_FLAG, WRITE_FLAG, COPY, ATTN = range(6)
+RECORD, WAIT_EVENT, WAIT_FLAG, WRITE_FLAG, COPY, ATTN, ATTN_FUSED = range(7)
 ARRIVED, FREED = 0, 1
 RIGHT, LEFT = 0, 1
+# simulator-only expansions of the persistent ring kernel (its in-kernel waits and reads)
+SEG_READ, KERNEL_END = 100, 101
 
 
 class Op(ctypes.Structure):
@@ -31,12 +33,12 @@ class Op(ctypes.Structure):
                 ("b", ctypes.c_int64), ("c", ctypes.c_int64)]
 
 
-def plan(S, rank, g0):
+def plan(S, rank, g0, fused=False):
     lib = _lib.load()
-    n = lib.fa4cp_ring_ce_plan(S, rank, g0, None, 0)
+    n = lib.fa4cp_ring_ce_plan(S, rank, g0, int(fused), None, 0)
     assert n > 0, _lib.last_error()
     buf = (Op * n)()
-    assert lib.fa4cp_ring_ce_plan(S, rank, g0, buf, n) == n
+    assert lib.fa4cp_ring_ce_plan(S, rank, g0, int(fused), buf, n) == n
     return [(o.stream, o.kind, o.a, o.b, o.c) for o in buf]
 
 
@@ -44,22 +46,41 @@ class Part:
     """One K or V part of a receive slot."""
 
     def __init__(self):
-        self.hop = None          # hop whose data the part holds
-        self.tag = None          # (origin rank, call) of that data
+        self.tag = None          # (origin rank, call) of the data it holds
         self.writing = False
         self.readers = 0
-        self.attended = False
-        self.forwarded = False
+        self.attended = True     # an empty slot may be filled
+        self.forwarded = True
         self.needs_fwd = False
 
 
-def simulate(S, calls, seed, serial):
+def expand(ops, kernel_waits=True):
+    """The fused launch as what it does on the compute queue: step 0 on the local K/V, then
+    per step s a wait for ARRIVED >= base + s and the reads of slot s-1, all released at the
+    kernel's end."""
+    out = []
+    for o in ops:
+        st, kind, a, b, c = o
+        if kind == ATTN_FUSED:
+            out.append((st, SEG_READ, 0, -1, 0))
+            for s in range(1, a):
+                if kernel_waits:
+                    out.append((st, WAIT_FLAG, ARRIVED, b + s, 0))
+                out.append((st, SEG_READ, s, s - 1, 0))
+            out.append((st, KERNEL_END, 0, 0, 0))
+        else:
+            out.append(o)
+    return out
+
+
+def simulate(S, calls, seed, serial, fused=False, plan_fn=None, kernel_waits=True):
+    plan_fn = plan_fn or plan
     rng = random.Random(seed)
     ranks = []
     for r in range(S):
         ops = []
         for c in range(calls):
-            for o in plan(S, r, c * (S - 1)):
+            for o in expand(plan_fn(S, r, c * (S - 1), fused), kernel_waits):
                 ops.append((c,) + o)
         # resolve each event wait to the latest record of that event before it (host order)
         last_record, waits_on = {}, {}
@@ -72,11 +93,8 @@ def simulate(S, calls, seed, serial):
         for i, o in enumerate(ops):
             queues.setdefault(0 if serial else o[1], []).append(i)
         ranks.append(dict(ops=ops, waits_on=waits_on, queues=queues, pos={q: 0 for q in queues},
-                          pending={}, done=set(), flags=[0, 0],
-                          slots=[[Part(), Part()], [Part(), Part()]]))
-
-    def step_of(hop, c):
-        return hop - c * (S - 1)
+                          pending={}, done=set(), flags=[0, 0], kernel_reads=[],
+                          slots=[[Part(), Part()] for _ in range(max(S - 1, 1))]))
 
     def runnable(r, q):
         R = ranks[r]
@@ -93,37 +111,39 @@ def simulate(S, calls, seed, serial):
             return R["flags"][a] >= b
         return True
 
+    def read_slot(r, step, idx, c):
+        want = ((r - step) % S, c)
+        if idx < 0:
+            assert step == 0
+            return []
+        parts = ranks[r]["slots"][idx]
+        for p in parts:
+            assert not p.writing and p.tag is not None, "attention reads a slot that is not ready"
+            assert p.tag == want, f"rank {r} step {step} attends {p.tag}, wants {want}"
+            p.readers += 1
+        return parts
+
     def begin(r, i):
         R = ranks[r]
         c, st, kind, a, b, cc = R["ops"][i]
         if kind == COPY:
             if b >= 0:
-                src = R["slots"][b & 1][a]
-                assert src.hop == b and not src.writing, "push reads a slot that is not ready"
+                src = R["slots"][b][a]
+                assert not src.writing and src.tag is not None, "push reads a slot that is not ready"
+                assert src.tag == ((r - (b + 1)) % S, c), "push forwards the wrong shard"
                 tag = src.tag
                 src.readers += 1
             else:
                 tag, src = (r, c), None
-            dst = ranks[(r + 1) % S]["slots"][cc & 1][a]
+            dst = ranks[(r + 1) % S]["slots"][cc][a]
             assert dst.readers == 0 and not dst.writing, "push overwrites a slot in use"
-            assert dst.hop is None or (dst.attended and (dst.forwarded or not dst.needs_fwd)), \
+            assert dst.attended and (dst.forwarded or not dst.needs_fwd), \
                 "push overwrites data not yet attended / forwarded"
-            dst.hop, dst.tag, dst.writing = cc, tag, True
+            dst.tag, dst.writing = tag, True
             dst.attended = dst.forwarded = False
-            dst.needs_fwd = step_of(cc, c) < S - 1
+            dst.needs_fwd = cc + 2 <= S - 1  # step cc+1's data goes on at push cc+2
             return ("copy", src, dst)
-        if kind == ATTN:
-            want = ((r - a) % S, c)
-            if b < 0:
-                assert a == 0
-                return ("attn", [])
-            parts = R["slots"][b & 1]
-            for p in parts:
-                assert p.hop == b and not p.writing, "attention reads a slot that is not ready"
-                assert p.tag == want, f"rank {r} step {a} attends {p.tag}, wants {want}"
-                p.readers += 1
-            return ("attn", parts)
-        return None
+        return ("attn", read_slot(r, a, b, c))
 
     def end(token):
         if token[0] == "copy":
@@ -150,32 +170,60 @@ def simulate(S, calls, seed, serial):
         if kind in (COPY, ATTN):
             R["pending"][q] = (i, begin(r, i))
             return
-        if kind == WRITE_FLAG:
+        if kind == SEG_READ:
+            R["kernel_reads"].append(("attn", read_slot(r, a, b, c)))
+        elif kind == KERNEL_END:
+            if mode == 1 and rng.random() < 0.9:
+                return  # a slow kernel: its reads stay in flight a while longer
+            for token in R["kernel_reads"]:
+                end(token)
+            R["kernel_reads"] = []
+        elif kind == WRITE_FLAG:
             peer = ranks[(r + 1) % S] if a == RIGHT else ranks[(r - 1) % S]
             assert cc >= peer["flags"][b], "counters only grow"
             peer["flags"][b] = cc
         R["done"].add(i)
         R["pos"][q] += 1
 
+    # adversarial timing: per seed, attention (or copies, or one whole rank) is slow, so a
+    # neighbour can run far ahead while a read or write is still in flight
+    mode = seed % 4
+    slow_rank = rng.randrange(S)
+
+    def slow(r, q):
+        R = ranks[r]
+        if mode == 3:
+            return r == slow_rank
+        if q not in R["pending"]:
+            return False
+        kind = R["ops"][R["pending"][q][0]][2]
+        return (mode == 1 and kind == ATTN) or (mode == 2 and kind == COPY)
+
     total = sum(len(R["ops"]) for R in ranks)
     while sum(len(R["done"]) for R in ranks) < total:
         cands = [(r, q) for r in range(S) for q in ranks[r]["queues"] if runnable(r, q)]
-        assert cands, f"deadlock (S={S}, seed={seed}, serial={serial})"
+        assert cands, f"deadlock (S={S}, seed={seed}, serial={serial}, fused={fused})"
+        fast = [x for x in cands if not slow(*x)]
+        if fast and rng.random() < 0.97:
+            cands = fast
         execute(*rng.choice(cands))
     for R in ranks:  # every call attended every step
-        assert sum(1 for o in R["ops"] if o[2] == ATTN) == S * calls
+        n_steps = sum(1 for o in R["ops"] if o[2] in (ATTN, SEG_READ))
+        assert n_steps == S * calls
 
 
+@pytest.mark.parametrize("fused", [False, True])
 @pytest.mark.parametrize("S", [2, 3, 4, 8])
-def test_plan_is_deadlock_free_and_hazard_free(S):
-    for seed in range(40 if S < 8 else 12):
-        simulate(S, calls=3, seed=seed, serial=False)
+def test_plan_is_deadlock_free_and_hazard_free(S, fused):
+    for seed in range(30 if S < 8 else 10):
+        simulate(S, calls=3, seed=seed, serial=False, fused=fused)
 
 
+@pytest.mark.parametrize("fused", [False, True])
 @pytest.mark.parametrize("S", [2, 3, 4, 8])
-def test_plan_with_streams_serialised_in_host_order(S):
-    for seed in range(10):
-        simulate(S, calls=3, seed=seed, serial=True)
+def test_plan_with_streams_serialised_in_host_order(S, fused):
+    for seed in range(8):
+        simulate(S, calls=3, seed=seed, serial=True, fused=fused)
 
 
 def test_plan_shape():
@@ -183,22 +231,33 @@ def test_plan_shape():
     kinds = [o[1] for o in ops]
     assert kinds.count(ATTN) == 4 and kinds.count(COPY) == 6  # 3 hops x (K, V)
     assert [o for o in ops if o[1] == ATTN][0][3] == -1       # step 0 on the caller's K/V
-    assert plan(1, 0, 0) == [(0, ATTN, 0, -1, 0), (0, RECORD, 1, 0, 0)]
+    fused = plan(4, 1, 3, fused=True)
+    assert [o[1] for o in fused].count(ATTN_FUSED) == 1
+    assert [o for o in fused if o[1] == ATTN_FUSED][0][2:4] == (4, 3)
+    assert plan(1, 0, 0) == [(0, ATTN, 0, -1, 0)]
     with pytest.raises(AssertionError):
         plan(65, 0, 0)
 
 
-def test_planted_mistake_is_caught():
-    """A plan without the slot-release wait must fail the simulator (checks the checker)."""
-    real = plan
+@pytest.mark.parametrize("fused,drop", [(False, "freed_wait"), (False, "arrived_wait"),
+                                        (False, "release_after_push"), (True, "freed_wait"),
+                                        (True, "kernel_wait"), (True, "release_after_push")])
+def test_planted_mistake_is_caught(fused, drop):
+    """A plan missing one of its waits must fail the simulator (checks the checker)."""
+    def broken(S, rank, g0, fused):
+        out = []
+        for o in plan(S, rank, g0, fused):
+            st, kind, a, b, c = o
+            if drop == "freed_wait" and kind == WAIT_FLAG and a == FREED:
+                continue
+            if drop == "arrived_wait" and kind == WAIT_FLAG and a == ARRIVED and st == 0:
+                continue
+            if drop == "release_after_push" and kind == WAIT_EVENT and st == 3 and a != 1:
+                continue
+            out.append(o)
+        return out
 
-    def broken(S, rank, g0):
-        return [o for o in real(S, rank, g0) if not (o[1] == WAIT_FLAG and o[2] == FREED)]
-
-    globals()["plan"] = broken
-    try:
-        with pytest.raises(AssertionError):
-            for seed in range(40):
-                simulate(4, calls=3, seed=seed, serial=False)
-    finally:
-        globals()["plan"] = real
+    with pytest.raises(AssertionError):
+        for seed in range(40):
+            simulate(4, calls=3, seed=seed, serial=False, fused=fused, plan_fn=broken,
+                     kernel_waits=drop != "kernel_wait")
