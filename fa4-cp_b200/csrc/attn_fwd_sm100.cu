@@ -520,6 +520,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #ifndef FA4CP_EXP2_EMU_PER_8
 #define FA4CP_EXP2_EMU_PER_8 0
 #endif
+#ifndef FA4CP_EXP2_EMU_FP8
+#define FA4CP_EXP2_EMU_FP8 0
+#endif
 #ifndef FA4CP_P_SPLIT
 #define FA4CP_P_SPLIT 1
 #endif
@@ -530,7 +533,7 @@ struct Traits2 {
   static constexpr bool FP8 = FP8_;
   // of every 8 element pairs of P, this many take exp2 on the FMA pipe (exp2_poly_x2)
   // and the rest on the MUFU unit, balancing the two pipes against the tensor core
-  static constexpr int EXP2_EMU_PER_8 = FA4CP_EXP2_EMU_PER_8;
+  static constexpr int EXP2_EMU_PER_8 = FP8 ? FA4CP_EXP2_EMU_FP8 : FA4CP_EXP2_EMU_PER_8;
   // P is handed to the MMA warp in this many key slices (one barrier each), so the PV
   // MMAs of the first slice run while the softmax warpgroup finishes the rest
   static constexpr int P_SPLIT = FA4CP_P_SPLIT;
@@ -619,7 +622,7 @@ inline int persistent_tiles(int n_qtiles, int Hq, int nseq) {
 // exp2 of one element pair: the pair index decides, at compile time, which pipe does it
 template <class TR>
 __device__ __forceinline__ uint64_t exp2_pair(int pair, uint64_t x) {
-  if ((pair & 7) < TR::EXP2_EMU_PER_8) return exp2_poly_x2(x);
+  if ((pair & 7) < TR::EXP2_EMU_PER_8) return TR::FP8 ? exp2_poly2_x2(x) : exp2_poly_x2(x);
   return f2pack(ex2_approx(f2lo(x)), ex2_approx(f2hi(x)));
 }
 
