@@ -527,7 +527,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #define FA4CP_P_SPLIT 1
 #endif
 
-template <int D_, int BN_, int STAGES_, bool FP8_>
+template <int D_, int BN_, int STAGES_, bool FP8_, int PERSIST_ = -1>
 struct Traits2 {
   static constexpr int D = D_, BN = BN_, STAGES = STAGES_;
   static constexpr bool FP8 = FP8_;
@@ -559,7 +559,7 @@ struct Traits2 {
   // time, so per-CTA set-up and epilogue weigh twice as much); f16/bf16 measured faster with
   // one CTA per tile, where the tile loop has a single trip and its cross-tile state folds
   // away, leaving the softmax warpgroups 216 registers.
-  static constexpr bool PERSISTENT = FP8;
+  static constexpr bool PERSISTENT = PERSIST_ < 0 ? FP8 : PERSIST_ != 0;
   static constexpr int REGS_SOFTMAX = PERSISTENT ? 200 : 216;
   static constexpr int REGS_PRODUCER = PERSISTENT ? 104 : 72;
   static_assert(128 * (2 * REGS_SOFTMAX + REGS_PRODUCER) <= THREADS * 168,
@@ -1349,8 +1349,10 @@ extern "C" int fa4cp_ring_attn_fused(const void* q, const void* k, const void* v
                                      const int32_t* cu, int32_t nseq, int32_t max_seqlen,
                                      int64_t total, int32_t num_heads_q, int32_t num_heads_kv,
                                      int32_t head_dim, int32_t dtype, float softmax_scale,
-                                     int32_t nranks, int32_t rank, const uint32_t* arrived,
-                                     uint32_t arrived_base, void* stream) {
+                                     const float* q_descale, const float* k_descales,
+                                     const float* v_descales, int32_t nranks, int32_t rank,
+                                     const uint32_t* arrived, uint32_t arrived_base,
+                                     void* stream) {
   FA4CP_CHECK_ARG(nseq >= 1 && cu != nullptr, "cu_seqlens must describe >= 1 sequence");
   FA4CP_CHECK_ARG(nranks >= 1 && nranks <= 64 && rank >= 0 && rank < nranks,
                   "bad ring size %d / rank %d", nranks, rank);
@@ -1358,17 +1360,21 @@ extern "C" int fa4cp_ring_attn_fused(const void* q, const void* k, const void* v
                   "H_q=%d not a multiple of H_kv=%d", num_heads_q, num_heads_kv);
   FA4CP_CHECK_ARG(total >= 0 && max_seqlen >= 0, "bad sizes");
   FA4CP_CHECK_ARG(softmax_scale > 0.f, "softmax_scale must be positive");
-  if (dtype != FA4CP_DTYPE_BF16 && dtype != FA4CP_DTYPE_F16) {
-    set_last_error("the ring kernel takes f16 or bf16 (dtype %d)", dtype);
+  const bool fp8 = dtype == FA4CP_DTYPE_E4M3;
+  if (dtype != FA4CP_DTYPE_BF16 && dtype != FA4CP_DTYPE_F16 && !(fp8 && head_dim == 128)) {
+    set_last_error("the ring kernel takes f16 / bf16 (D 64, 128) or e4m3 (D 128); got dtype %d, D %d",
+                   dtype, head_dim);
     return FA4CP_ERR_UNSUPPORTED;
   }
+  FA4CP_CHECK_ARG(fp8 || (!q_descale && !k_descales && !v_descales),
+                  "descales apply to e4m3 inputs only");
   if (total == 0) return FA4CP_OK;
   FA4CP_CHECK_ARG(q && k && v && out && lse, "null tensor pointer");
   FA4CP_CHECK_ARG(nranks == 1 || (slots_k && slots_v), "slots are required for nranks > 1");
   FA4CP_CHECK_ARG(aligned16(q) && aligned16(k) && aligned16(v) && aligned16(out) &&
                       aligned16(slots_k) && aligned16(slots_v) && slot_stride % 16 == 0,
                   "tensors, slots and the slot stride must be 16-byte aligned");
-  FA4CP_CHECK_ARG(nranks == 1 || slot_stride >= total * num_heads_kv * int64_t(head_dim) * 2,
+  FA4CP_CHECK_ARG(nranks == 1 || slot_stride >= total * num_heads_kv * int64_t(head_dim) * (fp8 ? 1 : 2),
                   "slot stride smaller than one K/V shard");
   RingFusedParams p{};
   p.cu = cu;
@@ -1383,9 +1389,15 @@ extern "C" int fa4cp_ring_attn_fused(const void* q, const void* k, const void* v
   p.S = nranks;
   p.rank = rank;
   p.in_fmt = dtype == FA4CP_DTYPE_BF16 ? 1 : 0;
-  p.out_bf16 = p.in_fmt;
+  p.out_bf16 = (dtype == FA4CP_DTYPE_BF16 || fp8) ? 1 : 0;
   p.scale_log2 = softmax_scale * kLog2e;
+  p.q_descale = q_descale;
+  p.k_descales = k_descales;
+  p.v_descales = v_descales;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (fp8)  // one tile per CTA (the ring kernel is not persistent)
+    return launch_ring_fused<Traits2<128, 128, 3, true, 0>>(q, k, v, slots_k, slots_v, slot_stride,
+                                                            total, max_seqlen, p, st);
   if (head_dim == 128)
     return launch_ring_fused<Traits2<128, 128, 2, false>>(q, k, v, slots_k, slots_v, slot_stride,
                                                           total, max_seqlen, p, st);

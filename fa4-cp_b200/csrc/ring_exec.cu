@@ -88,7 +88,7 @@ struct RingComm {
   cudaEvent_t ev_hop[kMaxRing] = {};   // hop s landed
   cudaEvent_t ev_step[kMaxRing] = {};  // attention of step s done (its K/V slot is free)
   int sm_reserve = kDefaultSmReserve;  // SMs the persistent attention grid leaves to NCCL
-  bool fused = true;                   // copy engine: persistent ring kernel where supported
+  int fused = 1;  // persistent ring kernel: 0 never, 1 for f16 / bf16, 2 also for e4m3
   // optional timing: 2 timing events per attention launch and per hop, filled in call order
   std::vector<cudaEvent_t> tev, hev;
   int t_used = 0, h_used = 0;
@@ -431,7 +431,8 @@ extern "C" int fa4cp_ring_timing(int64_t handle, int32_t max_launches) {
 
 extern "C" int fa4cp_ring_set_fused(int64_t handle, int32_t fused) {
   FA4CP_CHECK_ARG(handle != 0, "null ring handle");
-  reinterpret_cast<RingComm*>(handle)->fused = fused != 0;
+  FA4CP_CHECK_ARG(fused >= 0 && fused <= 2, "fused mode %d not in 0..2", fused);
+  reinterpret_cast<RingComm*>(handle)->fused = fused;
   return FA4CP_OK;
 }
 
@@ -615,21 +616,24 @@ extern "C" int fa4cp_ring_attn_fwd(int64_t handle, const void* q, const void* k,
     return FA4CP_OK;
   };
 
-  // the persistent ring kernel: every step in one launch (f16 / bf16, D 64 or 128)
+  // the persistent ring kernel: every step in one launch (f16 / bf16 D 64 or 128, e4m3 D 128)
   auto attn_fused = [&](const void* sk, const void* sv, int64_t stride, const uint32_t* arrived,
                         uint32_t base) -> int {
     const bool timed = rc->t_used < int(rc->tev.size() / 2);
     if (timed) FA4CP_CHECK_CUDA(cudaEventRecord(rc->tev[2 * rc->t_used], st));
     int r = fa4cp_ring_attn_fused(q, k, v, sk, sv, stride, out, lse, cu, nseq, max_seqlen, total,
-                                  num_heads_q, num_heads_kv, head_dim, q_dtype, softmax_scale, S,
-                                  rank, arrived, base, stream);
+                                  num_heads_q, num_heads_kv, head_dim, q_dtype, softmax_scale,
+                                  q_descale, k_descales, v_descales, S, rank, arrived, base,
+                                  stream);
     if (r != FA4CP_OK) return r;
     if (timed) FA4CP_CHECK_CUDA(cudaEventRecord(rc->tev[2 * rc->t_used++ + 1], st));
     return FA4CP_OK;
   };
-  const bool fusable = rc->fused && q_dtype == kv_dtype &&
-                       (q_dtype == FA4CP_DTYPE_BF16 || q_dtype == FA4CP_DTYPE_F16) &&
-                       (head_dim == 64 || head_dim == 128);
+  const bool fusable =
+      q_dtype == kv_dtype &&
+      ((rc->fused >= 1 && (q_dtype == FA4CP_DTYPE_BF16 || q_dtype == FA4CP_DTYPE_F16) &&
+        (head_dim == 64 || head_dim == 128)) ||
+       (rc->fused >= 2 && q_dtype == FA4CP_DTYPE_E4M3 && head_dim == 128));
   if (S == 1) return fusable ? attn_fused(nullptr, nullptr, 0, nullptr, 0) : attn_step(0, k, v);
   if (rc->ce)
     return run_ce(rc, attn_step, fusable ? &attn_fused : nullptr, k, v, kv_bytes, st);

@@ -11,7 +11,11 @@
 //   1 <= s <= rank   the front half [0, h) of the K/V of rank (rank - s) mod S (slot s-1);
 //   s > rank         all of it, [0, 2h), for late-half rows only.
 // The online softmax runs across the whole sequence, so out and lse are written once: no
-// per-step partial, merge or launch.  Both query tiles of a CTA walk the same number of K/V
+// per-step partial, merge or launch.  e4m3: the K and V descales belong to the source rank,
+// so they change at step boundaries.  The running max is kept in scaled (log2) units, and O is
+// kept in units of the current step's V descale: entering a step whose V descale differs,
+// the softmax warps rescale O by old / new (together with any lazy max rescale), and the
+// epilogue multiplies by the last one.  Both query tiles of a CTA walk the same number of K/V
 // tiles: at the end of step 0 the lower tile walks one tile past its diagonal, which the
 // causal mask zeroes.  Before the producer's first load of slot s-1 it waits (bounded) for
 // the rank's ARRIVED hop counter to reach arrived_base + s.
@@ -27,6 +31,10 @@ struct RingFusedParams {
   int n_pairs;                // query-tile pairs per half, max over sequences
   int in_fmt, out_bf16;
   float scale_log2;
+  // e4m3 only: q descale [Hkv]; k / v descales [S, Hkv] indexed by SOURCE rank (nullptr: 1)
+  const float* q_descale;
+  const float* k_descales;
+  const float* v_descales;
 };
 
 constexpr int kErrArrived = kErrDrain + 1;
@@ -129,7 +137,7 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
                       const __grid_constant__ CUtensorMap tmV0,
                       const __grid_constant__ CUtensorMap tmKs,
                       const __grid_constant__ CUtensorMap tmVs, const RingFusedParams p) {
-  static_assert(!TR::FP8 && !TR::PERSISTENT, "the ring kernel is the f16/bf16 one-tile form");
+  static_assert(!TR::PERSISTENT, "the ring kernel runs one tile per CTA");
   constexpr int D = TR::D, BN = TR::BN, ST = TR::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -271,8 +279,9 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
    } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      const uint32_t idesc_qk = make_idesc(BM, BN, p.in_fmt, p.in_fmt, 0, 0);
-      const uint32_t idesc_pv = make_idesc(BM, D, p.in_fmt, p.in_fmt, 0, 1);
+      const int fmt = TR::FP8 ? 0 : p.in_fmt;
+      const uint32_t idesc_qk = make_idesc(BM, BN, fmt, fmt, 0, 0);
+      const uint32_t idesc_pv = make_idesc(BM, D, fmt, fmt, 0, 1);
       auto issue_s = [&](int t, int stage) {
         const uint32_t sQ = smem_u32(smem + TR::OFF_Q + t * TR::Q_TILE_BYTES);
         const uint32_t sK = smem_u32(smem + TR::OFF_K + stage * TR::KV_BYTES);
@@ -281,8 +290,12 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
           const int off = kk * 32;  // bytes along D of this K-step
           const uint32_t ca = (off / 128) * TR::Q_CHUNK_BYTES + (off % 128);
           const uint32_t cb = (off / 128) * TR::KV_CHUNK_BYTES + (off % 128);
-          mma_f16_ss(tmem + uint32_t(TR::tm_s(t)), make_desc_sw128(sQ + ca, 16, 1024),
-                     make_desc_sw128(sK + cb, 16, 1024), idesc_qk, kk > 0 ? 1u : 0u);
+          const uint64_t adesc = make_desc_sw128(sQ + ca, 16, 1024);
+          const uint64_t bdesc = make_desc_sw128(sK + cb, 16, 1024);
+          if constexpr (TR::FP8)
+            mma_f8_ss(tmem + uint32_t(TR::tm_s(t)), adesc, bdesc, idesc_qk, kk > 0 ? 1u : 0u);
+          else
+            mma_f16_ss(tmem + uint32_t(TR::tm_s(t)), adesc, bdesc, idesc_qk, kk > 0 ? 1u : 0u);
         }
         tc_commit(s_full(t));
       };
@@ -291,8 +304,12 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
 #pragma unroll
         for (int kk = 0; kk < BN / TR::MMA_K; ++kk) {
           const uint64_t bdesc = make_desc_sw128(sV + kk * TR::MMA_K * 128, TR::KV_CHUNK_BYTES, 1024);
-          mma_f16_ts(tmem + uint32_t(TR::tm_o(t)), tmem + uint32_t(TR::tm_s(t) + kk * 8), bdesc,
-                     idesc_pv, (!first || kk > 0) ? 1u : 0u);
+          const uint32_t a_tmem = tmem + uint32_t(TR::tm_s(t) + kk * 8);
+          const uint32_t acc = (!first || kk > 0) ? 1u : 0u;
+          if constexpr (TR::FP8)
+            mma_f8_ts(tmem + uint32_t(TR::tm_o(t)), a_tmem, bdesc, idesc_pv, acc);
+          else
+            mma_f16_ts(tmem + uint32_t(TR::tm_o(t)), a_tmem, bdesc, idesc_pv, acc);
         }
       };
       const int nmax = max(n_t[0], n_t[1]);
@@ -354,15 +371,35 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
     if (nn > 0) {
       const int first = q0 + t * BM;
       const int key_lim = first + r + g.diag;  // step 0 only
-      const float scale = p.scale_log2;
-      const uint64_t scale2 = f2pack(scale, scale);
-      float m = kNegInf, l = 0.f;
+      const float qd = (TR::FP8 && p.q_descale != nullptr) ? p.q_descale[w.kvh] : 1.0f;
+      // score scale (log2 units) and V descale of step s: the descales of its source rank
+      auto step_scales = [&](int s, float& sc, float& vs) {
+        const int src = (p.rank - s + p.S) % p.S;
+        sc = p.scale_log2 * qd;
+        vs = 1.0f;
+        if constexpr (TR::FP8) {
+          if (p.k_descales != nullptr) sc *= p.k_descales[src * p.Hkv + w.kvh];
+          if (p.v_descales != nullptr) vs = p.v_descales[src * p.Hkv + w.kvh];
+        }
+      };
+      float scale, vscale;
+      step_scales(0, scale, vscale);
+      int step = 0;
+      float m = kNegInf, l = 0.f;  // m: running max of the scaled scores (log2 units)
       bool aborted = false;
       SegCursor cur;
       cur.start(g, BN);
 
       for (int j = 0; j < nn; ++j) {
         cur.seek(g, j, BN);
+        float fo = 1.0f;  // O factor when the V descale changes with the step
+        if (cur.s != step) {
+          step = cur.s;
+          float vs_new;
+          step_scales(step, scale, vs_new);
+          fo = vscale / vs_new;
+          vscale = vs_new;
+        }
         bool ok = mbar_wait(s_full(t), j & 1, abort, kErrSFull, status);
         if (!__all_sync(0xffffffffu, ok)) { aborted = true; break; }
         tc_fence_after();
@@ -392,17 +429,17 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
 #pragma unroll
           for (int e = 0; e < 32; e += 2)
             mx4[c] = fmax3(mx4[c], __uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1]));
-        const float mx = fmax3(fmaxf(mx4[0], mx4[1]), mx4[2], mx4[3]);
+        const float mx = fmax3(fmaxf(mx4[0], mx4[1]), mx4[2], mx4[3]) * scale;  // scale > 0
         const float m_new = fmaxf(m, mx);
         if (j == 0) {
           m = m_new;
         } else {
-          const bool need = (m_new - m) * scale > kRescaleThreshold;
-          if (__any_sync(0xffffffffu, need)) {
+          const bool need = (m_new - m) > kRescaleThreshold;
+          if (__any_sync(0xffffffffu, need) || fo != 1.0f) {  // fo is uniform in the CTA
             // PV_t(j-1) is complete: S_t(j) was issued after it and has completed.
-            const float f = need ? ex2_approx((m - m_new) * scale) : 1.0f;
+            const float f = need ? ex2_approx(m - m_new) : 1.0f;
             if (need) { l *= f; m = m_new; }
-            const uint64_t f2 = f2pack(f, f);
+            const uint64_t f2 = f2pack(f * fo, f * fo);
 #pragma unroll 1
             for (int c = 0; c < D / 32; ++c) {
               uint32_t o[32];
@@ -420,36 +457,59 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
             tmem_wait_st();
           }
         }
-        const float neg_m = (m == kNegInf) ? 0.f : -m * scale;
+        const float neg_m = (m == kNegInf) ? 0.f : -m;
         const uint64_t negm2 = f2pack(neg_m, neg_m);
+        const uint64_t scale2 = f2pack(scale, scale);
         uint64_t rs2[2] = {0ull, 0ull};
-        // P in 64-key halves: exps of a half are kept (as fp32 bits, in place of S) for the
-        // row sum, which is added up after P has been handed to the MMA warp
-#pragma unroll
-        for (int half = 0; half < BN / 64; ++half) {
+        if constexpr (TR::FP8) {
           uint32_t pw[32];
 #pragma unroll
-          for (int e = 0; e < 64; e += 2) {
-            const int c = half * 2 + (e >> 5), ee = e & 31;
-            const uint64_t a = ffma2(f2pack(__uint_as_float(sr[c][ee]), __uint_as_float(sr[c][ee + 1])), scale2, negm2);
-            const uint64_t ex = exp2_pair<TR>(half * 32 + (e >> 1), a);
-            const float x0 = f2lo(ex), x1 = f2hi(ex);
-            sr[c][ee] = __float_as_uint(x0);
-            sr[c][ee + 1] = __float_as_uint(x1);
-            pw[e >> 1] = p.in_fmt ? pack_bf16x2(x0, x1) : pack_f16x2(x0, x1);
+          for (int c = 0; c < BN / 32; ++c) {
+#pragma unroll
+            for (int e = 0; e < 32; e += 4) {
+              const uint64_t a = ffma2(f2pack(__uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1])), scale2, negm2);
+              const uint64_t b = ffma2(f2pack(__uint_as_float(sr[c][e + 2]), __uint_as_float(sr[c][e + 3])), scale2, negm2);
+              const uint64_t ea = exp2_pair<TR>((c * 32 + e) / 2, a);
+              const uint64_t eb = exp2_pair<TR>((c * 32 + e) / 2 + 1, b);
+              rs2[0] = fadd2(rs2[0], ea);
+              rs2[1] = fadd2(rs2[1], eb);
+              pw[(c * 32 + e) / 4] = pack_e4m3x4(f2lo(ea), f2hi(ea), f2lo(eb), f2hi(eb));
+            }
           }
-          tmem_st32(t_lane + uint32_t(TR::tm_s(t) + half * 32), pw);
+          static_assert(!TR::FP8 || BN == 128, "FP8 P store assumes 128 keys (32 columns)");
+          tmem_st32(t_lane + uint32_t(TR::tm_s(t)), pw);
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive(p_full(t));
+        } else {
+          // P in 64-key halves: exps of a half are kept (as fp32 bits, in place of S) for the
+          // row sum, which is added up after P has been handed to the MMA warp
+#pragma unroll
+          for (int half = 0; half < BN / 64; ++half) {
+            uint32_t pw[32];
+#pragma unroll
+            for (int e = 0; e < 64; e += 2) {
+              const int c = half * 2 + (e >> 5), ee = e & 31;
+              const uint64_t a = ffma2(f2pack(__uint_as_float(sr[c][ee]), __uint_as_float(sr[c][ee + 1])), scale2, negm2);
+              const uint64_t ex = exp2_pair<TR>(half * 32 + (e >> 1), a);
+              const float x0 = f2lo(ex), x1 = f2hi(ex);
+              sr[c][ee] = __float_as_uint(x0);
+              sr[c][ee + 1] = __float_as_uint(x1);
+              pw[e >> 1] = p.in_fmt ? pack_bf16x2(x0, x1) : pack_f16x2(x0, x1);
+            }
+            tmem_st32(t_lane + uint32_t(TR::tm_s(t) + half * 32), pw);
+          }
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive(p_full(t));
+#pragma unroll
+          for (int c = 0; c < BN / 32; ++c)
+#pragma unroll
+            for (int e = 0; e < 32; e += 4) {
+              rs2[0] = fadd2(rs2[0], f2pack(__uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1])));
+              rs2[1] = fadd2(rs2[1], f2pack(__uint_as_float(sr[c][e + 2]), __uint_as_float(sr[c][e + 3])));
+            }
         }
-        tmem_wait_st();
-        tc_fence_before();
-        mbar_arrive(p_full(t));
-#pragma unroll
-        for (int c = 0; c < BN / 32; ++c)
-#pragma unroll
-          for (int e = 0; e < 32; e += 4) {
-            rs2[0] = fadd2(rs2[0], f2pack(__uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1])));
-            rs2[1] = fadd2(rs2[1], f2pack(__uint_as_float(sr[c][e + 2]), __uint_as_float(sr[c][e + 3])));
-          }
         const uint64_t rs = fadd2(rs2[0], rs2[1]);
         l += f2lo(rs) + f2hi(rs);
       }
@@ -464,7 +524,7 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
         const bool valid = r < rows_t[t];
         const int64_t grow = int64_t(q_start) + first + r;
         const bool any_key = (m != kNegInf) && (l > 0.f);
-        const float inv_l = any_key ? 1.0f / l : 0.f;
+        const float inv_l = any_key ? vscale / l : 0.f;  // O is in units of the last V descale
         uint8_t* orow = static_cast<uint8_t*>(p.out) + (grow * p.Hq + w.head) * int64_t(D) * 2;
 #pragma unroll 1
         for (int c = 0; c < D / 32; ++c) {
@@ -488,8 +548,7 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
           }
         }
         if (valid)
-          p.lse[grow * p.Hq + w.head] =
-              any_key ? (m * scale + lg2_approx(l)) * kLn2 : kNegInf;
+          p.lse[grow * p.Hq + w.head] = any_key ? (m + lg2_approx(l)) * kLn2 : kNegInf;
       }
     }
   }

@@ -236,14 +236,13 @@ class NativeRing:
 
         _lib.check(self.lib.fa4cp_ring_timing(self.handle, int(max_launches)), "ring_timing")
 
-    def set_fused(self, fused: bool) -> None:
-        """Whole forward in one launch of the persistent ring kernel where it applies."""
+    def set_fused(self, mode: int) -> None:
+        """Persistent ring kernel: 0 never, 1 for f16 / bf16 (default), 2 also for e4m3."""
         from . import _lib
 
-        if getattr(self, "_fused", None) != bool(fused):
-            _lib.check(self.lib.fa4cp_ring_set_fused(self.handle, int(bool(fused))),
-                       "ring_set_fused")
-            self._fused = bool(fused)
+        if getattr(self, "_fused", None) != int(mode):
+            _lib.check(self.lib.fa4cp_ring_set_fused(self.handle, int(mode)), "ring_set_fused")
+            self._fused = int(mode)
 
     def set_sm_reserve(self, n: int) -> None:
         """SMs the persistent attention grid leaves free for the hop's NCCL kernel."""

@@ -259,9 +259,10 @@ FA4CP_API int fa4cp_local_cu(const int32_t* full_cu, int32_t nseq, int32_t cp_si
  *   every rank before the process group is torn down.
  * fa4cp_ring_set_sm_reserve: SMs (0..64, default 8) the persistent attention grid leaves
  *   free during a ring call, so that the hop's NCCL kernel runs beside it.
- * fa4cp_ring_set_fused: 1 (default) runs the whole forward as one launch of the persistent
- *   ring kernel (fa4cp_ring_attn_fused) where it applies (copy-engine transport or a single
- *   rank; f16 / bf16; D 64 or 128); 0 keeps one attention launch per step.
+ * fa4cp_ring_set_fused: mode 1 (default) runs the whole forward as one launch of the
+ *   persistent ring kernel (fa4cp_ring_attn_fused) for f16 / bf16 with D 64 or 128 (copy-engine
+ *   transport or a single rank); mode 2 also for e4m3 with D 128 (measured slower than the
+ *   persistent per-step e4m3 kernel at cp = 2); 0 keeps one attention launch per step.
  * fa4cp_ring_timing: time the next `max_launches` attention launches and hops (0 = off) with
  *   CUDA events; fa4cp_ring_timeline writes (start, end) pairs in ms relative to the first
  *   timed launch's start into HOST float arrays (attention launches and hops, in issue order,
@@ -330,7 +331,9 @@ FA4CP_API int fa4cp_ring_ce_plan(int32_t nranks, int32_t rank, int64_t g0, int32
  * and the incremental merges of fa4_ring/merge.py:45-64).
  *   q [total, Hq, D], k/v [total, Hkv, D] local; slots_k / slots_v: slot i at
  *   slots_k + i * slot_stride bytes, each [total, Hkv, D] (the source's shard, same cu);
- *   out [total, Hq, D] (q dtype); lse [total, Hq] float32.  f16 / bf16, D 64 or 128.
+ *   out [total, Hq, D] (q dtype; bf16 for e4m3); lse [total, Hq] float32.  f16 / bf16 with
+ *   D 64 or 128, or e4m3 with D 128: then q_descale [Hkv] and k_descales / v_descales
+ *   [nranks, Hkv] indexed by SOURCE rank (each may be NULL = 1); NULL for 16-bit inputs.
  */
 FA4CP_API int fa4cp_ring_attn_fused(const void* q, const void* k, const void* v,
                                     const void* slots_k, const void* slots_v,
@@ -338,8 +341,10 @@ FA4CP_API int fa4cp_ring_attn_fused(const void* q, const void* k, const void* v,
                                     const int32_t* cu, int32_t nseq, int32_t max_seqlen,
                                     int64_t total, int32_t num_heads_q, int32_t num_heads_kv,
                                     int32_t head_dim, int32_t dtype, float softmax_scale,
-                                    int32_t nranks, int32_t rank, const uint32_t* arrived,
-                                    uint32_t arrived_base, void* stream);
+                                    const float* q_descale, const float* k_descales,
+                                    const float* v_descales, int32_t nranks, int32_t rank,
+                                    const uint32_t* arrived, uint32_t arrived_base,
+                                    void* stream);
 
 FA4CP_API int fa4cp_ring_unique_id(uint8_t* id_out);
 FA4CP_API int fa4cp_ring_comm_init(const uint8_t* id, int32_t nranks, int32_t rank,
