@@ -104,6 +104,35 @@ __global__ void local_cu_kernel(const int32_t* __restrict__ full_cu, int n, int 
   if (i < n) local_cu[i] = full_cu[i] / S;
 }
 
+// GDN context-parallel index metadata (the reference's fa4_ring/gdn_cp/metadata.py:48-96):
+// restore[n] = slot of natural token n in the rank-major all-gather [rank0 | rank1 | ...]
+// (each rank's part L = total / S rows); extract[i] = natural position of local token i of
+// rank `rank`.  Sequence j: natural rows [full_cu[j], full_cu[j+1]), local rows
+// [full_cu[j] / S, full_cu[j+1] / S), h = N_j / (2S); local position p < h is chunk `rank`,
+// p >= h chunk 2S-1-rank.
+__global__ void gdn_indices_kernel(const int32_t* __restrict__ full_cu, int nseq, int S, int rank,
+                                   int64_t total, int64_t* __restrict__ restore,
+                                   int64_t* __restrict__ extract) {
+  const int64_t L = total / S;
+  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+  for (int64_t n = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; n < total; n += stride) {
+    if (restore != nullptr) {
+      const int j = find_seq(full_cu, nseq, n, 1);
+      const int64_t a = full_cu[j], h = (int64_t(full_cu[j + 1]) - a) / (2 * S);
+      const int64_t o = n - a, c = o / h, q = o - c * h;
+      const int64_t r = c < S ? c : 2 * S - 1 - c;
+      const int64_t p = c < S ? q : h + q;
+      restore[n] = r * L + a / S + p;
+    }
+    if (extract != nullptr && n < L) {
+      const int j = find_seq(full_cu, nseq, n, S);
+      const int64_t a = full_cu[j], h = (int64_t(full_cu[j + 1]) - a) / (2 * S);
+      const int64_t p = n - a / S;
+      extract[n] = a + (p < h ? int64_t(rank) * h + p : (2 * S - 1 - int64_t(rank)) * h + (p - h));
+    }
+  }
+}
+
 int num_sms() {
   static int sms = 0;
   if (sms == 0) {
@@ -204,6 +233,23 @@ extern "C" int fa4cp_half_index(const int32_t* cu, int32_t nseq, int64_t total, 
   half_index_kernel<<<unsigned(blocks), threads, 0, static_cast<cudaStream_t>(stream)>>>(
       cu, nseq, half, front, out_idx);
   return check_launch("half_index");
+}
+
+extern "C" int fa4cp_gdn_cp_indices(const int32_t* full_cu, int32_t nseq, int32_t cp_size,
+                                    int32_t cp_rank, int64_t total, int64_t* restore_perm,
+                                    int64_t* extract_idx, void* stream) {
+  FA4CP_CHECK_ARG(nseq >= 1 && full_cu != nullptr, "full_cu must describe at least one sequence");
+  FA4CP_CHECK_ARG(cp_size >= 1 && cp_rank >= 0 && cp_rank < cp_size, "bad cp rank %d of %d",
+                  cp_rank, cp_size);
+  FA4CP_CHECK_ARG(total >= 0 && total % (2 * int64_t(cp_size)) == 0,
+                  "total %lld is not a multiple of 2*cp_size", static_cast<long long>(total));
+  if (total == 0 || (restore_perm == nullptr && extract_idx == nullptr)) return FA4CP_OK;
+  const int threads = 256;
+  int64_t blocks = (total + threads - 1) / threads;
+  if (blocks > int64_t(num_sms()) * 8) blocks = int64_t(num_sms()) * 8;
+  gdn_indices_kernel<<<unsigned(blocks), threads, 0, static_cast<cudaStream_t>(stream)>>>(
+      full_cu, nseq, cp_size, cp_rank, total, restore_perm, extract_idx);
+  return check_launch("gdn_cp_indices");
 }
 
 extern "C" int fa4cp_local_cu(const int32_t* full_cu, int32_t nseq, int32_t cp_size,

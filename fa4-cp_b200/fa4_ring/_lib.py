@@ -64,6 +64,7 @@ _SIGNATURES = {
     "fa4cp_zigzag_unshard": [ctypes.POINTER(_vp), _vp, _vp, _i32, _i64, _i32, _i64, _vp],
     "fa4cp_half_index": [_vp, _i32, _i64, _i32, _vp, _vp],
     "fa4cp_local_cu": [_vp, _i32, _i32, _vp, _vp],
+    "fa4cp_gdn_cp_indices": [_vp, _i32, _i32, _i32, _i64, _vp, _vp, _vp],
     "fa4cp_ring_ipc_alloc": [_i64, _i64, _vp],
     "fa4cp_ring_ipc_open": [_i64, _vp, _vp],
     "fa4cp_ring_ipc_close": [_i64],

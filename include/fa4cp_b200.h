@@ -233,6 +233,20 @@ FA4CP_API int fa4cp_half_index(const int32_t* cu, int32_t nseq, int64_t total, i
                      int64_t* out_idx, void* stream);
 
 /*
+ * GDN context-parallel index metadata, on the device.
+ * Replaces: the Python loops of fa4_ring/gdn_cp/metadata.py:48-96 (build_gdn_cp_metadata).
+ *   full_cu int32 [nseq+1] natural-order boundaries (every length a multiple of 2*cp_size);
+ *   restore_perm int64 [total] (or NULL): slot of natural token n in the rank-major
+ *   all-gather of the local shards (rank r's part at r * total / cp_size);
+ *   extract_idx int64 [total / cp_size] (or NULL): natural position of local token i of
+ *   cp_rank.  The gathers themselves are fa4cp_zigzag_unshard (restore, with the shard
+ *   pointers into the all-gather buffer) and fa4cp_zigzag_shard (extract).
+ */
+FA4CP_API int fa4cp_gdn_cp_indices(const int32_t* full_cu, int32_t nseq, int32_t cp_size,
+                                   int32_t cp_rank, int64_t total, int64_t* restore_perm,
+                                   int64_t* extract_idx, void* stream);
+
+/*
  * local_cu[j] = full_cu[j] / cp_size for j in [0, nseq]  (the local cu_seqlens that
  * fa4_ring/zigzag.py:94-97 builds on the host).
  */

@@ -9,7 +9,9 @@ the Python step loop over ``KVRing``, and in ``batched`` mode; FP8 e4m3 Q/K/V an
 with e4m3 K/V (quantised per rank, descales all-gathered by source rank) through the
 native executor, checked against the dense attention of the dequantised tensors.  The
 copy-engine cases run twice in a row (the hop counters carry over between calls), and
-the packed case makes the receive slots grow.  Tolerances: bf16 2e-2, FP8 6e-2.
+the packed case makes the receive slots grow.  Tolerances: bf16 2e-2, FP8 6e-2.  Last, the
+GDN all-gather CP wrapper (``fa4_ring.gdn_cp.gdn_cp_allgather``) against the single-device
+scan, exactly.
 """
 
 import datetime
@@ -107,6 +109,30 @@ def main():
                         print(f"world={world} seqs={num_seqs} {kind} mode={mode} "
                               f"executor={executor} seq{j} max_err={err:.3e}")
                         ok &= err <= tol
+        # GDN all-gather CP (Plan A): the CP output equals the single-device scan, exactly
+        from fa4_ring.gdn_cp import build_gdn_cp_metadata, gdn_cp_allgather
+        lens = [2 * world * n for n in (5, 12)]
+        cu = [0] + [int(x) for x in np.cumsum(lens)]
+        gen = torch.Generator().manual_seed(7)
+        natural = torch.randint(-8, 8, (cu[-1], 16), generator=gen).float().to(dev)
+
+        def seg_cumsum(x, fcu):
+            out = torch.empty_like(x)
+            c = [int(t) for t in fcu.tolist()]
+            for a, b in zip(c[:-1], c[1:]):
+                out[a:b] = torch.cumsum(x[a:b], dim=0)
+            return out.reshape(out.shape[0], 2, 8)
+
+        meta = build_gdn_cp_metadata(lens, world, rank)
+        local = zigzag_shard_varlen(natural, cu, rank, world)[0]
+        got = gdn_cp_allgather(local, seg_cumsum, meta)
+        want = seg_cumsum(natural, meta.full_cu_seqlens)
+        want = zigzag_shard_varlen(want.reshape(cu[-1], -1), cu, rank, world)[0].reshape(got.shape)
+        gdn_ok = torch.tensor([1 if torch.equal(got, want) else 0], device=dev)
+        dist.all_reduce(gdn_ok, op=dist.ReduceOp.MIN)
+        if rank == 0:
+            print(f"world={world} gdn_cp_allgather exact={bool(gdn_ok.item())}")
+        ok &= bool(gdn_ok.item())
         torch.cuda.synchronize()
         dist.barrier()
     finally:

@@ -20,6 +20,10 @@ Fixtures written:
                   pattern's rows), plus ``merge`` known answers incl. -inf rows
   cfg1.npz     -- BASELINE configs[0] (N=4096, Hq=8, Hkv=2, D=128, cp=4, seed 0):
                   sampled rows + checksums of the ring output and dense LSE
+  gdn_meta.npz -- the GDN context-parallel index metadata of the reference's
+                  ``fa4_ring/gdn_cp/metadata.py`` (``build_gdn_cp_metadata``): restore_perm,
+                  extract_idx, full_cu_seqlens for every rank of GDN_CASES
+                  (``--only gdn`` writes just this one)
 """
 
 import argparse
@@ -50,6 +54,33 @@ VARLEN_CASES = [  # tests/test_algorithm_cpu.py:217-223 (seq_lens, H, Hkv, D, cp
 ]
 
 
+GDN_CASES = [  # (cp, full sequence lengths); the first three from tests/test_gdn_cp_cpu.py
+    (4, [48]),
+    (4, [32, 16, 48]),
+    (8, [64, 64]),
+    (2, [12]),
+    (3, [6, 18, 30]),
+    (8, [80, 16]),
+]
+
+
+def write_gdn(root):
+    from fa4_ring.gdn_cp.metadata import build_gdn_cp_metadata  # the reference's module
+    out = {}
+    for ci, (cp, lens) in enumerate(GDN_CASES):
+        out[f"c{ci}_lens"] = np.asarray(lens)
+        out[f"c{ci}_cp"] = np.asarray(cp)
+        for r in range(cp):
+            m = build_gdn_cp_metadata(lens, cp, r)
+            out[f"c{ci}_r{r}_restore"] = m.restore_perm.numpy()
+            out[f"c{ci}_r{r}_extract"] = m.extract_idx.numpy()
+            out[f"c{ci}_r{r}_cu"] = m.full_cu_seqlens.numpy()
+    out["n_cases"] = np.asarray(len(GDN_CASES))
+    p = os.path.join(HERE, "gdn_meta.npz")
+    np.savez_compressed(p, **out)
+    print(f"wrote {p} ({os.path.getsize(p)} bytes)")
+
+
 def load_reference(root):
     sys.path.insert(0, root)
     import fa4_ring.zigzag as zz  # the reference's module
@@ -68,8 +99,12 @@ def gen_inputs(n, H, Hkv, D, seed=0):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="reference checkout root")
+    ap.add_argument("--only", choices=["gdn"], default=None, help="write one fixture only")
     args = ap.parse_args()
     zz, algo = load_reference(os.path.abspath(args.reference))
+    write_gdn(os.path.abspath(args.reference))
+    if args.only == "gdn":
+        return
     torch.set_num_threads(os.cpu_count() or 1)
 
     # ---------------- zig-zag known answers ----------------

@@ -184,3 +184,31 @@ def test_planted_mistake_is_caught():
         outs.append(acc[0])
     bad = orc.zigzag_unshard(outs, cp)
     assert not np.allclose(bad, a["case1_ring_out"], **TOL)
+
+
+def test_gdn_cp_indices_match_reference_golden():
+    """oracle/gdn_oracle.py restates build_gdn_cp_metadata; bit-exact against the fixtures the
+    reference itself wrote (tests/golden/gdn_meta.npz)."""
+    from oracle import gdn_oracle
+    z = np.load(os.path.join(GOLDEN, "gdn_meta.npz"))
+    for ci in range(int(z["n_cases"])):
+        lens, cp = z[f"c{ci}_lens"].tolist(), int(z[f"c{ci}_cp"])
+        for r in range(cp):
+            restore, extract, cu = gdn_oracle.gdn_cp_indices(lens, cp, r)
+            np.testing.assert_array_equal(restore, z[f"c{ci}_r{r}_restore"])
+            np.testing.assert_array_equal(extract, z[f"c{ci}_r{r}_extract"])
+            np.testing.assert_array_equal(cu, z[f"c{ci}_r{r}_cu"])
+
+
+def test_gdn_cp_extract_is_the_ring_sharding():
+    """GDN CP and the ring use one sharding: extract_idx == the zig-zag varlen rows."""
+    from oracle import gdn_oracle
+    for cp, lens in [(2, [12]), (4, [32, 16, 48]), (8, [64, 16])]:
+        cu = [0] + list(np.cumsum(lens))
+        for r in range(cp):
+            _, extract, _ = gdn_oracle.gdn_cp_indices(lens, cp, r)
+            rows, _ = orc.zigzag_varlen_rows(cu, r, cp)
+            np.testing.assert_array_equal(extract, rows)
+            restore, _, _ = gdn_oracle.gdn_cp_indices(lens, cp, 0)
+            gathered = np.concatenate([orc.zigzag_varlen_rows(cu, rr, cp)[0] for rr in range(cp)])
+            np.testing.assert_array_equal(gathered[restore], np.arange(cu[-1]))
