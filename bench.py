@@ -443,6 +443,8 @@ def gpu_main(args, rank, world, local_rank):
             "sample": "oracle (numpy restatement of the reference's CPU ring simulation) on "
                       "rank 0 of cfg2 at cp=8: all 8 ring steps, 32 heads, T=4096 local "
                       f"tokens; {flops_cpu:.3e} FLOP in {secs_cpu:.1f} s"}
+    if world == 1:
+        line["hbm_kernels"] = hbm_kernels(dev)
     traffic = _traffic_from_profile(args.config, world)
     if traffic is not None:
         line["roofline"]["traffic"] = traffic
@@ -459,6 +461,61 @@ def _traffic_from_profile(config, world):
         return t.get(f"{config}_cp{world}")
     except (OSError, ValueError):
         return None
+
+
+# --------------------------------------------------------------------------- HBM-bound kernels
+def hbm_kernels(dev, iters=10):
+    """HBM roofline of the merge and zig-zag kernels on cfg2-sized tensors (T=32768 rows,
+    Hq=32, D=128, bf16), each timed alone with CUDA events (inputs larger than L2, flushed
+    before every launch).  Algorithmic bytes: incremental merge 2*(T*H*D*2 + T*H*4) read +
+    (T*H*D*2 + T*H*4) written; k-way merge k*(T*H*D*2 + T*H*4) read + T*H*D*2 + T*H*4
+    written; zig-zag shard / unshard 2 * bytes moved."""
+    from fa4_ring import _lib
+    from fa4_ring.merge import merge_state_in_place, merge_states
+    from fa4_ring.zigzag import zigzag_shard, zigzag_unshard
+    peaks, kind = load_peaks()
+    hbm = peaks["hbm_gbs"]
+    T, H, D, K = 32768, 32, 128, 8
+    g = torch.Generator(device=dev).manual_seed(5)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    vs = [torch.randn(T, H, D, device=dev, generator=g).bfloat16() for _ in range(K)]
+    ss = [torch.randn(T, H, device=dev, generator=g) * 3 for _ in range(K)]
+    acc_v, acc_s = vs[0].clone(), ss[0].clone()
+    out_v = torch.empty_like(vs[0])
+    out_s = torch.empty_like(ss[0])
+    x = torch.randn(4 * T, H, D, device=dev, generator=g).bfloat16()  # a 131072-token sequence
+    shards = [zigzag_shard(x, r, 2) for r in range(2)]
+
+    def timed(fn):
+        fn()
+        torch.cuda.synchronize()
+        tot = 0.0
+        for _ in range(iters):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            torch.cuda.synchronize()
+            tot += a.elapsed_time(b)
+        return tot / iters
+
+    row = T * H * D * 2 + T * H * 4
+    cases = {
+        "merge_state_inplace": (lambda: merge_state_in_place(acc_v, acc_s, vs[1], ss[1]), 3 * row),
+        f"merge_states_k{K}": (lambda: merge_states(vs, ss, out=out_v, lse_out=out_s), (K + 1) * row),
+        "zigzag_shard_cp2": (lambda: zigzag_shard(x, 0, 2), 2 * x.numel() * 2 // 2),
+        "zigzag_unshard_cp2": (lambda: zigzag_unshard(shards, 2), 2 * x.numel() * 2),
+    }
+    res = {}
+    for name, (fn, nbytes) in cases.items():
+        ms = timed(fn)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        res[name] = {"ms": round(ms, 4), "bytes": int(nbytes), "achieved": round(gbs, 1),
+                     "peak": hbm, "unit": "GB/s", "frac": round(gbs / hbm, 4)}
+    status = _lib.device_status()
+    return {"kernels": res, "peak_kind": f"{kind} hbm_gbs (copy)", "device_status": status,
+            "shape": f"T={T}, Hq={H}, D={D}, bf16 out, fp32 LSE; zig-zag over 131072 rows"}
 
 
 # --------------------------------------------------------------------------- reference arm
@@ -514,6 +571,8 @@ def main():
     ap.add_argument("--timeline", action="store_true",
                     help="with --quick: print each rank's launch/hop timeline of the last "
                          "forward to stderr")
+    ap.add_argument("--aux", action="store_true",
+                    help="only the HBM-bound kernels (merges, zig-zag) against the HBM peak")
     ap.add_argument("--quick", action="store_true",
                     help="profiling run: timed loop only (no e2e, no CPU baseline)")
     args = ap.parse_args()
@@ -529,6 +588,11 @@ def main():
         return 0
 
     torch.cuda.set_device(local_rank)
+    if args.aux:
+        if rank == 0:
+            print(json.dumps({"aux": True, "hbm_kernels": hbm_kernels(torch.device("cuda", local_rank))}),
+                  flush=True)
+        return 0
     if world > 1:
         from fa4_ring.comm import nccl_pg_options
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),

@@ -9,7 +9,7 @@
 // two LSE words (broadcast within the group of threads of that (row, head)), the
 // two value vectors, and writes one vector (+ the LSE from the group leader).
 // A partial whose LSE is -inf is never read (a back-half-only step leaves the
-// front rows' values undefined).
+// front rows' values undefined); a row where both LSEs are -inf gets zeros and -inf.
 #include "common.cuh"
 
 namespace fa4cp {
@@ -70,7 +70,15 @@ __global__ void __launch_bounds__(256) merge_inplace_kernel(
        i += int64_t(gridDim.x) * blockDim.x) {
     const int64_t rh = i / vecs_per_head;
     const float sa = s[rh], sb = so[rh];
-    if (sb == kNegInf) continue;          // partial covers nothing here: identity
+    if (sb == kNegInf) {                  // partial covers nothing here: identity, or zeros
+      if (sa == kNegInf) {                // when neither covers the row (the reference's
+        float z[N];                       // clamped denominator gives 0)
+#pragma unroll
+        for (int e = 0; e < N; ++e) z[e] = 0.f;
+        v[i] = pack(z, (T*)nullptr);
+      }
+      continue;
+    }
     float fa[N], fb[N];
     unpack(vo[i], fb, (T*)nullptr);
     if (sa == kNegInf) {                   // accumulator empty: take the partial
@@ -87,6 +95,82 @@ __global__ void __launch_bounds__(256) merge_inplace_kernel(
       for (int e = 0; e < N; ++e) fa[e] = fa[e] * ca + fb[e] * cb;
     }
     v[i] = pack(fa, (T*)nullptr);
+  }
+}
+
+// Single-pass in-place merge when a head holds 2^LOG <= 32 vectors: the flat vector index is
+// walked in warp-sized chunks, so the vectors of one (row, head) lie in one warp; after a
+// __syncwarp (every lane of the group has read the old LSE) the group's first lane writes the
+// merged LSE.  Shifts replace the 64-bit division of the generic form, and each warp takes
+// U chunks per trip -- all their LSE loads, then all their vector loads -- so that U
+// independent DRAM round trips are in flight per thread instead of two dependent ones.
+template <typename T, int LOG>
+__global__ void __launch_bounds__(256) merge_inplace_fused_kernel(
+    uint4* __restrict__ v, float* __restrict__ s, const uint4* __restrict__ vo,
+    const float* __restrict__ so, int64_t total) {
+  static_assert(LOG >= 0 && LOG <= 5, "a head's vectors must fit in one warp");
+  constexpr int N = Vec<T>::N, VPH = 1 << LOG, U = 4;
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t warps = (int64_t(gridDim.x) * blockDim.x) >> 5;
+  for (int64_t base = warp * 32 * U; base < total; base += warps * 32 * U) {  // warp-uniform
+    float sa[U], sb[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t i = base + u * 32 + lane;
+      sa[u] = sb[u] = kNegInf;
+      if (i < total) {
+        sa[u] = s[i >> LOG];
+        sb[u] = so[i >> LOG];
+      }
+    }
+    uint4 ra[U], rb[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {  // a -inf operand is never read
+      const int64_t i = base + u * 32 + lane;
+      if (i < total && sb[u] != kNegInf) {
+        rb[u] = vo[i];
+        if (sa[u] != kNegInf) ra[u] = v[i];
+      }
+    }
+    float s_new[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t i = base + u * 32 + lane;
+      s_new[u] = sa[u];
+      if (i >= total) continue;
+      float fa[N];
+      if (sb[u] == kNegInf) {
+        if (sa[u] != kNegInf) continue;  // a partial covering nothing is the identity
+#pragma unroll
+        for (int e = 0; e < N; ++e) fa[e] = 0.f;  // neither covers the row: zeros, as the
+      } else {                                      // reference's clamped denominator gives
+        float fb[N];
+        unpack(rb[u], fb, (T*)nullptr);
+        if (sa[u] == kNegInf) {  // accumulator empty: take the partial
+#pragma unroll
+          for (int e = 0; e < N; ++e) fa[e] = fb[e];
+          s_new[u] = sb[u];
+        } else {
+          unpack(ra[u], fa, (T*)nullptr);
+          const float m = fmaxf(sa[u], sb[u]);
+          const float wa = ex2_approx((sa[u] - m) * kLog2e);
+          const float wb = ex2_approx((sb[u] - m) * kLog2e);
+          const float inv = 1.0f / (wa + wb);
+          const float ca = wa * inv, cb = wb * inv;
+#pragma unroll
+          for (int e = 0; e < N; ++e) fa[e] = fa[e] * ca + fb[e] * cb;
+          s_new[u] = m + lg2_approx(wa + wb) * kLn2;
+        }
+      }
+      v[i] = pack(fa, (T*)nullptr);
+    }
+    __syncwarp();
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t i = base + u * 32 + lane;
+      if (i < total && sb[u] != kNegInf && (lane & (VPH - 1)) == 0) s[i >> LOG] = s_new[u];
+    }
   }
 }
 
@@ -199,6 +283,29 @@ extern "C" int fa4cp_merge_state_inplace(void* v, float* s, const void* v_other,
   const unsigned g = grid_for(rh * vph);
   auto* vv = static_cast<uint4*>(v);
   auto* vo = static_cast<const uint4*>(v_other);
+  if ((vph & (vph - 1)) == 0 && vph <= 32) {  // one pass (the common head_dim 64 / 128 / 256)
+    int lg = 0;
+    while ((1 << lg) < vph) ++lg;
+    const int64_t total = rh * vph;
+#define FA4CP_MERGE_FUSED(T)                                                                     \
+    switch (lg) {                                                                              \
+      case 0: merge_inplace_fused_kernel<T, 0><<<g, 256, 0, st>>>(vv, s, vo, s_other, total); break; \
+      case 1: merge_inplace_fused_kernel<T, 1><<<g, 256, 0, st>>>(vv, s, vo, s_other, total); break; \
+      case 2: merge_inplace_fused_kernel<T, 2><<<g, 256, 0, st>>>(vv, s, vo, s_other, total); break; \
+      case 3: merge_inplace_fused_kernel<T, 3><<<g, 256, 0, st>>>(vv, s, vo, s_other, total); break; \
+      case 4: merge_inplace_fused_kernel<T, 4><<<g, 256, 0, st>>>(vv, s, vo, s_other, total); break; \
+      default: merge_inplace_fused_kernel<T, 5><<<g, 256, 0, st>>>(vv, s, vo, s_other, total); break; \
+    }
+    if (dtype == FA4CP_DTYPE_BF16) {
+      FA4CP_MERGE_FUSED(__nv_bfloat16)
+    } else if (dtype == FA4CP_DTYPE_F16) {
+      FA4CP_MERGE_FUSED(__half)
+    } else {
+      FA4CP_MERGE_FUSED(float)
+    }
+#undef FA4CP_MERGE_FUSED
+    return check_launch("merge_state_inplace");
+  }
   if (dtype == FA4CP_DTYPE_BF16)
     merge_inplace_kernel<__nv_bfloat16><<<g, 256, 0, st>>>(vv, s, vo, s_other, rh, vph);
   else if (dtype == FA4CP_DTYPE_F16)

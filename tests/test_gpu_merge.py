@@ -24,11 +24,15 @@ def _partials(T, H, D, dtype, gen, k=2, neg_inf_every=3):
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
-@pytest.mark.parametrize("T,H,D", [(37, 5, 24), (1000, 8, 128), (64, 2, 64)])
+@pytest.mark.parametrize("T,H,D", [(37, 5, 24), (1000, 8, 128), (64, 2, 64), (37, 5, 8),
+                                   (129, 3, 256)])
 def test_merge_state_in_place(dtype, T, H, D):
+    """One-pass form (a head's vectors in one warp: D 8..256 in 16-bit, D 4..128 in fp32)
+    and the two-pass form (D=24, fp32 D=256), with -inf rows in either operand."""
     from fa4_ring.merge import merge_state_in_place
     g = torch.Generator().manual_seed(T + H + D)
     (va, vb), (sa, sb) = _partials(T, H, D, dtype, g)
+    sa[1::5] = float("-inf")  # empty accumulator rows: the partial is taken as is
     want_o, want_l = orc.merge(to_np(va), to_np(sa), to_np(vb), to_np(sb))
     merge_state_in_place(va, sa, vb, sb)
     np.testing.assert_allclose(to_np(va), want_o, atol=TOL[dtype], rtol=TOL[dtype])
