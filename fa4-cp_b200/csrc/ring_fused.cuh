@@ -72,36 +72,39 @@ struct RingTile {
   int seq, half, pair, head, kvh;
 };
 
-// CTA order: pair slots over both halves by decreasing work -- late-half pairs (latest
-// first), then early-half pairs -- in chunks of kQtileChunk; inside a chunk by sequence,
-// kv head, pair, query head of the GQA group (the kv-head grouping keeps the K/V of the CTAs
-// in flight in L2).
+// CTA order: all late-half pairs (they carry every step s > rank, the heavy tiles) before
+// any early-half pair; within a half, pairs latest first (heaviest step 0), in chunks of
+// kQtileChunk, inside a chunk by sequence, kv head, pair, query head of the GQA group (the
+// kv-head grouping keeps the K/V of the CTAs in flight in L2).  Measured on one GPU with
+// cfg2 shapes at cp=8: the slowest rank's launch 1.104 -> 1.058 ms against chunks that mix
+// the two halves.
 __device__ __forceinline__ bool ring_tile(const RingFusedParams& p, RingTile& w) {
-  const int n_q = 2 * p.n_pairs;
-  const int ch = min(kQtileChunk, n_q);
+  const int ch = min(kQtileChunk, p.n_pairs);
+  const int chunks_per_half = (p.n_pairs + ch - 1) / ch;
   const int per_seq = ch * p.Hq;
   const int per_chunk = per_seq * p.nseq;
   const int L = int(blockIdx.x);
-  const int chunk = L / per_chunk;
+  int chunk = L / per_chunk;
   int r = L - chunk * per_chunk;
+  const int round = chunk / chunks_per_half;  // 0: late half, 1: early half
+  chunk -= round * chunks_per_half;
   const int seq = r / per_seq;
   r -= seq * per_seq;
   const int kvh = r / (ch * p.group);
   const int r2 = r - kvh * (ch * p.group);
   const int qd = chunk * ch + r2 / p.group;
-  if (qd >= n_q) return false;
+  if (qd >= p.n_pairs || round > 1) return false;
   w.seq = seq;
-  w.half = qd < p.n_pairs ? 1 : 0;
-  w.pair = p.n_pairs - 1 - (qd % p.n_pairs);
+  w.half = 1 - round;
+  w.pair = p.n_pairs - 1 - qd;
   w.head = kvh * p.group + r2 % p.group;
   w.kvh = kvh;
   return true;
 }
 
 inline unsigned ring_grid(int n_pairs, int Hq, int nseq) {
-  const int n_q = 2 * n_pairs;
-  const int ch = n_q < kQtileChunk ? n_q : kQtileChunk;
-  return unsigned((n_q + ch - 1) / ch * ch * Hq * nseq);
+  const int ch = n_pairs < kQtileChunk ? n_pairs : kQtileChunk;
+  return unsigned(2 * ((n_pairs + ch - 1) / ch) * ch * Hq * nseq);
 }
 
 // K/V geometry of one CTA: step 0 (local, causal) then steps 1 .. S-1
