@@ -16,6 +16,8 @@
 // MMA issue order: S0, S1, PV0, S2, PV1, ... so the tensor core computes S_{j+1}
 // while the softmax warps turn S_j into P_j.  O is rescaled lazily: only when a
 // row's running max grows by more than 2^8 (log2 domain), so P <= 256.
+#include <atomic>
+
 #include "common.cuh"
 
 namespace fa4cp {
@@ -26,6 +28,9 @@ __device__ int g_attn_status = 0;
 // its launches, so the K/V hop's NCCL kernel finds SMs while the attention grid runs)
 thread_local int t_sm_reserve = 0;
 void set_sm_reserve(int n) { t_sm_reserve = n > 0 ? n : 0; }
+
+// bound of the ring kernel's wait for a hop counter written by a peer (fa4cp_ring_set_wait_timeout_ms)
+std::atomic<int> g_ring_wait_ms{10000};
 
 namespace {
 
@@ -1394,6 +1399,7 @@ extern "C" int fa4cp_ring_attn_fused(const void* q, const void* k, const void* v
   p.q_descale = q_descale;
   p.k_descales = k_descales;
   p.v_descales = v_descales;
+  p.arrive_wait_ns = static_cast<unsigned long long>(g_ring_wait_ms.load()) * 1000000ull;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (fp8)  // one tile per CTA (the ring kernel is not persistent)
     return launch_ring_fused<Traits2<128, 128, 3, true, 0>>(q, k, v, slots_k, slots_v, slot_stride,
@@ -1406,6 +1412,12 @@ extern "C" int fa4cp_ring_attn_fused(const void* q, const void* k, const void* v
                                                          total, max_seqlen, p, st);
   set_last_error("the ring kernel takes head_dim 64 or 128 (got %d)", head_dim);
   return FA4CP_ERR_UNSUPPORTED;
+}
+
+extern "C" int fa4cp_ring_set_wait_timeout_ms(int32_t ms) {
+  FA4CP_CHECK_ARG(ms >= 1 && ms <= 600000, "timeout %d ms not in [1, 600000]", ms);
+  g_ring_wait_ms.store(ms);
+  return FA4CP_OK;
 }
 
 extern "C" int fa4cp_device_status(int32_t* status, int32_t clear) {

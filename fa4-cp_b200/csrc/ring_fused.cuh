@@ -35,18 +35,25 @@ struct RingFusedParams {
   const float* q_descale;
   const float* k_descales;
   const float* v_descales;
+  unsigned long long arrive_wait_ns;  // bound of the wait for a hop counter
 };
 
 constexpr int kErrArrived = kErrDrain + 1;
-// cross-rank waits allow for host skew between ranks; a dead peer still ends the wait
-constexpr long long kArriveWaitCycles = 20000000000LL;  // ~10 s at 1.9 GHz
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
 
 // Bounded wait of one thread for a hop counter written by a peer GPU (a stream write through
 // NVLink): acquire at system scope, then order the CTA's later async-proxy (TMA) reads of
-// the slot after it.
+// the slot after it.  The bound is wall time (default 10 s, fa4cp_ring_set_wait_timeout_ms):
+// it allows for host skew between ranks, and a dead peer still ends the wait.
 __device__ __forceinline__ bool wait_arrived(const uint32_t* ctr, uint32_t target,
-                                             volatile int* abort, int* status) {
-  const long long t0 = clock64();
+                                             unsigned long long limit_ns, volatile int* abort,
+                                             int* status) {
+  const unsigned long long t0 = global_ns();
   for (uint32_t it = 0;; ++it) {
     uint32_t v;
     asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
@@ -59,7 +66,7 @@ __device__ __forceinline__ bool wait_arrived(const uint32_t* ctr, uint32_t targe
       *abort = 1;
       return false;
     }
-    if (clock64() - t0 > kArriveWaitCycles) {
+    if (global_ns() - t0 > limit_ns) {
       *abort = 1;
       atomicCAS(status, 0, kErrArrived);
       return false;
@@ -245,7 +252,8 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
         const int row = g.a + (j - cur.first) * BN;
         if (cur.s > waited) {
           if (p.arrived != nullptr &&
-              !wait_arrived(p.arrived, p.arrived_base + uint32_t(cur.s), abort, status))
+              !wait_arrived(p.arrived, p.arrived_base + uint32_t(cur.s), p.arrive_wait_ns, abort,
+                            status))
             break;
           waited = cur.s;
         }

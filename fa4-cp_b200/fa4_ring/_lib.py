@@ -77,6 +77,7 @@ _SIGNATURES = {
     "fa4cp_ring_comm_destroy": [_i64],
     "fa4cp_ring_set_sm_reserve": [_i64, _i32],
     "fa4cp_ring_set_fused": [_i64, _i32],
+    "fa4cp_ring_set_wait_timeout_ms": [_i32],
     "fa4cp_ring_timing": [_i64, _i32],
     "fa4cp_ring_timeline": [_i64, _vp, _i32, _vp, _i32, ctypes.POINTER(_i32), ctypes.POINTER(_i32)],
     "fa4cp_ring_timing_read": [_i64, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(_i32)],

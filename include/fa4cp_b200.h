@@ -349,6 +349,13 @@ FA4CP_API int fa4cp_ring_ce_plan(int32_t nranks, int32_t rank, int64_t g0, int32
  *   D 64 or 128, or e4m3 with D 128: then q_descale [Hkv] and k_descales / v_descales
  *   [nranks, Hkv] indexed by SOURCE rank (each may be NULL = 1); NULL for 16-bit inputs.
  */
+/*
+ * Wall-time bound (ms, default 10000) of the ring kernel's wait for a hop counter; past it
+ * the kernel records FA4CP status 0x10a (see fa4cp_device_status), lets its issued copies and
+ * MMAs finish and returns.  Process-wide; applies to launches made after the call.
+ */
+FA4CP_API int fa4cp_ring_set_wait_timeout_ms(int32_t ms);
+
 FA4CP_API int fa4cp_ring_attn_fused(const void* q, const void* k, const void* v,
                                     const void* slots_k, const void* slots_v,
                                     int64_t slot_stride, void* out, float* lse,
