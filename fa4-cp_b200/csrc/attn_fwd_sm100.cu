@@ -531,6 +531,20 @@ __global__ void __launch_bounds__(kThreads, 1)
 #ifndef FA4CP_P_SPLIT
 #define FA4CP_P_SPLIT 1
 #endif
+// register re-split (setmaxnreg) of the two-tile kernel: softmax warpgroups / the warpgroup
+// of the producer and MMA warps, persistent (P) and one-tile (NP) forms
+#ifndef FA4CP_REGS_SOFTMAX_P
+#define FA4CP_REGS_SOFTMAX_P 200
+#endif
+#ifndef FA4CP_REGS_PRODUCER_P
+#define FA4CP_REGS_PRODUCER_P 104
+#endif
+#ifndef FA4CP_REGS_SOFTMAX_NP
+#define FA4CP_REGS_SOFTMAX_NP 216
+#endif
+#ifndef FA4CP_REGS_PRODUCER_NP
+#define FA4CP_REGS_PRODUCER_NP 72
+#endif
 
 template <int D_, int BN_, int STAGES_, bool FP8_, int PERSIST_ = -1>
 struct Traits2 {
@@ -565,8 +579,8 @@ struct Traits2 {
   // one CTA per tile, where the tile loop has a single trip and its cross-tile state folds
   // away, leaving the softmax warpgroups 216 registers.
   static constexpr bool PERSISTENT = PERSIST_ < 0 ? FP8 : PERSIST_ != 0;
-  static constexpr int REGS_SOFTMAX = PERSISTENT ? 200 : 216;
-  static constexpr int REGS_PRODUCER = PERSISTENT ? 104 : 72;
+  static constexpr int REGS_SOFTMAX = PERSISTENT ? FA4CP_REGS_SOFTMAX_P : FA4CP_REGS_SOFTMAX_NP;
+  static constexpr int REGS_PRODUCER = PERSISTENT ? FA4CP_REGS_PRODUCER_P : FA4CP_REGS_PRODUCER_NP;
   static_assert(128 * (2 * REGS_SOFTMAX + REGS_PRODUCER) <= THREADS * 168,
                 "register re-split exceeds the launch allocation");
   __host__ __device__ static constexpr int tm_s(int t) { return t * BN; }
