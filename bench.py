@@ -458,7 +458,7 @@ def gpu_main(args, rank, world, local_rank):
         "exposed_comm_def": "100 * (step time - summed attention-kernel time) / step time, "
                             "max over ranks",
         "executor": (f"native (fa4cp_ring_attn_fwd), {nring.transport} transport, "
-                     f"{'persistent ring kernel' if n_attn_local == args.steps else 'per-step kernels'}"
+                     f"{'one ring-kernel launch per forward' if n_attn_local == args.steps else 'per-step kernels'}"
                      if nring is not None else "python step loop"),
         "roofline": {"bound": "tensor", "kernel": "fa4cp attn_fwd (tcgen05)",
                      "achieved": None if achieved is None else round(achieved, 1),
@@ -610,9 +610,9 @@ def main():
                     help="NCCL CTA policy of the ring's process group (zero: no SM CTAs)")
     ap.add_argument("--transport", choices=["copy_engine", "nccl"], default="copy_engine",
                     help="K/V transport of the native ring executor (N > 1)")
-    ap.add_argument("--ring-kernel", choices=["fused", "fused-all", "steps"], default="fused",
-                    help="copy-engine ring: one persistent ring kernel per forward for f16/bf16 "
-                         "(fused; fused-all: also e4m3) or one attention launch per step")
+    ap.add_argument("--ring-kernel", choices=["fused", "fused-16bit", "steps"], default="fused",
+                    help="copy-engine ring: one ring-kernel launch per forward (fused; "
+                         "fused-16bit: not for e4m3) or one attention launch per step")
     ap.add_argument("--sm-reserve", type=int, default=None,
                     help="SMs the persistent attention grid leaves to NCCL during a ring call "
                          "(native executor; default: the library's)")
@@ -648,7 +648,7 @@ def main():
                                 pg_options=nccl_pg_options(args.nccl_cta_policy))
     from fa4_ring import ring_attention
     ring_attention.RING_TRANSPORT = args.transport
-    ring_attention.RING_FUSED = {"fused": True, "fused-all": "all", "steps": False}[args.ring_kernel]
+    ring_attention.RING_FUSED = {"fused": True, "fused-16bit": "16bit", "steps": False}[args.ring_kernel]
     try:
         line = gpu_main(args, rank, world, local_rank)
     finally:

@@ -1265,16 +1265,25 @@ template <class TR>
 int launch_ring_fused(const void* q, const void* k, const void* v, const void* slots_k,
                       const void* slots_v, int64_t slot_stride, int64_t total, int max_seqlen,
                       const RingFusedParams& p0, cudaStream_t stream) {
+  using KernelFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap,
+                           RingFusedParams);
+  KernelFn kernel;
+  if constexpr (TR::PERSISTENT)
+    kernel = ring_fused_persistent_kernel<TR>;
+  else
+    kernel = ring_fused_kernel<TR>;
   static bool attr_set = false;
   if (!attr_set) {
-    FA4CP_CHECK_CUDA(cudaFuncSetAttribute(ring_fused_kernel<TR>,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+    FA4CP_CHECK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           TR::SMEM_BYTES));
     attr_set = true;
   }
   RingFusedParams p = p0;
   p.n_pairs = (max_seqlen / 2 + 2 * BM - 1) / (2 * BM);
   if (p.n_pairs <= 0 || total <= 0) return FA4CP_OK;
+  FA4CP_CHECK_ARG(int64_t(2) * ((p.n_pairs + kQtileChunk - 1) / kQtileChunk + 1) * kQtileChunk * p.Hq * p.nseq <
+                      (int64_t(1) << 31), "too many tiles");
+  p.n_tiles = int(ring_grid(p.n_pairs, p.Hq, p.nseq));
   CUtensorMap mq, mk0, mv0, mks, mvs;
   int rc;
   if ((rc = make_map(&mq, q, total, p.Hq, TR::D, TR::ELEM, BM))) return rc;
@@ -1289,9 +1298,15 @@ int launch_ring_fused(const void* q, const void* k, const void* v, const void* s
     mks = mk0;  // no step reads a slot
     mvs = mv0;
   }
-  FA4CP_CHECK_ARG(int64_t(ring_grid(p.n_pairs, p.Hq, p.nseq)) < (int64_t(1) << 31), "grid too large");
-  ring_fused_kernel<TR><<<ring_grid(p.n_pairs, p.Hq, p.nseq), TR::THREADS, TR::SMEM_BYTES, stream>>>(
-      mq, mk0, mv0, mks, mvs, p);
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0;
+    FA4CP_CHECK_CUDA(cudaGetDevice(&dev));
+    FA4CP_CHECK_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  }
+  // persistent (FP8): one CTA per SM walking the tile list; otherwise one CTA per tile
+  const int grid = (TR::PERSISTENT && p.n_tiles > sms) ? sms : p.n_tiles;
+  kernel<<<grid, TR::THREADS, TR::SMEM_BYTES, stream>>>(mq, mk0, mv0, mks, mvs, p);
   return check_launch("ring_fused");
 }
 
@@ -1415,9 +1430,9 @@ extern "C" int fa4cp_ring_attn_fused(const void* q, const void* k, const void* v
   p.v_descales = v_descales;
   p.arrive_wait_ns = static_cast<unsigned long long>(g_ring_wait_ms.load()) * 1000000ull;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (fp8)  // one tile per CTA (the ring kernel is not persistent)
-    return launch_ring_fused<Traits2<128, 128, 3, true, 0>>(q, k, v, slots_k, slots_v, slot_stride,
-                                                            total, max_seqlen, p, st);
+  if (fp8)  // persistent, as the per-step e4m3 kernel
+    return launch_ring_fused<Traits2<128, 128, 3, true>>(q, k, v, slots_k, slots_v, slot_stride,
+                                                         total, max_seqlen, p, st);
   if (head_dim == 128)
     return launch_ring_fused<Traits2<128, 128, 2, false>>(q, k, v, slots_k, slots_v, slot_stride,
                                                           total, max_seqlen, p, st);

@@ -88,7 +88,7 @@ struct RingComm {
   cudaEvent_t ev_hop[kMaxRing] = {};   // hop s landed
   cudaEvent_t ev_step[kMaxRing] = {};  // attention of step s done (its K/V slot is free)
   int sm_reserve = kDefaultSmReserve;  // SMs the persistent attention grid leaves to NCCL
-  int fused = 1;  // persistent ring kernel: 0 never, 1 for f16 / bf16, 2 also for e4m3
+  int fused = 2;  // ring kernel: 0 never, 1 for f16 / bf16 only, 2 also for e4m3 (default)
   // optional timing: 2 timing events per attention launch and per hop, filled in call order
   std::vector<cudaEvent_t> tev, hev;
   int t_used = 0, h_used = 0;

@@ -237,7 +237,7 @@ class NativeRing:
         _lib.check(self.lib.fa4cp_ring_timing(self.handle, int(max_launches)), "ring_timing")
 
     def set_fused(self, mode: int) -> None:
-        """Persistent ring kernel: 0 never, 1 for f16 / bf16 (default), 2 also for e4m3."""
+        """Ring kernel: 0 never, 1 for f16 / bf16 only, 2 also for e4m3 (the library default)."""
         from . import _lib
 
         if getattr(self, "_fused", None) != int(mode):

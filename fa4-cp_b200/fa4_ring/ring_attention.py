@@ -137,9 +137,9 @@ NATIVE_EXECUTOR = True
 # K/V transport of the native executor: "copy_engine" (NVLink copies + stream counters, no
 # SM used) or "nccl" (send/recv on the executor's own communicator)
 RING_TRANSPORT = "copy_engine"
-# copy engine: run the whole forward as one launch of the persistent ring kernel -- True:
-# for f16 / bf16 with D 64 or 128; "all": also for e4m3 with D 128 (slower than the
-# persistent per-step e4m3 kernel at cp = 2); False: one attention launch per step
+# copy engine: run the whole forward as one launch of the ring kernel -- True: for f16 / bf16
+# with D 64 or 128 and e4m3 with D 128; "16bit": f16 / bf16 only; False: one attention launch
+# per step
 RING_FUSED = True
 
 
@@ -177,7 +177,7 @@ def _native_forward(q, k, v, cfg: RingConfig, group, *, cu, nseq, max_seqlen,
         bufs = torch.empty(4 * kv_bytes, dtype=torch.uint8, device=dev)  # two [K | V] slots
     else:
         ring.ensure_capacity(kv_bytes)
-        ring.set_fused(2 if RING_FUSED == "all" else int(bool(RING_FUSED)))
+        ring.set_fused(1 if RING_FUSED == "16bit" else (2 if RING_FUSED else 0))
     ws = None
     if is_mixed(q, k):
         nbytes = _lib.load().fa4cp_attn_kv8_workspace_bytes(T, Hkv, D)
@@ -187,7 +187,7 @@ def _native_forward(q, k, v, cfg: RingConfig, group, *, cu, nseq, max_seqlen,
         q_descale=qd, k_descales=kds, v_descales=vds, kv_bufs=bufs, workspace=ws)
     fused = (ring.transport == "copy_engine" and bool(RING_FUSED) and q.dtype == k.dtype
              and ((q.dtype in (torch.float16, torch.bfloat16) and D in (64, 128))
-                  or (RING_FUSED == "all" and q.dtype == torch.float8_e4m3fn and D == 128)))
+                  or (RING_FUSED is True and q.dtype == torch.float8_e4m3fn and D == 128)))
     _lib.count_launches(1 if fused else S * (3 if ws is not None else 1))
     return out
 

@@ -273,10 +273,10 @@ FA4CP_API int fa4cp_local_cu(const int32_t* full_cu, int32_t nseq, int32_t cp_si
  *   every rank before the process group is torn down.
  * fa4cp_ring_set_sm_reserve: SMs (0..64, default 8) the persistent attention grid leaves
  *   free during a ring call, so that the hop's NCCL kernel runs beside it.
- * fa4cp_ring_set_fused: mode 1 (default) runs the whole forward as one launch of the
- *   persistent ring kernel (fa4cp_ring_attn_fused) for f16 / bf16 with D 64 or 128 (copy-engine
- *   transport or a single rank); mode 2 also for e4m3 with D 128 (measured slower than the
- *   persistent per-step e4m3 kernel at cp = 2); 0 keeps one attention launch per step.
+ * fa4cp_ring_set_fused: mode 2 (default) runs the whole forward as one launch of the ring
+ *   kernel (fa4cp_ring_attn_fused) for f16 / bf16 with D 64 or 128 and e4m3 with D 128
+ *   (copy-engine transport or a single rank); mode 1 for f16 / bf16 only; 0 keeps one
+ *   attention launch per step.
  * fa4cp_ring_timing: time the next `max_launches` attention launches and hops (0 = off) with
  *   CUDA events; fa4cp_ring_timeline writes (start, end) pairs in ms relative to the first
  *   timed launch's start into HOST float arrays (attention launches and hops, in issue order,

@@ -58,7 +58,7 @@ def main():
                 ("bf16", "incremental", "copy_engine_steps"),
                 ("bf16", "incremental", "nccl"), ("bf16", "incremental", "python"),
                 ("bf16", "batched", "python"), ("e4m3", "incremental", "copy_engine"),
-                ("e4m3", "incremental", "copy_engine_steps"), ("e4m3", "incremental", "copy_engine_all"),
+                ("e4m3", "incremental", "copy_engine_steps"),
                 ("mixed", "incremental", "copy_engine"), ("e4m3", "incremental", "nccl")]
         for num_seqs in (1, 3):
             g = torch.Generator().manual_seed(1234)
@@ -76,8 +76,7 @@ def main():
                 kw = {"cu_seqlens": lcu, "max_seqlen": max(lens) // world}
             for kind, mode, executor in runs:
                 ring_attention.NATIVE_EXECUTOR = executor != "python"
-                ring_attention.RING_FUSED = {"copy_engine_steps": False,
-                                             "copy_engine_all": "all"}.get(executor, True)
+                ring_attention.RING_FUSED = executor != "copy_engine_steps"
                 if executor != "python":
                     ring_attention.RING_TRANSPORT = ("copy_engine" if executor.startswith("copy")
                                                      else executor)
