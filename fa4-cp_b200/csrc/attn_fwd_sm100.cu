@@ -1168,16 +1168,24 @@ int make_map(CUtensorMap* map, const void* base, int64_t rows, int heads, int D,
   return FA4CP_OK;
 }
 
+// Opt a kernel into its dynamic shared memory once per device (the attribute is per device;
+// one bit per device id for up to 64 devices, set after the call succeeded).
+template <class Fn>
+int smem_optin(Fn kernel, int bytes, std::atomic<uint64_t>& done) {
+  int dev = 0;
+  FA4CP_CHECK_CUDA(cudaGetDevice(&dev));
+  const uint64_t bit = dev < 64 ? (uint64_t(1) << dev) : 0;
+  if (bit != 0 && (done.load() & bit)) return FA4CP_OK;
+  FA4CP_CHECK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  done.fetch_or(bit);
+  return FA4CP_OK;
+}
+
 template <class TR>
 int launch(const void* q, const void* k, const void* v, int64_t total_q, int64_t total_k,
            int max_seqlen_q, const Params& p0, cudaStream_t stream) {
-  static bool attr_set = false;
-  if (!attr_set) {
-    FA4CP_CHECK_CUDA(cudaFuncSetAttribute(attn_fwd_kernel<TR>,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          TR::SMEM_BYTES));
-    attr_set = true;
-  }
+  static std::atomic<uint64_t> optin{0};
+  if (int rc0 = smem_optin(attn_fwd_kernel<TR>, TR::SMEM_BYTES, optin)) return rc0;
   CUtensorMap mq, mk, mv;
   int rc = make_map(&mq, q, total_q, p0.Hq, TR::D, TR::ELEM, BM);
   if (rc) return rc;
@@ -1201,13 +1209,8 @@ int launch(const void* q, const void* k, const void* v, int64_t total_q, int64_t
 template <class TR>
 int launch2(const void* q, const void* k, const void* v, int64_t total_q, int64_t total_k,
             int max_seqlen_q, const Params& p0, cudaStream_t stream) {
-  static bool attr_set = false;
-  if (!attr_set) {
-    FA4CP_CHECK_CUDA(cudaFuncSetAttribute(attn_fwd_2q_kernel<TR>,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          TR::SMEM_BYTES));
-    attr_set = true;
-  }
+  static std::atomic<uint64_t> optin{0};
+  if (int rc0 = smem_optin(attn_fwd_2q_kernel<TR>, TR::SMEM_BYTES, optin)) return rc0;
   CUtensorMap mq, mk, mv;
   int rc = make_map(&mq, q, total_q, p0.Hq, TR::D, TR::ELEM, BM);
   if (rc) return rc;
@@ -1272,12 +1275,8 @@ int launch_ring_fused(const void* q, const void* k, const void* v, const void* s
     kernel = ring_fused_persistent_kernel<TR>;
   else
     kernel = ring_fused_kernel<TR>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    FA4CP_CHECK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          TR::SMEM_BYTES));
-    attr_set = true;
-  }
+  static std::atomic<uint64_t> optin{0};
+  if (int rc0 = smem_optin(kernel, TR::SMEM_BYTES, optin)) return rc0;
   RingFusedParams p = p0;
   p.n_pairs = (max_seqlen / 2 + 2 * BM - 1) / (2 * BM);
   if (p.n_pairs <= 0 || total <= 0) return FA4CP_OK;
