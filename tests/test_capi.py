@@ -78,3 +78,19 @@ def test_zigzag_argument_validation(lib):
     assert b"divisible" in lib.fa4cp_last_error()
     assert lib.fa4cp_zigzag_shard(dummy, dummy, None, 1, 8, 2, 2, 4, None) == -1   # rank >= cp
     assert lib.fa4cp_half_index(dummy, 1, 7, 1, dummy, None) == -1                  # odd total
+
+
+def test_header_is_c_and_library_links_from_c(lib, tmp_path):
+    """include/fa4cp_b200.h compiles as C; a C program links the library and calls the
+    host-only entry points (tests/c_abi/c_abi_check.c)."""
+    from fa4_ring import _lib
+    src = os.path.join(ROOT, "tests", "c_abi", "c_abi_check.c")
+    exe = str(tmp_path / "c_abi_check")
+    libdir = os.path.dirname(_lib.LIB_PATH)
+    cc = subprocess.run(["gcc", "-std=c11", "-Wall", "-Werror", "-I", os.path.join(ROOT, "include"),
+                         src, "-o", exe, "-L", libdir, "-l:" + os.path.basename(_lib.LIB_PATH),
+                         "-Wl,-rpath," + libdir], capture_output=True, text=True)
+    assert cc.returncode == 0, cc.stderr
+    run = subprocess.run([exe], capture_output=True, text=True)
+    assert run.returncode == 0, (run.returncode, run.stdout, run.stderr)
+    assert "c abi ok" in run.stdout
