@@ -62,6 +62,11 @@ struct Params {
   // self-test only (fa4cp_selftest_wait_expiry): index of the KV tile whose K copy the
   // producer never issues, so the consumer's bounded wait must expire; -1 otherwise
   int debug_withhold_kv;
+  // paged K/V (two-tile kernel, VARLEN pattern): K/V rows of sequence j at logical row r live
+  // in page block_table[j * max_pages + r / page_size], row r % page_size of the page pool
+  // [pages, page_size, Hkv, D]; nullptr: contiguous K/V at cu_k
+  const int32_t* block_table;
+  int page_size, max_pages;
 };
 
 template <int D_, int BN_, int STAGES_, bool FP8_>
@@ -594,7 +599,7 @@ struct Traits2 {
 // One unit of work of the persistent kernel: 2 x 128 query rows of one (head, sequence).
 struct TileWork {
   Geometry g;
-  int head, kvh, q0, diag, nmax;
+  int seq, head, kvh, q0, diag, nmax;
   int rows_t[2], n_t[2];
 };
 
@@ -617,6 +622,7 @@ __device__ __forceinline__ bool tile_work(const Params& p, int tile, int BN, Til
   if (qt_desc >= p.n_qtiles) return false;
   w.head = kvh * p.group + r2 % p.group;
   w.kvh = kvh;
+  w.seq = seq;
   w.g = seq_geometry(p, seq);
   w.q0 = (p.n_qtiles - 1 - qt_desc) * 2 * BM;
   if (w.q0 >= w.g.q_len) return false;
@@ -739,22 +745,34 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
                         &tmQ, c * TR::CHUNK, w.head, w.g.q_start + w.q0 + t * BM, q_full);
         for (int j = 0; j < w.nmax; ++j, ++kv_it) {
           const int s = kv_it % ST, ph = (kv_it / ST) & 1;
-          const int row = w.g.k_start + j * BN;
+          int row = w.g.k_start + j * BN, page = 0;
+          if (p.block_table != nullptr) {  // paged: the tile lies inside one page
+            page = p.block_table[int64_t(w.seq) * p.max_pages + (j * BN) / p.page_size];
+            row = (j * BN) % p.page_size;
+          }
           if (kv_it >= ST && !mbar_wait(k_empty(s), ph ^ 1, abort, kErrKEmpty, status)) { ok = false; break; }
           if (kv_it != p.debug_withhold_kv) {
             mbar_arrive_expect_tx(k_full(s), TR::KV_BYTES);
 #pragma unroll
-            for (int c = 0; c < TR::NCH; ++c)
-              tma_load_3d_hint(smem_u32(smem + TR::OFF_K + s * TR::KV_BYTES + c * TR::KV_CHUNK_BYTES),
-                               &tmK, c * TR::CHUNK, w.kvh, row, k_full(s), pol_kv);
+            for (int c = 0; c < TR::NCH; ++c) {
+              const uint32_t dst = smem_u32(smem + TR::OFF_K + s * TR::KV_BYTES + c * TR::KV_CHUNK_BYTES);
+              if (p.block_table != nullptr)
+                tma_load_4d_hint(dst, &tmK, c * TR::CHUNK, w.kvh, row, page, k_full(s), pol_kv);
+              else
+                tma_load_3d_hint(dst, &tmK, c * TR::CHUNK, w.kvh, row, k_full(s), pol_kv);
+            }
             last_k[s] = kv_it;
           }
           if (kv_it >= ST && !mbar_wait(v_empty(s), ph ^ 1, abort, kErrVEmpty, status)) { ok = false; break; }
           mbar_arrive_expect_tx(v_full(s), TR::KV_BYTES);
 #pragma unroll
-          for (int c = 0; c < TR::NCH; ++c)
-            tma_load_3d_hint(smem_u32(smem + TR::OFF_V + s * TR::KV_BYTES + c * TR::KV_CHUNK_BYTES),
-                             &tmV, c * TR::CHUNK, w.kvh, row, v_full(s), pol_kv);
+          for (int c = 0; c < TR::NCH; ++c) {
+            const uint32_t dst = smem_u32(smem + TR::OFF_V + s * TR::KV_BYTES + c * TR::KV_CHUNK_BYTES);
+            if (p.block_table != nullptr)
+              tma_load_4d_hint(dst, &tmV, c * TR::CHUNK, w.kvh, row, page, v_full(s), pol_kv);
+            else
+              tma_load_3d_hint(dst, &tmV, c * TR::CHUNK, w.kvh, row, v_full(s), pol_kv);
+          }
           last_v[s] = kv_it;
         }
         ++tile_it;
@@ -1264,6 +1282,40 @@ int make_map4(CUtensorMap* map, const void* base, int64_t rows, int heads, int D
   return FA4CP_OK;
 }
 
+// Paged K/V through the two-tile kernel: the pools [num_pages, page_size, Hkv, D] are 4-D
+// tensor maps (page = the slowest coordinate); the producer looks up each K/V tile's page.
+template <class TR>
+int launch2_paged(const void* q, const void* k_pages, const void* v_pages, int num_pages,
+                  int64_t total_q, int max_seqlen_q, const Params& p0, cudaStream_t stream) {
+  static std::atomic<uint64_t> optin{0};
+  if (int rc0 = smem_optin(attn_fwd_2q_kernel<TR>, TR::SMEM_BYTES, optin)) return rc0;
+  FA4CP_CHECK_ARG(p0.page_size % TR::BN == 0, "page_size %d must be a multiple of %d",
+                  p0.page_size, TR::BN);
+  CUtensorMap mq, mk, mv;
+  int rc;
+  if ((rc = make_map(&mq, q, total_q, p0.Hq, TR::D, TR::ELEM, BM))) return rc;
+  const int64_t page_bytes = int64_t(p0.page_size) * p0.Hkv * TR::D * TR::ELEM;
+  if ((rc = make_map4(&mk, k_pages, p0.page_size, p0.Hkv, TR::D, TR::ELEM, TR::BN, num_pages, page_bytes)))
+    return rc;
+  if ((rc = make_map4(&mv, v_pages, p0.page_size, p0.Hkv, TR::D, TR::ELEM, TR::BN, num_pages, page_bytes)))
+    return rc;
+  Params p = p0;
+  p.n_qtiles = (max_seqlen_q + 2 * BM - 1) / (2 * BM);
+  if (p.n_qtiles <= 0) return FA4CP_OK;
+  FA4CP_CHECK_ARG(int64_t(p.n_qtiles + kQtileChunk) * p.Hq * p.nseq < (int64_t(1) << 31),
+                  "too many tiles");
+  p.n_tiles = persistent_tiles(p.n_qtiles, p.Hq, p.nseq);
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0;
+    FA4CP_CHECK_CUDA(cudaGetDevice(&dev));
+    FA4CP_CHECK_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  }
+  const int grid = (TR::PERSISTENT && p.n_tiles > sms) ? sms : p.n_tiles;
+  attn_fwd_2q_kernel<TR><<<grid, TR::THREADS, TR::SMEM_BYTES, stream>>>(mq, mk, mv, p);
+  return check_launch("attn_fwd_2q (paged)");
+}
+
 template <class TR>
 int launch_ring_fused(const void* q, const void* k, const void* v, const void* slots_k,
                       const void* slots_v, int64_t slot_stride, int64_t total, int max_seqlen,
@@ -1446,6 +1498,76 @@ extern "C" int fa4cp_ring_set_wait_timeout_ms(int32_t ms) {
   FA4CP_CHECK_ARG(ms >= 1 && ms <= 600000, "timeout %d ms not in [1, 600000]", ms);
   g_ring_wait_ms.store(ms);
   return FA4CP_OK;
+}
+
+extern "C" int fa4cp_attn_fwd_paged(const void* q, const void* k_pages, const void* v_pages,
+                                    const int32_t* block_table, int32_t page_size,
+                                    int32_t num_pages, int32_t max_pages_per_seq, void* out,
+                                    float* lse, const int32_t* cu_q, const int32_t* cu_k,
+                                    int32_t nseq, int32_t max_seqlen_q, int64_t total_q,
+                                    int32_t num_heads_q, int32_t num_heads_kv, int32_t head_dim,
+                                    int32_t in_dtype, int32_t out_dtype, int32_t causal,
+                                    float softmax_scale, const float* q_descale,
+                                    const float* k_descale, const float* v_descale,
+                                    void* stream) {
+  FA4CP_CHECK_ARG(nseq >= 1 && cu_q != nullptr && cu_k != nullptr,
+                  "cu_seqlens_q/k must describe >= 1 sequence");
+  FA4CP_CHECK_ARG(block_table != nullptr && page_size > 0 && num_pages > 0 && max_pages_per_seq > 0,
+                  "paged K/V needs a block table, a page size and the pool size");
+  FA4CP_CHECK_ARG(num_heads_q > 0 && num_heads_kv > 0 && num_heads_q % num_heads_kv == 0,
+                  "H_q=%d not a multiple of H_kv=%d", num_heads_q, num_heads_kv);
+  FA4CP_CHECK_ARG(total_q >= 0 && max_seqlen_q >= 0, "bad sizes");
+  FA4CP_CHECK_ARG(out_dtype == FA4CP_DTYPE_BF16 || out_dtype == FA4CP_DTYPE_F16,
+                  "output dtype must be f16 or bf16");
+  FA4CP_CHECK_ARG(softmax_scale > 0.f, "softmax_scale must be positive");
+  const bool fp8 = in_dtype == FA4CP_DTYPE_E4M3;
+  FA4CP_CHECK_ARG(fp8 || in_dtype == FA4CP_DTYPE_BF16 || in_dtype == FA4CP_DTYPE_F16,
+                  "input dtype must be f16, bf16 or e4m3");
+  FA4CP_CHECK_ARG(fp8 || (q_descale == nullptr && k_descale == nullptr && v_descale == nullptr),
+                  "descales apply to e4m3 inputs only");
+  if (total_q == 0) return FA4CP_OK;
+  FA4CP_CHECK_ARG(q && out && lse && k_pages && v_pages, "null tensor pointer");
+  FA4CP_CHECK_ARG(aligned16(q) && aligned16(k_pages) && aligned16(v_pages) && aligned16(out),
+                  "q, the page pools and out must be 16-byte aligned");
+  Params p{};
+  p.cu_q = cu_q;
+  p.cu_k = cu_k;
+  p.out = out;
+  p.lse = lse;
+  p.q_descale = q_descale;
+  p.k_descale = k_descale;
+  p.v_descale = v_descale;
+  p.nseq = nseq;
+  p.Hq = num_heads_q;
+  p.Hkv = num_heads_kv;
+  p.group = num_heads_q / num_heads_kv;
+  p.pattern = FA4CP_PATTERN_VARLEN;
+  p.causal = causal ? 1 : 0;
+  p.accumulate = 0;
+  p.in_fmt = in_dtype == FA4CP_DTYPE_BF16 ? 1 : 0;
+  p.out_bf16 = out_dtype == FA4CP_DTYPE_BF16 ? 1 : 0;
+  p.scale_log2 = softmax_scale * kLog2e;
+  p.debug_withhold_kv = -1;
+  p.block_table = block_table;
+  p.page_size = page_size;
+  p.max_pages = max_pages_per_seq;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (fp8) {
+    FA4CP_CHECK_ARG(out_dtype == FA4CP_DTYPE_BF16, "e4m3 inputs produce a bf16 output");
+    if (head_dim == 128)
+      return launch2_paged<Traits2<128, 128, 3, true>>(q, k_pages, v_pages, num_pages, total_q,
+                                                        max_seqlen_q, p, st);
+  } else {
+    if (head_dim == 128)
+      return launch2_paged<Traits2<128, 128, 2, false>>(q, k_pages, v_pages, num_pages, total_q,
+                                                         max_seqlen_q, p, st);
+    if (head_dim == 64)
+      return launch2_paged<Traits2<64, 128, 3, false>>(q, k_pages, v_pages, num_pages, total_q,
+                                                        max_seqlen_q, p, st);
+  }
+  set_last_error("paged K/V takes head_dim 64 or 128 (f16 / bf16) or 128 (e4m3); got %d",
+                 head_dim);
+  return FA4CP_ERR_UNSUPPORTED;
 }
 
 extern "C" int fa4cp_device_status(int32_t* status, int32_t clear) {

@@ -54,6 +54,8 @@ _SIGNATURES = {
     "fa4cp_attn_fwd_kv8_noalloc": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i64, _i64,
                                    _i32, _i32, _i32, _i32, _i32, _i32, _f32, _vp, _vp, _i32, _vp],
     "fa4cp_attn_kv8_workspace_bytes": [_i64, _i32, _i32],
+    "fa4cp_attn_fwd_paged": [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _i32, _i32,
+                             _i64, _i32, _i32, _i32, _i32, _i32, _i32, _f32, _vp, _vp, _vp, _vp],
     "fa4cp_dequant_e4m3": [_vp, _vp, _vp, _i64, _i32, _i32, _vp],
     "fa4cp_quantize_e4m3": [_vp, _i32, _i64, _vp, _vp, _vp],
     "fa4cp_merge_state_inplace": [_vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _vp],

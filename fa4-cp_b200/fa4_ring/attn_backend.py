@@ -175,3 +175,56 @@ def b200_attn(
 
 # Drop-in name of the reference's per-chunk entry (fa4_ring/fa4_backend.py:58).
 fa4_attn = b200_attn
+
+
+def b200_attn_paged(
+    q: torch.Tensor,            # [T_q, H, D]
+    k_pages: torch.Tensor,      # [num_pages, page_size, H_kv, D]
+    v_pages: torch.Tensor,      # [num_pages, page_size, H_kv, D]
+    block_table: torch.Tensor,  # int32 [num_seqs, max_pages_per_seq]
+    *,
+    cu_seqlens_q: torch.Tensor,  # int32 [num_seqs + 1]
+    cu_seqlens_k: torch.Tensor,  # int32 [num_seqs + 1], logical K/V lengths
+    max_seqlen_q: int,
+    causal: bool,
+    softmax_scale: Optional[float] = None,
+    q_descale: Optional[torch.Tensor] = None,
+    k_descale: Optional[torch.Tensor] = None,
+    v_descale: Optional[torch.Tensor] = None,
+) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Varlen attention over a paged K/V cache (``fa4cp_attn_fwd_paged``): the K/V rows of
+    sequence j at logical position r are row ``r % page_size`` of page
+    ``block_table[j, r // page_size]``.  ``page_size`` must be a multiple of 128.  Causal
+    masking is bottom-right aligned per sequence, as :func:`b200_attn`.  Returns
+    ``(out [T_q, H, D], lse [T_q, H] fp32 natural log)``.  Not in the reference, whose K/V is
+    contiguous."""
+    _lib.require_cuda(q, k_pages, v_pages, block_table)
+    assert k_pages.dim() == 4 and k_pages.shape == v_pages.shape, "pools are [pages, page, H_kv, D]"
+    assert k_pages.dtype == v_pages.dtype == q.dtype, "q and the pools must share a dtype"
+    num_pages, page_size, h_kv, D = k_pages.shape
+    assert q.shape[2] == D and q.shape[1] % h_kv == 0
+    if softmax_scale is None:
+        softmax_scale = 1.0 / math.sqrt(D)
+    dev = q.device
+    fp8 = q.dtype == torch.float8_e4m3fn
+    qd = norm_descale(q_descale, h_kv, dev) if fp8 else None
+    kd = norm_descale(k_descale, h_kv, dev) if fp8 else None
+    vd = norm_descale(v_descale, h_kv, dev) if fp8 else None
+    q = q.contiguous()
+    bt = block_table.to(device=dev, dtype=torch.int32).contiguous()
+    cu_q = cu_seqlens_q.to(device=dev, dtype=torch.int32).contiguous()
+    cu_k = cu_seqlens_k.to(device=dev, dtype=torch.int32).contiguous()
+    assert bt.dim() == 2 and bt.shape[0] == cu_q.numel() - 1 == cu_k.numel() - 1
+    out = torch.empty(q.shape, dtype=out_dtype_for(q.dtype), device=dev)
+    lse = torch.empty(q.shape[:2], dtype=torch.float32, device=dev)
+    lib = _lib.load()
+    rc = lib.fa4cp_attn_fwd_paged(
+        q.data_ptr(), k_pages.contiguous().data_ptr(), v_pages.contiguous().data_ptr(),
+        bt.data_ptr(), page_size, num_pages, bt.shape[1], out.data_ptr(), lse.data_ptr(),
+        cu_q.data_ptr(), cu_k.data_ptr(), cu_q.numel() - 1, int(max_seqlen_q), q.shape[0],
+        q.shape[1], h_kv, D, _lib.dtype_code(q.dtype), _lib.dtype_code(out.dtype),
+        1 if causal else 0, float(softmax_scale), _lib.ptr(qd), _lib.ptr(kd), _lib.ptr(vd),
+        _lib.stream_of(q))
+    _lib.check(rc, "attn_fwd_paged")
+    _lib.count_launches()
+    return out, lse

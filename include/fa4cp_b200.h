@@ -108,6 +108,29 @@ FA4CP_API int fa4cp_attn_fwd(const void* q, const void* k, const void* v, void* 
                    void* stream);
 
 /*
+ * Attention over a PAGED K/V cache (variable-length, causal or not): fa4cp_attn_fwd's
+ * VARLEN pattern with K/V rows looked up through a block table instead of contiguous rows.
+ *   k_pages, v_pages  [num_pages, page_size, Hkv, D] page pools (dtype as q)
+ *   block_table       int32 [nseq, max_pages_per_seq]: physical page of each logical page
+ *   page_size         a multiple of 128 (a K/V tile never straddles two pages)
+ *   cu_k              int32 [nseq+1] LOGICAL cumulative K/V lengths (sequence j has
+ *                     cu_k[j+1]-cu_k[j] <= max_pages_per_seq * page_size keys)
+ * Other arguments as fa4cp_attn_fwd (no accumulate).  Page indices are read on the device and
+ * not validated; one outside [0, num_pages) reads zeros.  head_dim 64 / 128 (f16, bf16), 128
+ * (e4m3).  No counterpart in the reference, whose rotated K/V is contiguous
+ * (its README's "no paged KV" limitation, README.md:139-141).
+ */
+FA4CP_API int fa4cp_attn_fwd_paged(const void* q, const void* k_pages, const void* v_pages,
+                                   const int32_t* block_table, int32_t page_size,
+                                   int32_t num_pages, int32_t max_pages_per_seq, void* out,
+                                   float* lse, const int32_t* cu_q, const int32_t* cu_k,
+                                   int32_t nseq, int32_t max_seqlen_q, int64_t total_q,
+                                   int32_t num_heads_q, int32_t num_heads_kv, int32_t head_dim,
+                                   int32_t in_dtype, int32_t out_dtype, int32_t causal,
+                                   float softmax_scale, const float* q_descale,
+                                   const float* k_descale, const float* v_descale, void* stream);
+
+/*
  * Attention with a bf16 query and e4m3 keys/values (mixed precision, e.g. FP8 KV with a
  * bf16 Q).  One tcgen05 MMA takes a single operand type, so K and V are first
  * dequantised (value x per-kv-head descale) into `workspace` as bf16 and attended by the
