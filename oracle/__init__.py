@@ -11,4 +11,7 @@ fallback.
 per-chunk attention / online-softmax merge / ring simulation of
 ``tests/test_algorithm_cpu.py``.  It is pinned against golden vectors produced
 by importing the reference itself (``tests/golden/make_golden.py``).
+
+``bwd_oracle`` is the gradient of that forward (the reference itself is forward-only),
+pinned against torch autograd through the reference's dense forward.
 """

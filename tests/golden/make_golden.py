@@ -24,6 +24,12 @@ Fixtures written:
                   ``fa4_ring/gdn_cp/metadata.py`` (``build_gdn_cp_metadata``): restore_perm,
                   extract_idx, full_cu_seqlens for every rank of GDN_CASES
                   (``--only gdn`` writes just this one)
+  bwd.npz      -- gradients of the reference's dense forward
+                  (``fa4_ring/reference.py:29-54``, ``full_causal_reference(backend="torch")``)
+                  by torch autograd, for the ALGO_CASES shapes: q, k, v from seed 0 as above,
+                  the upstream gradient ``randn(N, H, D)`` after ``manual_seed(1)``
+                  (``--only bwd`` writes just this one).  The reference has no backward of
+                  its own (README.md:142); these pin the backward oracle.
 """
 
 import argparse
@@ -81,6 +87,28 @@ def write_gdn(root):
     print(f"wrote {p} ({os.path.getsize(p)} bytes)")
 
 
+def write_bwd(root):
+    from fa4_ring.reference import full_causal_reference  # the reference's module
+    out = {}
+    for i, (n, H, Hkv, D, cp) in enumerate(ALGO_CASES):
+        q, k, v = gen_inputs(n, H, Hkv, D)
+        torch.manual_seed(1)
+        dout = torch.randn(n, H, D)
+        qg, kg, vg = (t.clone().requires_grad_(True) for t in (q, k, v))
+        o = full_causal_reference(qg, kg, vg, softmax_scale=1.0 / math.sqrt(D), backend="torch")
+        dq, dk, dv = torch.autograd.grad(o, (qg, kg, vg), dout)
+        out[f"case{i}_dims"] = np.asarray([n, H, Hkv, D, cp])
+        out[f"case{i}_input_sums"] = np.asarray(
+            [float(t.double().sum()) for t in (q, k, v, dout)])
+        out[f"case{i}_dq"] = dq.numpy()
+        out[f"case{i}_dk"] = dk.numpy()
+        out[f"case{i}_dv"] = dv.numpy()
+    out["n_cases"] = np.asarray(len(ALGO_CASES))
+    p = os.path.join(HERE, "bwd.npz")
+    np.savez_compressed(p, **out)
+    print(f"wrote {p} ({os.path.getsize(p)} bytes)")
+
+
 def load_reference(root):
     sys.path.insert(0, root)
     import fa4_ring.zigzag as zz  # the reference's module
@@ -99,11 +127,15 @@ def gen_inputs(n, H, Hkv, D, seed=0):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="reference checkout root")
-    ap.add_argument("--only", choices=["gdn"], default=None, help="write one fixture only")
+    ap.add_argument("--only", choices=["gdn", "bwd"], default=None,
+                    help="write one fixture only")
     args = ap.parse_args()
     zz, algo = load_reference(os.path.abspath(args.reference))
-    write_gdn(os.path.abspath(args.reference))
-    if args.only == "gdn":
+    if args.only in (None, "gdn"):
+        write_gdn(os.path.abspath(args.reference))
+    if args.only in (None, "bwd"):
+        write_bwd(os.path.abspath(args.reference))
+    if args.only is not None:
         return
     torch.set_num_threads(os.cpu_count() or 1)
 

@@ -212,3 +212,92 @@ def test_gdn_cp_extract_is_the_ring_sharding():
             restore, _, _ = gdn_oracle.gdn_cp_indices(lens, cp, 0)
             gathered = np.concatenate([orc.zigzag_varlen_rows(cu, rr, cp)[0] for rr in range(cp)])
             np.testing.assert_array_equal(gathered[restore], np.arange(cu[-1]))
+
+
+# ---------------------------------------------------------------------------
+# backward: the oracle against autograd through the reference's dense forward
+# ---------------------------------------------------------------------------
+
+def _bwd_case(b, i):
+    n, H, Hkv, D, cp = (int(x) for x in b[f"case{i}_dims"])
+    q, k, v = _inputs(n, H, Hkv, D)
+    torch.manual_seed(1)
+    dout = torch.randn(n, H, D)
+    _check_sums(b[f"case{i}_input_sums"], (q, k, v, dout))
+    return (n, H, Hkv, D, cp), [t.numpy() for t in (q, k, v, dout)]
+
+
+@pytest.mark.parametrize("i", range(7))
+def test_bwd_oracle_matches_reference_autograd(i):
+    from oracle import bwd_oracle as bo
+    b = _load("bwd.npz")
+    (n, H, Hkv, D, cp), (q, k, v, dout) = _bwd_case(b, i)
+    scale = 1.0 / math.sqrt(D)
+    dense = bo.attn_bwd(q, k, v, dout, True, scale)
+    ring = bo.simulate_ring_bwd(q, k, v, dout, cp, scale)
+    for name, d, r in zip(("dq", "dk", "dv"), dense, ring):
+        want = b[f"case{i}_{name}"]
+        np.testing.assert_allclose(d, want, **TOL, err_msg=f"dense {name}")
+        np.testing.assert_allclose(r, want, **TOL, err_msg=f"ring cp={cp} {name}")
+
+
+def test_bwd_oracle_varlen_ring_equals_dense_per_sequence():
+    from oracle import bwd_oracle as bo
+    rng = np.random.default_rng(5)
+    H, Hkv, D, cp = 6, 2, 16, 4
+    lens = [16, 40, 8]
+    full_cu = [0] + list(np.cumsum(lens))
+    N = full_cu[-1]
+    q, dout = rng.standard_normal((N, H, D)), rng.standard_normal((N, H, D))
+    k, v = rng.standard_normal((N, Hkv, D)), rng.standard_normal((N, Hkv, D))
+    scale = 1.0 / math.sqrt(D)
+    # dense, per sequence
+    want = [np.zeros_like(x) for x in (q, k, v)]
+    outs, lses = np.zeros((N, H, D)), np.zeros((N, H))
+    for a, e in zip(full_cu[:-1], full_cu[1:]):
+        g = bo.attn_bwd(q[a:e], k[a:e], v[a:e], dout[a:e], True, scale)
+        for w, x in zip(want, g):
+            w[a:e] = x
+        outs[a:e], lses[a:e] = orc.attn(q[a:e], k[a:e], v[a:e], True, scale, np.float64)
+    # ring over packed zig-zag shards
+    shard = lambda x, r: orc.zigzag_shard_varlen(x, full_cu, r, cp)[0]  # noqa: E731
+    lcu = orc.zigzag_shard_varlen(q, full_cu, 0, cp)[1]
+    ks = [shard(k, r) for r in range(cp)]
+    vs = [shard(v, r) for r in range(cp)]
+    got_q = [None] * cp
+    got_k = [np.zeros_like(x) for x in ks]
+    got_v = [np.zeros_like(x) for x in vs]
+    for rank in range(cp):
+        dq, dkv = bo.ring_rank_bwd(shard(q, rank), ks, vs, shard(dout, rank), shard(outs, rank),
+                                   shard(lses, rank), rank, cp, scale, cu=lcu)
+        got_q[rank] = dq
+        for src, (b2, c2) in dkv.items():
+            got_k[src] += b2
+            got_v[src] += c2
+    for name, w, got in (("dq", want[0], got_q), ("dk", want[1], got_k), ("dv", want[2], got_v)):
+        for r in range(cp):
+            np.testing.assert_allclose(got[r], shard(w, r), atol=1e-10, rtol=1e-10,
+                                       err_msg=f"{name} rank {r}")
+
+
+def test_bwd_planted_mistake_is_caught():
+    """A backward that uses the step's own LSE instead of the final one is wrong: the
+    ring check must see it."""
+    from oracle import bwd_oracle as bo
+    b = _load("bwd.npz")
+    (n, H, Hkv, D, cp), (q, k, v, dout) = _bwd_case(b, 2)
+    scale = 1.0 / math.sqrt(D)
+    ks = [orc.zigzag_shard(k, r, cp) for r in range(cp)]
+    vs = [orc.zigzag_shard(v, r, cp) for r in range(cp)]
+    rank = 1
+    lq, ldo = orc.zigzag_shard(q, rank, cp), orc.zigzag_shard(dout, rank, cp)
+    dq = np.zeros(lq.shape)
+    out, lse = orc.attn(q, k, v, True, scale, np.float64)
+    delta = bo.row_delta(orc.zigzag_shard(out, rank, cp), ldo)
+    for (_s, src, pat) in orc.ring_schedule(rank, cp):
+        _o, step_lse = orc.ring_step(lq, ks[src], vs[src], [0, lq.shape[0]], pat, scale,
+                                     np.float64)
+        dq += bo.ring_step_bwd(lq, ks[src], vs[src], ldo, step_lse, delta, [0, lq.shape[0]], pat,
+                               scale)[0]
+    want = orc.zigzag_shard(b["case2_dq"], rank, cp)
+    assert np.abs(dq - want).max() > 1e-2
