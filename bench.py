@@ -20,6 +20,11 @@ cp=8 (a bounded sample), on the host cores.  ``--impl reference`` times that CPU
 path alone (the reference is pure Python over third-party GPU kernels that are not
 installed here and its GPU orchestration attends wrong KV shards; its own CPU
 simulation is the path that runs).
+
+``--bwd`` measures the ring BACKWARD instead (not in the reference, which is forward-only):
+``ring_flash_attn_backward`` on bf16 cfg2 / cfg4 shards with the forward's (out, lse) and a
+seeded upstream gradient, FLOPs = 2.5x the forward's (5 matmuls of the forward's size, N^2/2
+convention), one JSON line with ``metric`` "causal ring-attn backward TFLOP/s".
 """
 
 import argparse
@@ -499,6 +504,85 @@ def gpu_main(args, rank, world, local_rank):
     return line
 
 
+def bwd_main(args, rank, world, local_rank):
+    """The ring backward, timed like the forward (L2 flushed, CUDA events, max over ranks)."""
+    from fa4_ring import RingConfig, _lib
+    from fa4_ring.ring_attention import ring_flash_attn_with_lse
+    from fa4_ring.ring_backward import ring_flash_attn_backward
+    from fa4_ring.zigzag import zigzag_shard_varlen
+
+    dev = torch.device("cuda", local_rank)
+    C = CONFIGS[args.config]
+    if C["kind"] != "bf16":
+        raise SystemExit("--bwd runs the bf16 configurations (cfg2, cfg4)")
+    Hq, Hkv, D = C["Hq"], C["Hkv"], C["D"]
+    cp = world
+    lens = config_lens(args.config, cp, args.seq_len)
+    full_cu = [0] + [int(x) for x in np.cumsum(lens)]
+    N = full_cu[-1]
+    g = torch.Generator(device=dev).manual_seed(1234)
+    shards, lcu = [], None
+    for h in (Hq, Hkv, Hkv, Hq):  # q, k, v, dout
+        full = torch.randn(N, h, D, generator=g, device=dev, dtype=torch.bfloat16)
+        loc, lcu = zigzag_shard_varlen(full, full_cu, rank, cp)
+        shards.append(loc)
+        del full
+    lq, lk, lv, ldo = shards
+    varlen = len(lens) > 1
+    kw = dict(cu_seqlens=lcu if varlen else None, max_seqlen=max(lens) // cp if varlen else None)
+    cfg = RingConfig(cp_size=cp, cp_rank=rank)
+    out, lse = ring_flash_attn_with_lse(lq, lk, lv, cfg, **kw)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    step_flops = 2.5 * float(sum(causal_flops(n, Hq, D) for n in lens))
+
+    def run():
+        return ring_flash_attn_backward(ldo, lq, lk, lv, out, lse, cfg, **kw)
+
+    for _ in range(args.warmup):
+        run()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    n0 = _lib.launch_count
+    with ClockSampler(local_rank) as clk:
+        for i in range(args.steps):
+            flush.zero_()
+            ev[i][0].record()
+            run()
+            ev[i][1].record()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+    launches = _lib.launch_count - n0
+    ms = torch.tensor([sum(a.elapsed_time(b) for a, b in ev) / args.steps], dtype=torch.float64,
+                      device=dev)
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    status = _lib.device_status()
+    if rank != 0:
+        return None
+    ms_step = ms.item()
+    value = step_flops / (ms_step * 1e-3) / 1e12
+    peaks, peaks_kind = load_peaks()
+    peak = peaks["bf16_tflops"]
+    return {
+        "metric": "causal ring-attn backward TFLOP/s (dq, dk, dv; 2.5x forward FLOPs)",
+        "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded randn q, k, v, dout)",
+        "config": {"workload": f"{args.config} backward: {C['text']}", "cp": cp,
+                   "l2": "flushed (256 MiB write) before every timed step"},
+        "roofline": {"bound": "tensor", "achieved": round(value / world, 2), "peak": peak,
+                     "unit": "TFLOP/s", "frac": round(value / world / peak, 4),
+                     "traffic": None, "note": f"whole backward step per GPU (all kernels), "
+                     f"of {peaks_kind} bf16 burst peak"},
+        "gpu_launches": launches, "clocks": clk.summary(), "device_status": int(status),
+    }
+
+
 def _traffic_from_profile(config, world):
     """DRAM bytes per attention launch recorded from an ncu capture of this workload
     (profiles/attn_fwd_traffic.json), or None when none was captured."""
@@ -621,6 +705,8 @@ def main():
                          "forward to stderr")
     ap.add_argument("--aux", action="store_true",
                     help="only the HBM-bound kernels (merges, zig-zag) against the HBM peak")
+    ap.add_argument("--bwd", action="store_true",
+                    help="time the ring backward (bf16 cfg2 / cfg4) instead of the forward")
     ap.add_argument("--quick", action="store_true",
                     help="profiling run: timed loop only (no e2e, no CPU baseline)")
     args = ap.parse_args()
@@ -650,7 +736,7 @@ def main():
     ring_attention.RING_TRANSPORT = args.transport
     ring_attention.RING_FUSED = {"fused": True, "fused-16bit": "16bit", "steps": False}[args.ring_kernel]
     try:
-        line = gpu_main(args, rank, world, local_rank)
+        line = (bwd_main if args.bwd else gpu_main)(args, rank, world, local_rank)
     finally:
         if world > 1:
             from fa4_ring.comm import close_native_rings

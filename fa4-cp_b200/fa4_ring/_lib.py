@@ -85,6 +85,11 @@ _SIGNATURES = {
     "fa4cp_ring_timing_read": [_i64, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(_i32)],
     "fa4cp_ring_attn_fwd": [_i64, _vp, _vp, _vp, _vp, _i64, _vp, _vp, _vp, _i32, _i32, _i64, _i32,
                             _i32, _i32, _i32, _i32, _f32, _vp, _vp, _vp, _vp, _i64, _vp],
+    "fa4cp_attn_bwd_preprocess": [_vp, _vp, _vp, _i64, _i32, _i32, _i32, _vp],
+    "fa4cp_attn_bwd": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i64,
+                       _i64, _i32, _i32, _i32, _i32, _i32, _i32, _f32, _vp],
+    "fa4cp_convert_f32": [_vp, _vp, _i64, _i32, _vp],
+    "fa4cp_add_f32": [_vp, _vp, _i64, _vp],
 }
 _RESTYPE = {"fa4cp_last_error": ctypes.c_char_p, "fa4cp_attn_kv8_workspace_bytes": _i64}
 

@@ -139,6 +139,85 @@ class KVRing:
             self.consumed[s] = ev
 
 
+class GradRing:
+    """The rotating fp32 dK/dV accumulators of the ring backward.
+
+    At step ``s`` a rank computes the gradient contribution of its queries to the K/V of
+    source ``(rank - s) mod S`` into a fresh buffer (:meth:`fresh`), then :meth:`pass_on`
+    adds the accumulator of the same source that ``rank - 1`` passed on after ITS step
+    ``s - 1``, and sends the sum to ``rank + 1``.  A source's accumulator therefore starts
+    on the source itself (step 0) and visits every rank once; the pass after step ``S - 1``
+    delivers it, complete, to its owner (:meth:`finish`).  ``S`` passes of
+    ``2 * T * H_kv * D * 4`` bytes.
+
+    On CUDA every pass is an NCCL send/recv on the comm stream (the one :class:`KVRing`
+    uses, so the two rotations are issued in one order on every rank), ordered by events:
+    the pass of step ``s`` waits for the step's add on the compute stream; the add of step
+    ``s`` waits for the pass of step ``s - 1``, which delivered its input.  Two compute
+    buffers alternate, so step ``s + 1`` computes while the pass of step ``s`` is in
+    flight; one receive buffer suffices because a pass is issued only after the add that
+    read the previous one.  With a CPU group (gloo) the passes block.
+    """
+
+    def __init__(self, shape, cp_rank: int, cp_size: int, device: torch.device,
+                 group: Optional["dist.ProcessGroup"] = None):
+        assert cp_size >= 2, "a ring needs at least two ranks"
+        self.S = cp_size
+        self.group = group
+        self.device = device
+        self.send_to = _global_rank(group, (cp_rank + 1) % cp_size)
+        self.recv_from = _global_rank(group, (cp_rank - 1) % cp_size)
+        self.cuda = device.type == "cuda"
+        self.bufs = [torch.empty(shape, dtype=torch.float32, device=device) for _ in range(2)]
+        self.recv = torch.empty(shape, dtype=torch.float32, device=device)
+        self.stream = comm_stream(device) if self.cuda else None
+        self.passed: Dict[int, Optional[torch.cuda.Event]] = {}
+
+    def _current(self):
+        return torch.cuda.current_stream(self.device)
+
+    def fresh(self, s: int) -> torch.Tensor:
+        """A zeroed fp32 buffer for step ``s``'s contribution."""
+        buf = self.bufs[s % 2]
+        prev = self.passed.get(s - 2)
+        if self.cuda and prev is not None:
+            self._current().wait_event(prev)  # its last send (step s - 2) is done
+        buf.zero_()
+        return buf
+
+    def pass_on(self, s: int, buf: torch.Tensor, add) -> None:
+        """``buf`` holds step ``s``'s contribution (enqueued on the current stream): add the
+        accumulator received for this source with ``add(dst, src)`` (from step 1 on), send
+        the sum to ``rank + 1`` and receive the accumulator of the next step's source."""
+        if s > 0:
+            if self.cuda:
+                self._current().wait_event(self.passed[s - 1])
+            add(buf, self.recv)
+        ops = [dist.P2POp(dist.isend, buf, self.send_to, group=self.group),
+               dist.P2POp(dist.irecv, self.recv, self.recv_from, group=self.group)]
+        if self.cuda:
+            ready = torch.cuda.Event()
+            ready.record(self._current())
+            with torch.cuda.stream(self.stream):
+                self.stream.wait_event(ready)
+                for req in dist.batch_isend_irecv(ops):
+                    req.wait()
+                ev = torch.cuda.Event()
+                ev.record(self.stream)
+            self.passed[s] = ev
+        else:
+            for req in dist.batch_isend_irecv(ops):
+                req.wait()
+            self.passed[s] = None
+
+    def finish(self) -> torch.Tensor:
+        """The complete accumulator of this rank's own K/V (after the pass of step S-1)."""
+        assert (self.S - 1) in self.passed, "every step must be passed on first"
+        if self.cuda:
+            self._current().wait_event(self.passed[self.S - 1])
+        return self.recv
+
+
 class NativeRing:
     """The library's native ring executor (``fa4cp_ring_*``) for one cp group on one GPU.
 

@@ -92,24 +92,31 @@ def ring_flash_attn(
     ``max_seqlen`` (max local shard length).  ``cu_seqlens`` given on the host is
     validated (even lengths); a CUDA ``cu_seqlens`` is trusted, to avoid a sync.
     Output dtype: the input dtype, or bf16 for e4m3 inputs.
+
+    Differentiable (not in the reference, which is forward-only): when grad mode is on and
+    any of q, k, v requires grad (f16 / bf16, head_dim 64 or 128), the call records the
+    ring backward of :mod:`.ring_backward` for autograd.
     """
+    if torch.is_grad_enabled() and any(t.requires_grad for t in (local_q, local_k, local_v)):
+        return _RingFlashAttnFn.apply(local_q, local_k, local_v, cfg, group, descales,
+                                      cu_seqlens, max_seqlen)
+    return ring_flash_attn_with_lse(local_q, local_k, local_v, cfg, group=group,
+                                    descales=descales, cu_seqlens=cu_seqlens,
+                                    max_seqlen=max_seqlen)[0]
+
+
+def ring_flash_attn_with_lse(local_q, local_k, local_v, cfg: RingConfig, *, group=None,
+                             descales: Optional[Descales] = None, cu_seqlens=None,
+                             max_seqlen=None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """:func:`ring_flash_attn` returning ``(out [T, H, D], lse [T, H])``: the final
+    natural-log LSE of every local row (what :func:`.ring_backward.ring_flash_attn_backward`
+    takes).  No autograd."""
     _check_qkv(local_q, local_k, local_v)
     S, rank = cfg.cp_size, cfg.cp_rank
     T, Hq, D = local_q.shape
     assert local_k.shape[0] == T, "q and kv shards must have the same token count"
     dev = local_q.device
-
-    if cu_seqlens is None:
-        assert T % 2 == 0, "the local shard length must be even (zig-zag)"
-        cu = _single_cu(T, dev)
-        max_seqlen = T
-    else:
-        assert max_seqlen is not None, "max_seqlen required when cu_seqlens is given"
-        if not cu_seqlens.is_cuda:
-            _validate_cu(cu_seqlens)
-        cu = cu_seqlens.to(device=dev, dtype=torch.int32).contiguous()
-    nseq = cu.numel() - 1
-    max_seqlen = int(max_seqlen)
+    cu, nseq, max_seqlen = local_cu_args(T, dev, cu_seqlens, max_seqlen)
 
     k0 = local_k.contiguous()
     v0 = local_v.contiguous()
@@ -128,7 +135,41 @@ def ring_flash_attn(
             ring.done(step)
 
     return ring_forward(local_q, kv_at, step_done, cfg, cu=cu, nseq=nseq, max_seqlen=max_seqlen,
-                        descales=descales)
+                        descales=descales, return_lse=True)
+
+
+def local_cu_args(T: int, dev, cu_seqlens, max_seqlen) -> Tuple[torch.Tensor, int, int]:
+    """``(cu int32 on dev, nseq, max_seqlen)`` of a local shard (one sequence when
+    ``cu_seqlens`` is None)."""
+    if cu_seqlens is None:
+        assert T % 2 == 0, "the local shard length must be even (zig-zag)"
+        return _single_cu(T, dev), 1, T
+    assert max_seqlen is not None, "max_seqlen required when cu_seqlens is given"
+    if not cu_seqlens.is_cuda:
+        _validate_cu(cu_seqlens)
+    cu = cu_seqlens.to(device=dev, dtype=torch.int32).contiguous()
+    return cu, cu.numel() - 1, int(max_seqlen)
+
+
+class _RingFlashAttnFn(torch.autograd.Function):
+    """Autograd node of :func:`ring_flash_attn`: the forward keeps (q, k, v, out, lse); the
+    backward runs the ring backward over the same group."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, cfg, group, descales, cu_seqlens, max_seqlen):
+        out, lse = ring_flash_attn_with_lse(q, k, v, cfg, group=group, descales=descales,
+                                            cu_seqlens=cu_seqlens, max_seqlen=max_seqlen)
+        ctx.save_for_backward(q, k, v, out, lse)
+        ctx.cfg, ctx.group, ctx.cu, ctx.max_seqlen = cfg, group, cu_seqlens, max_seqlen
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        from .ring_backward import ring_flash_attn_backward
+        q, k, v, out, lse = ctx.saved_tensors
+        dq, dk, dv = ring_flash_attn_backward(dout, q, k, v, out, lse, ctx.cfg, group=ctx.group,
+                                              cu_seqlens=ctx.cu, max_seqlen=ctx.max_seqlen)
+        return dq, dk, dv, None, None, None, None, None
 
 
 # Run incremental-mode rings over an NCCL group through the native executor
@@ -189,16 +230,17 @@ def _native_forward(q, k, v, cfg: RingConfig, group, *, cu, nseq, max_seqlen,
              and ((q.dtype in (torch.float16, torch.bfloat16) and D in (64, 128))
                   or (RING_FUSED is True and q.dtype == torch.float8_e4m3fn and D == 128)))
     _lib.count_launches(1 if fused else S * (3 if ws is not None else 1))
-    return out
+    return out, lse
 
 
 def ring_forward(local_q, kv_at, step_done, cfg: RingConfig, *, cu: torch.Tensor, nseq: int,
-                 max_seqlen: int, descales: Optional[Descales] = None) -> torch.Tensor:
+                 max_seqlen: int, descales: Optional[Descales] = None, return_lse: bool = False):
     """The per-step compute of :func:`ring_flash_attn` for one rank.
 
     ``kv_at(step)`` returns the (K, V) that originated on ``(rank - step) mod S`` (the
     ring supplies it after its hop; a single-GPU test supplies every rank's shard
     directly); ``step_done(step)`` is called after the step's kernels are enqueued.
+    Returns ``out``, or ``(out, lse)`` with ``return_lse``.
     """
     S, rank = cfg.cp_size, cfg.cp_rank
     T, Hq, D = local_q.shape
@@ -250,7 +292,8 @@ def ring_forward(local_q, kv_at, step_done, cfg: RingConfig, *, cu: torch.Tensor
 
     if batched and len(partials) > 1:
         final = torch.empty((T, Hq, D), dtype=out_dt, device=dev)
+        final_lse = torch.empty((T, Hq), dtype=torch.float32, device=dev)
         merge_states([p[0] for p in partials], [p[1] for p in partials], out=final,
-                     lse_out=torch.empty((T, Hq), dtype=torch.float32, device=dev))
-        return final
-    return out
+                     lse_out=final_lse)
+        return (final, final_lse) if return_lse else final
+    return (out, lse) if return_lse else out

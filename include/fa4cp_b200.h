@@ -410,6 +410,42 @@ FA4CP_API int fa4cp_ring_attn_fwd(int64_t handle, const void* q, const void* k, 
                                   const float* k_descales, const float* v_descales,
                                   void* workspace, int64_t workspace_bytes, void* stream);
 
+/*
+ * Attention BACKWARD of one ring step.  No counterpart in the reference, which is
+ * forward-only (README.md:142: "forward-only (inference). No backward"); these are the
+ * gradients of its forward (tests/test_algorithm_cpu.py:36-48) over the rows of the step
+ * patterns of fa4_ring/ring_attention.py:109-166.  f16 / bf16, head_dim 64 or 128.
+ *
+ * fa4cp_attn_bwd_preprocess: delta[row, h] = sum_d dout * out   (float32 [total_q, Hq]);
+ *   out, dout [total_q, Hq, D] in `dtype`, 4-byte aligned.
+ * fa4cp_attn_bwd: ADDS one step's gradient contributions into float32 accumulators:
+ *   dq_acc [total_q, Hq, D]  (added with atomics: every key tile adds into a query row)
+ *   dk_acc, dv_acc [total_k, Hkv, D]  (read-add-write; a key row has one writer per launch)
+ *   lse   float32 [total_q, Hq], natural log, of the FINAL output (so the steps' gradients
+ *         add up); rows with lse -inf contribute nothing
+ *   delta from fa4cp_attn_bwd_preprocess on the final output
+ *   cu_q, cu_k, pattern, causal, softmax_scale: as fa4cp_attn_fwd (the step's rows)
+ *   max_seqlen_k upper bound on any sequence's key count under `pattern` (sizes the grid:
+ *         VARLEN max cu_k length; FRONT_KV half the max local length; BACK_Q the max)
+ *   16-byte aligned q, k, v, dout and accumulators.  dq_acc's sums are fp32 atomics, so
+ *   their rounding order (not the math) varies between runs.
+ * fa4cp_convert_f32: dst (f16 | bf16 | f32) = src (float32), n elements.
+ * fa4cp_add_f32: dst += src, n float32 elements, n % 4 == 0, 16-byte aligned.
+ */
+FA4CP_API int fa4cp_attn_bwd_preprocess(const void* out, const void* dout, float* delta,
+                                        int64_t total_q, int32_t num_heads_q, int32_t head_dim,
+                                        int32_t dtype, void* stream);
+FA4CP_API int fa4cp_attn_bwd(const void* q, const void* k, const void* v, const void* dout,
+                             const float* lse, const float* delta, float* dq_acc, float* dk_acc,
+                             float* dv_acc, const int32_t* cu_q, const int32_t* cu_k,
+                             int32_t nseq, int32_t max_seqlen_k, int64_t total_q, int64_t total_k,
+                             int32_t num_heads_q, int32_t num_heads_kv, int32_t head_dim,
+                             int32_t dtype, int32_t pattern, int32_t causal, float softmax_scale,
+                             void* stream);
+FA4CP_API int fa4cp_convert_f32(const float* src, void* dst, int64_t n, int32_t dst_dtype,
+                                void* stream);
+FA4CP_API int fa4cp_add_f32(float* dst, const float* src, int64_t n, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

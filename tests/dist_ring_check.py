@@ -9,9 +9,11 @@ the Python step loop over ``KVRing``, and in ``batched`` mode; FP8 e4m3 Q/K/V an
 with e4m3 K/V (quantised per rank, descales all-gathered by source rank) through the
 native executor, checked against the dense attention of the dequantised tensors.  The
 copy-engine cases run twice in a row (the hop counters carry over between calls), and
-the packed case makes the receive slots grow.  Tolerances: bf16 2e-2, FP8 6e-2.  Last, the
-GDN all-gather CP wrapper (``fa4_ring.gdn_cp.gdn_cp_allgather``) against the single-device
-scan, exactly.
+the packed case makes the receive slots grow.  Tolerances: bf16 2e-2, FP8 6e-2.  Then the
+ring backward (autograd through ``ring_flash_attn``: K/V hops plus the rotating fp32 dK/dV
+accumulators over NCCL) against the oracle's dense gradient, within 2e-2 * max(1, max|ref|).
+Last, the GDN all-gather CP wrapper (``fa4_ring.gdn_cp.gdn_cp_allgather``) against the
+single-device scan, exactly.
 """
 
 import datetime
@@ -108,6 +110,30 @@ def main():
                         print(f"world={world} seqs={num_seqs} {kind} mode={mode} "
                               f"executor={executor} seq{j} max_err={err:.3e}")
                         ok &= err <= tol
+            # backward through autograd: dq, dk, dv of every rank's shards
+            ring_attention.NATIVE_EXECUTOR = True
+            ring_attention.RING_TRANSPORT = "copy_engine"
+            ring_attention.RING_FUSED = True
+            gd = torch.Generator().manual_seed(99)
+            dout_full = torch.randn(cu[-1], H, D, generator=gd).bfloat16().to(dev)
+            ldo = (zigzag_shard(dout_full, rank, world) if num_seqs == 1
+                   else zigzag_shard_varlen(dout_full, cu, rank, world)[0])
+            leaves = [t.clone().requires_grad_(True) for t in (lq, lk, lv)]
+            out = ring_flash_attn(*leaves, RingConfig(cp_size=world, cp_rank=rank), **kw)
+            out.backward(ldo)
+            grads = [gather_full(t.grad, world, cu, num_seqs) for t in leaves]
+            ins = [gather_full(t, world, cu, num_seqs) for t in (lq, lk, lv, ldo)]
+            if rank == 0:
+                from oracle import bwd_oracle as bo
+                for j in range(len(lens)):
+                    a, b = cu[j], cu[j + 1]
+                    refs = bo.attn_bwd(*(x[a:b].astype(np.float64) for x in ins), True, scale)
+                    for name, gfull, ref in zip(("dq", "dk", "dv"), grads, refs):
+                        mag = max(1.0, float(np.abs(ref).max()))
+                        err = float(np.abs(gfull[a:b] - ref).max())
+                        print(f"world={world} seqs={num_seqs} backward seq{j} {name} "
+                              f"max_err={err:.3e} (max|ref| {mag:.2f})")
+                        ok &= err <= 2e-2 * mag
         # GDN all-gather CP (Plan A): the CP output equals the single-device scan, exactly
         from fa4_ring.gdn_cp import build_gdn_cp_metadata, gdn_cp_allgather
         lens = [2 * world * n for n in (5, 12)]

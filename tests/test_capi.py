@@ -72,6 +72,23 @@ def test_attn_argument_validation(lib, args, needle):
     assert needle in lib.fa4cp_last_error()
 
 
+def test_backward_argument_validation(lib):
+    dummy = ctypes.c_void_p(16)
+
+    def bwd(dtype=1, pattern=0, hq=8, hkv=2, d=128):
+        return lib.fa4cp_attn_bwd(dummy, dummy, dummy, dummy, dummy, dummy, dummy, dummy, dummy,
+                                  dummy, dummy, 1, 128, 128, 128, hq, hkv, d, dtype, pattern, 1,
+                                  0.1, None)
+
+    assert bwd(dtype=3) == -1 and b"f16 or bf16" in lib.fa4cp_last_error()  # no e4m3 backward
+    assert bwd(pattern=5) == -1 and b"pattern" in lib.fa4cp_last_error()
+    assert bwd(hq=6, hkv=4) == -1 and b"multiple" in lib.fa4cp_last_error()
+    assert bwd(d=256) == -2 and b"head_dim" in lib.fa4cp_last_error()        # unsupported
+    assert lib.fa4cp_attn_bwd_preprocess(dummy, dummy, dummy, 4, 2, 128, 2, None) == -1
+    assert lib.fa4cp_add_f32(dummy, dummy, 6, None) == -1                     # 6 % 4 != 0
+    assert lib.fa4cp_convert_f32(dummy, dummy, 4, 3, None) == -1              # no e4m3 target
+
+
 def test_zigzag_argument_validation(lib):
     dummy = ctypes.c_void_p(16)
     assert lib.fa4cp_zigzag_shard(dummy, dummy, None, 1, 10, 0, 2, 4, None) == -1  # 10 % 4 != 0
