@@ -12,9 +12,11 @@
 // Kernel layout (one CTA = 128 keys of one kv head of one sequence, 8 warps x 16 keys):
 //   * the CTA's K and V tiles stay in shared memory for its whole life;
 //   * it walks the query heads of its GQA group and, per head, the 32-row query tiles that can
-//     see its keys (causal: from the first visible tile on), staging Q, dO, LSE, Delta;
-//   * each warp computes S^T and dP^T for its 16 keys (mma.sync m16n8k16, fp32 accumulators),
-//     forms P^T and dS^T in registers, and accumulates dV and dK for its keys in registers;
+//     see its keys (causal: from the first visible tile on); Q, dO, LSE and Delta of the next
+//     tile load with cp.async (double-buffered) while the current one computes;
+//   * each warp computes S^T and dP^T for its 16 keys (mma.sync m16n8k16, fp32 accumulators,
+//     operand fragments by ldmatrix, transposed where the operand is stored k-major), forms
+//     P^T and dS^T in registers, and accumulates dV and dK for its keys in registers;
 //   * dS^T goes through shared memory so that all 8 warps compute the tile's dQ = dS K, which is
 //     added to an fp32 dQ accumulator in HBM with vector atomics (many key tiles add into one
 //     query row);
@@ -61,9 +63,34 @@ template <> struct Mma16<__half> {
 __device__ __forceinline__ uint32_t ld_pair(const uint16_t* p) {
   return *reinterpret_cast<const uint32_t*>(p);
 }
-// two 16-bit elements from different rows: lo in the low half
-__device__ __forceinline__ uint32_t ld_split(const uint16_t* lo, const uint16_t* hi) {
-  return uint32_t(*lo) | (uint32_t(*hi) << 16);
+
+// four 8x8 16-bit matrices from shared memory; lanes 8m..8m+7 give the row addresses of
+// matrix m.  Plain: thread t receives row t/4, columns 2(t%4), 2(t%4)+1 of each matrix;
+// .trans: rows 2(t%4), 2(t%4)+1 of column t/4.
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+// asynchronous global -> shared copies; src_bytes 0 reads nothing and zero-fills
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
+               "r"(src_bytes));
+}
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src, int src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src),
+               "r"(src_bytes));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N));
 }
 
 struct BwdParams {
@@ -109,33 +136,37 @@ __device__ __forceinline__ BwdGeo bwd_geometry(const BwdParams& p, int seq) {
   return g;
 }
 
+// shared memory (16-bit elements unless noted): K and V tiles for the CTA's life; Q and dO
+// tiles double-buffered (the next query tile loads while this one computes); the dS^T tile;
+// then LSE and Delta rows (float, double-buffered)
 template <int D>
 struct BwdSmem {
-  static constexpr int LDK = D + 8;            // row pitch of K / V / Q / dO tiles (elements)
+  static constexpr int LDK = D + 8;            // row pitch of K / V / Q / dO tiles
   static constexpr int LDS = kBwdBM + 8;       // row pitch of the dS^T tile
+  static constexpr int TILE = kBwdBM * LDK;    // one Q or dO tile
   static constexpr int K_OFF = 0;
   static constexpr int V_OFF = K_OFF + kBwdBN * LDK;
   static constexpr int Q_OFF = V_OFF + kBwdBN * LDK;
-  static constexpr int O_OFF = Q_OFF + kBwdBM * LDK;
-  static constexpr int S_OFF = O_OFF + kBwdBM * LDK;
+  static constexpr int O_OFF = Q_OFF + 2 * TILE;
+  static constexpr int S_OFF = O_OFF + 2 * TILE;
   static constexpr int HALVES = S_OFF + kBwdBN * LDS;
-  static constexpr int BYTES = HALVES * 2 + 2 * kBwdBM * 4;   // + LSE and Delta rows
-  static_assert((LDK * 2) % 16 == 0 && (HALVES * 2) % 16 == 0, "16-byte rows");
+  static constexpr int BYTES = HALVES * 2 + 2 * 2 * kBwdBM * 4;
+  static_assert((LDK * 2) % 16 == 0 && (LDS * 2) % 16 == 0 && (HALVES * 2) % 16 == 0,
+                "16-byte rows");
 };
 
-// rows [row0, row0 + nrows) of a [rows, heads, D] tensor, head `h`, into a pitch-LDK tile;
-// rows at or past `valid` are zero-filled
+// rows [row0, row0 + nrows) of a [rows, heads, D] tensor, head `h`, into a pitch-LDK tile
+// with cp.async; rows at or past `valid` are zero-filled (no global read)
 template <int D, int NROWS>
-__device__ __forceinline__ void stage_rows(uint16_t* dst, const uint16_t* src, int64_t row0,
-                                           int valid, int heads, int h) {
+__device__ __forceinline__ void stage_rows_async(uint16_t* dst, const uint16_t* src,
+                                                 int64_t row0, int valid, int heads, int h) {
   constexpr int CPR = D / 8;  // 16-byte chunks per row
   constexpr int LDK = BwdSmem<D>::LDK;
   for (int c = threadIdx.x; c < NROWS * CPR; c += kBwdThreads) {
     const int r = c / CPR, col = (c % CPR) * 8;
-    uint4 val = make_uint4(0u, 0u, 0u, 0u);
-    if (r < valid)
-      val = *reinterpret_cast<const uint4*>(src + ((row0 + r) * heads + h) * int64_t(D) + col);
-    *reinterpret_cast<uint4*>(dst + r * LDK + col) = val;
+    const bool ok = r < valid;
+    const uint16_t* g = ok ? src + ((row0 + r) * heads + h) * int64_t(D) + col : src;
+    cp_async16(smem_u32(dst + r * LDK + col), g, ok ? 16 : 0);
   }
 }
 
@@ -146,6 +177,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) attn_bwd_kernel(const BwdParam
   constexpr int NT_D = D / 8;          // n-tiles over the head dim
   constexpr int NT_Q = kBwdBM / 8;     // n-tiles over a query tile
   constexpr int NQ = NT_D / 4;         // dQ n-tiles per warp (2 m-tiles x 4 warp columns)
+  static_assert(NT_Q % 2 == 0 && NQ % 2 == 0, "n-tiles are loaded in pairs");
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint16_t* sh = reinterpret_cast<uint16_t*>(smem_raw);
   uint16_t* sK = sh + SM::K_OFF;
@@ -153,8 +185,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1) attn_bwd_kernel(const BwdParam
   uint16_t* sQ = sh + SM::Q_OFF;
   uint16_t* sO = sh + SM::O_OFF;
   uint16_t* sS = sh + SM::S_OFF;
-  float* sL = reinterpret_cast<float*>(sh + SM::HALVES);
-  float* sD = sL + kBwdBM;
+  float* sL = reinterpret_cast<float*>(sh + SM::HALVES);  // [2][BM] raw LSE
+  float* sD = sL + 2 * kBwdBM;                             // [2][BM] Delta
 
   const int seq = blockIdx.z, hk = blockIdx.y;
   const BwdGeo geo = bwd_geometry(p, seq);
@@ -167,17 +199,37 @@ __global__ void __launch_bounds__(kBwdThreads, 1) attn_bwd_kernel(const BwdParam
     q_first = (q_first / kBwdBM) * kBwdBM;
   }
   if (q_first >= geo.ql) return;
+  const int n_qt = (geo.ql - q_first + kBwdBM - 1) / kBwdBM;  // query tiles per head
+  const int n_tiles = p.group * n_qt;                         // over the group's heads
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, tq = lane & 3;
+  const int lm = lane >> 3, lr = lane & 7;  // ldmatrix: matrix and row this lane addresses
   const uint16_t* gq = static_cast<const uint16_t*>(p.q);
   const uint16_t* gk = static_cast<const uint16_t*>(p.k);
   const uint16_t* gv = static_cast<const uint16_t*>(p.v);
   const uint16_t* gdo = static_cast<const uint16_t*>(p.dout);
 
+  // K / V (in the first cp.async group, with query tile 0)
   const int kvalid = geo.kl - k0 < kBwdBN ? geo.kl - k0 : kBwdBN;
-  stage_rows<D, kBwdBN>(sK, gk, int64_t(geo.ks) + k0, kvalid, p.Hkv, hk);
-  stage_rows<D, kBwdBN>(sV, gv, int64_t(geo.ks) + k0, kvalid, p.Hkv, hk);
+  stage_rows_async<D, kBwdBN>(sK, gk, int64_t(geo.ks) + k0, kvalid, p.Hkv, hk);
+  stage_rows_async<D, kBwdBN>(sV, gv, int64_t(geo.ks) + k0, kvalid, p.Hkv, hk);
+
+  auto stage_tile = [&](int t, int buf) {
+    const int hq = hk * p.group + t / n_qt;
+    const int q0 = q_first + (t % n_qt) * kBwdBM;
+    const int qvalid = geo.ql - q0 < kBwdBM ? geo.ql - q0 : kBwdBM;
+    stage_rows_async<D, kBwdBM>(sQ + buf * SM::TILE, gq, int64_t(geo.qs) + q0, qvalid, p.Hq, hq);
+    stage_rows_async<D, kBwdBM>(sO + buf * SM::TILE, gdo, int64_t(geo.qs) + q0, qvalid, p.Hq, hq);
+    if (threadIdx.x < kBwdBM) {
+      const int r = threadIdx.x;
+      const bool ok = r < qvalid;
+      const int64_t idx = ok ? (int64_t(geo.qs) + q0 + r) * p.Hq + hq : 0;
+      cp_async4(smem_u32(sL + buf * kBwdBM + r), p.lse + idx, ok ? 4 : 0);
+      cp_async4(smem_u32(sD + buf * kBwdBM + r), p.delta + idx, ok ? 4 : 0);
+    }
+    cp_async_commit();
+  };
 
   float dk[NT_D][4], dv[NT_D][4];
 #pragma unroll
@@ -188,133 +240,143 @@ __global__ void __launch_bounds__(kBwdThreads, 1) attn_bwd_kernel(const BwdParam
   const int krow = warp * 16 + g;     // this thread's first key row in the tile (then + 8)
   const int key0 = k0 + krow;         // its position in the sequence's key range
   const int shift = geo.kl - geo.ql;  // causal alignment (bottom-right)
+  const uint32_t sK_a = smem_u32(sK), sV_a = smem_u32(sV), sS_a = smem_u32(sS);
+  // byte offsets of this lane's ldmatrix row address within a tile
+  //   A (16 K/V rows of the warp x 16 columns): matrices (rows +0/+8) x (columns +0/+8)
+  const uint32_t a_off = uint32_t(((warp * 16 + (lm & 1) * 8 + lr) * LDK + (lm >> 1) * 8) * 2);
+  //   B from row-major [n][k] (Q, dO as the n side): n-tile pair x (k +0/+8)
+  const uint32_t b_off = uint32_t((((lm >> 1) * 8 + lr) * LDK + (lm & 1) * 8) * 2);
+  //   B from row-major [k][n] (dO, Q, K as the k side), transposed: (k +0/+8) x n-tile pair
+  const uint32_t bt_off = uint32_t((((lm & 1) * 8 + lr) * LDK + (lm >> 1) * 8) * 2);
 
-  for (int hh = 0; hh < p.group; ++hh) {
-    const int hq = hk * p.group + hh;
-    for (int q0 = q_first; q0 < geo.ql; q0 += kBwdBM) {
-      const int qvalid = geo.ql - q0 < kBwdBM ? geo.ql - q0 : kBwdBM;
-      __syncthreads();  // the previous tile's readers of sQ / sO / sS / sL / sD are done
-      stage_rows<D, kBwdBM>(sQ, gq, int64_t(geo.qs) + q0, qvalid, p.Hq, hq);
-      stage_rows<D, kBwdBM>(sO, gdo, int64_t(geo.qs) + q0, qvalid, p.Hq, hq);
-      if (threadIdx.x < kBwdBM) {
-        const int r = threadIdx.x;
-        float l2 = __builtin_huge_valf(), dl = 0.f;
-        if (r < qvalid) {
-          const int64_t idx = (int64_t(geo.qs) + q0 + r) * p.Hq + hq;
-          const float l = p.lse[idx];
-          if (l != -__builtin_huge_valf()) l2 = l * kLog2e;  // a row that sees no key: P = 0
-          dl = p.delta[idx];
+  stage_tile(0, 0);
+  for (int t = 0; t < n_tiles; ++t) {
+    const int buf = t & 1;
+    if (t + 1 < n_tiles) {
+      stage_tile(t + 1, buf ^ 1);  // its buffer's last readers finished before the last barrier
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();  // tile t (and K / V) visible to every thread
+    const int hq = hk * p.group + t / n_qt;
+    const int q0 = q_first + (t % n_qt) * kBwdBM;
+    const int qvalid = geo.ql - q0 < kBwdBM ? geo.ql - q0 : kBwdBM;
+    const uint32_t sQ_a = smem_u32(sQ + buf * SM::TILE), sO_a = smem_u32(sO + buf * SM::TILE);
+    const float* lse_t = sL + buf * kBwdBM;
+    const float* del_t = sD + buf * kBwdBM;
+
+    // S^T = K Q^T and dP^T = V dO^T for this warp's 16 keys x 32 queries
+    float s[NT_Q][4], dp[NT_Q][4];
+#pragma unroll
+    for (int n = 0; n < NT_Q; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) s[n][e] = dp[n][e] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      uint32_t ak[4], av[4];
+      ldsm_x4(ak, sK_a + a_off + kk * 32);
+      ldsm_x4(av, sV_a + a_off + kk * 32);
+#pragma unroll
+      for (int np = 0; np < NT_Q / 2; ++np) {
+        const uint32_t off = b_off + uint32_t((np * 16 * LDK + kk * 16) * 2);
+        uint32_t bq[4], bo[4];
+        ldsm_x4(bq, sQ_a + off);
+        ldsm_x4(bo, sO_a + off);
+        Mma16<T>::mma(s[2 * np], ak, bq[0], bq[1]);
+        Mma16<T>::mma(s[2 * np + 1], ak, bq[2], bq[3]);
+        Mma16<T>::mma(dp[2 * np], av, bo[0], bo[1]);
+        Mma16<T>::mma(dp[2 * np + 1], av, bo[2], bo[3]);
+      }
+    }
+
+    // P^T and dS^T (element e: key row krow + 8*(e>>1), query column n*8 + 2*tq + (e&1))
+#pragma unroll
+    for (int n = 0; n < NT_Q; ++n) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int qi = n * 8 + 2 * tq + (e & 1);
+        const int key = key0 + ((e & 2) ? 8 : 0);
+        const float l = lse_t[qi];
+        // a row that sees no key (LSE -inf) or lies past the tile's rows contributes nothing
+        const bool vis = qi < qvalid && l != -__builtin_huge_valf() && key < geo.kl &&
+                         (!p.causal || key <= q0 + qi + shift);
+        const float pr = vis ? ex2_approx(s[n][e] * p.scale_log2 - l * kLog2e) : 0.f;
+        s[n][e] = pr;
+        dp[n][e] = pr * (dp[n][e] - del_t[qi]);
+      }
+    }
+
+    // dV += P^T dO and dK += dS^T Q (k = the 32 queries of the tile)
+#pragma unroll
+    for (int kk = 0; kk < kBwdBM / 16; ++kk) {
+      const uint32_t ap[4] = {Mma16<T>::pack(s[2 * kk][0], s[2 * kk][1]),
+                              Mma16<T>::pack(s[2 * kk][2], s[2 * kk][3]),
+                              Mma16<T>::pack(s[2 * kk + 1][0], s[2 * kk + 1][1]),
+                              Mma16<T>::pack(s[2 * kk + 1][2], s[2 * kk + 1][3])};
+      const uint32_t ad[4] = {Mma16<T>::pack(dp[2 * kk][0], dp[2 * kk][1]),
+                              Mma16<T>::pack(dp[2 * kk][2], dp[2 * kk][3]),
+                              Mma16<T>::pack(dp[2 * kk + 1][0], dp[2 * kk + 1][1]),
+                              Mma16<T>::pack(dp[2 * kk + 1][2], dp[2 * kk + 1][3])};
+#pragma unroll
+      for (int jp = 0; jp < NT_D / 2; ++jp) {
+        const uint32_t off = bt_off + uint32_t((kk * 16 * LDK + jp * 16) * 2);
+        uint32_t bo[4], bq[4];
+        ldsm_x4_t(bo, sO_a + off);
+        ldsm_x4_t(bq, sQ_a + off);
+        Mma16<T>::mma(dv[2 * jp], ap, bo[0], bo[1]);
+        Mma16<T>::mma(dv[2 * jp + 1], ap, bo[2], bo[3]);
+        Mma16<T>::mma(dk[2 * jp], ad, bq[0], bq[1]);
+        Mma16<T>::mma(dk[2 * jp + 1], ad, bq[2], bq[3]);
+      }
+    }
+
+    // dS^T to shared memory, [key][query]
+#pragma unroll
+    for (int n = 0; n < NT_Q; ++n) {
+      *reinterpret_cast<uint32_t*>(sS + krow * LDS + n * 8 + 2 * tq) =
+          Mma16<T>::pack(dp[n][0], dp[n][1]);
+      *reinterpret_cast<uint32_t*>(sS + (krow + 8) * LDS + n * 8 + 2 * tq) =
+          Mma16<T>::pack(dp[n][2], dp[n][3]);
+    }
+    __syncthreads();
+
+    // dQ (32 x D) = dS (32 x 128 keys) K (128 x D): warp -> m-tile (warp & 1), NQ n-tiles
+    {
+      const int mt = warp & 1, nb = (warp >> 1) * NQ;
+      //   A = dS from the [key][query] tile, transposed: (keys +0/+8) x (queries +0/+8)
+      const uint32_t as_off = uint32_t((((lm >> 1) * 8 + lr) * LDS + mt * 16 + (lm & 1) * 8) * 2);
+      float dq[NQ][4];
+#pragma unroll
+      for (int j = 0; j < NQ; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) dq[j][e] = 0.f;
+#pragma unroll
+      for (int kk = 0; kk < kBwdBN / 16; ++kk) {
+        uint32_t a[4];
+        ldsm_x4_t(a, sS_a + as_off + uint32_t(kk * 16 * LDS * 2));
+#pragma unroll
+        for (int jp = 0; jp < NQ / 2; ++jp) {
+          uint32_t bk[4];
+          ldsm_x4_t(bk, sK_a + bt_off + uint32_t((kk * 16 * LDK + (nb + 2 * jp) * 8) * 2));
+          Mma16<T>::mma(dq[2 * jp], a, bk[0], bk[1]);
+          Mma16<T>::mma(dq[2 * jp + 1], a, bk[2], bk[3]);
         }
-        sL[r] = l2;
-        sD[r] = dl;
       }
-      __syncthreads();
-
-      // S^T = K Q^T and dP^T = V dO^T for this warp's 16 keys x 32 queries
-      float s[NT_Q][4], dp[NT_Q][4];
 #pragma unroll
-      for (int n = 0; n < NT_Q; ++n)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) s[n][e] = dp[n][e] = 0.f;
-#pragma unroll
-      for (int kk = 0; kk < D / 16; ++kk) {
-        const uint16_t* pk = sK + krow * LDK + kk * 16 + 2 * tq;
-        const uint16_t* pv = sV + krow * LDK + kk * 16 + 2 * tq;
-        const uint32_t ak[4] = {ld_pair(pk), ld_pair(pk + 8 * LDK), ld_pair(pk + 8),
-                                ld_pair(pk + 8 * LDK + 8)};
-        const uint32_t av[4] = {ld_pair(pv), ld_pair(pv + 8 * LDK), ld_pair(pv + 8),
-                                ld_pair(pv + 8 * LDK + 8)};
-#pragma unroll
-        for (int n = 0; n < NT_Q; ++n) {
-          const uint16_t* pq = sQ + (n * 8 + g) * LDK + kk * 16 + 2 * tq;
-          const uint16_t* po = sO + (n * 8 + g) * LDK + kk * 16 + 2 * tq;
-          Mma16<T>::mma(s[n], ak, ld_pair(pq), ld_pair(pq + 8));
-          Mma16<T>::mma(dp[n], av, ld_pair(po), ld_pair(po + 8));
-        }
-      }
-
-      // P^T and dS^T (element e: key row krow + 8*(e>>1), query column n*8 + 2*tq + (e&1))
-#pragma unroll
-      for (int n = 0; n < NT_Q; ++n) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int qi = n * 8 + 2 * tq + (e & 1);
-          const int key = key0 + ((e & 2) ? 8 : 0);
-          float pr = ex2_approx(s[n][e] * p.scale_log2 - sL[qi]);
-          const bool vis = key < geo.kl && (!p.causal || key <= q0 + qi + shift);
-          pr = vis ? pr : 0.f;
-          s[n][e] = pr;
-          dp[n][e] = pr * (dp[n][e] - sD[qi]);
-        }
-      }
-
-      // dV += P^T dO and dK += dS^T Q (k = the 32 queries of the tile)
-#pragma unroll
-      for (int kk = 0; kk < kBwdBM / 16; ++kk) {
-        const uint32_t ap[4] = {Mma16<T>::pack(s[2 * kk][0], s[2 * kk][1]),
-                                Mma16<T>::pack(s[2 * kk][2], s[2 * kk][3]),
-                                Mma16<T>::pack(s[2 * kk + 1][0], s[2 * kk + 1][1]),
-                                Mma16<T>::pack(s[2 * kk + 1][2], s[2 * kk + 1][3])};
-        const uint32_t ad[4] = {Mma16<T>::pack(dp[2 * kk][0], dp[2 * kk][1]),
-                                Mma16<T>::pack(dp[2 * kk][2], dp[2 * kk][3]),
-                                Mma16<T>::pack(dp[2 * kk + 1][0], dp[2 * kk + 1][1]),
-                                Mma16<T>::pack(dp[2 * kk + 1][2], dp[2 * kk + 1][3])};
-        const int r0 = kk * 16 + 2 * tq;
-#pragma unroll
-        for (int n = 0; n < NT_D; ++n) {
-          const int c = n * 8 + g;
-          const uint16_t* po = sO + r0 * LDK + c;
-          const uint16_t* pq = sQ + r0 * LDK + c;
-          Mma16<T>::mma(dv[n], ap, ld_split(po, po + LDK), ld_split(po + 8 * LDK, po + 9 * LDK));
-          Mma16<T>::mma(dk[n], ad, ld_split(pq, pq + LDK), ld_split(pq + 8 * LDK, pq + 9 * LDK));
-        }
-      }
-
-      // dS^T to shared memory, [key][query]
-#pragma unroll
-      for (int n = 0; n < NT_Q; ++n) {
-        *reinterpret_cast<uint32_t*>(sS + krow * LDS + n * 8 + 2 * tq) =
-            Mma16<T>::pack(dp[n][0], dp[n][1]);
-        *reinterpret_cast<uint32_t*>(sS + (krow + 8) * LDS + n * 8 + 2 * tq) =
-            Mma16<T>::pack(dp[n][2], dp[n][3]);
-      }
-      __syncthreads();
-
-      // dQ (32 x D) = dS (32 x 128 keys) K (128 x D): warp -> m-tile (warp & 1), NQ n-tiles
-      {
-        const int mt = warp & 1, nb = (warp >> 1) * NQ;
-        float dq[NQ][4];
-#pragma unroll
-        for (int j = 0; j < NQ; ++j)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) dq[j][e] = 0.f;
-#pragma unroll
-        for (int kk = 0; kk < kBwdBN / 16; ++kk) {
-          const int r0 = kk * 16 + 2 * tq;
-          const uint16_t* ps = sS + r0 * LDS + mt * 16 + g;
-          const uint32_t a[4] = {ld_split(ps, ps + LDS), ld_split(ps + 8, ps + LDS + 8),
-                                 ld_split(ps + 8 * LDS, ps + 9 * LDS),
-                                 ld_split(ps + 8 * LDS + 8, ps + 9 * LDS + 8)};
+      for (int half = 0; half < 2; ++half) {
+        const int qi = mt * 16 + g + 8 * half;
+        if (qi < qvalid) {
+          float* row = p.dq + ((int64_t(geo.qs) + q0 + qi) * p.Hq + hq) * int64_t(D);
 #pragma unroll
           for (int j = 0; j < NQ; ++j) {
-            const uint16_t* pk = sK + r0 * LDK + (nb + j) * 8 + g;
-            Mma16<T>::mma(dq[j], a, ld_split(pk, pk + LDK), ld_split(pk + 8 * LDK, pk + 9 * LDK));
-          }
-        }
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          const int qi = mt * 16 + g + 8 * half;
-          if (qi < qvalid) {
-            float* row = p.dq + ((int64_t(geo.qs) + q0 + qi) * p.Hq + hq) * int64_t(D);
-#pragma unroll
-            for (int j = 0; j < NQ; ++j) {
-              float2* dst = reinterpret_cast<float2*>(row + (nb + j) * 8 + 2 * tq);
-              atomicAdd(dst, make_float2(dq[j][2 * half] * p.scale, dq[j][2 * half + 1] * p.scale));
-            }
+            float2* dst = reinterpret_cast<float2*>(row + (nb + j) * 8 + 2 * tq);
+            atomicAdd(dst, make_float2(dq[j][2 * half] * p.scale, dq[j][2 * half + 1] * p.scale));
           }
         }
       }
     }
+    __syncthreads();  // buffer `buf`, sL/sD[buf] and sS are free for the next tiles
   }
 
   // dK, dV of this thread's two key rows into the fp32 accumulators
