@@ -574,6 +574,7 @@ def bwd_main(args, rank, world, local_rank):
         "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded randn q, k, v, dout)",
         "config": {"workload": f"{args.config} backward: {C['text']}", "cp": cp,
+                   "tokens": N,
                    "l2": "flushed (256 MiB write) before every timed step"},
         "roofline": {"bound": "tensor", "achieved": round(value / world, 2), "peak": peak,
                      "unit": "TFLOP/s", "frac": round(value / world / peak, 4),

@@ -188,9 +188,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1) attn_bwd_kernel(const BwdParam
   float* sL = reinterpret_cast<float*>(sh + SM::HALVES);  // [2][BM] raw LSE
   float* sD = sL + 2 * kBwdBM;                             // [2][BM] Delta
 
-  const int seq = blockIdx.z, hk = blockIdx.y;
+  // grid (kv head, key tile, sequence): the heads' tiles of one key range are adjacent in
+  // launch order, so the heaviest (earliest, under a causal mask) key tiles of every head
+  // start first and the light ones fill the tail
+  const int seq = blockIdx.z, hk = blockIdx.x;
   const BwdGeo geo = bwd_geometry(p, seq);
-  const int k0 = blockIdx.x * kBwdBN;
+  const int k0 = blockIdx.y * kBwdBN;
   if (k0 >= geo.kl || geo.ql <= 0) return;  // uniform over the CTA
   int q_first = 0;
   if (p.causal) {  // key j is visible to query i iff j <= i + (kl - ql)
@@ -488,7 +491,8 @@ int launch_bwd(const BwdParams& p, int nseq, int max_seqlen_k, cudaStream_t st) 
   }
   const int tiles = (max_seqlen_k + kBwdBN - 1) / kBwdBN;
   if (tiles <= 0) return FA4CP_OK;
-  dim3 grid(unsigned(tiles), unsigned(p.Hkv), unsigned(nseq));
+  FA4CP_CHECK_ARG(tiles <= 65535, "max_seqlen_k too large");
+  dim3 grid(unsigned(p.Hkv), unsigned(tiles), unsigned(nseq));
   attn_bwd_kernel<T, D><<<grid, kBwdThreads, BwdSmem<D>::BYTES, st>>>(p);
   return check_launch("attn_bwd");
 }
