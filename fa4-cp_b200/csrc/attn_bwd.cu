@@ -32,10 +32,15 @@
 namespace fa4cp {
 namespace {
 
-constexpr int kBwdBN = 128;              // keys per CTA
+#ifndef FA4CP_BWD_BN
+#define FA4CP_BWD_BN 128
+#endif
+constexpr int kBwdBN = FA4CP_BWD_BN;     // keys per CTA (64 or 128)
 constexpr int kBwdBM = 32;               // query rows per inner tile
 constexpr int kBwdWarps = kBwdBN / 16;   // one warp per 16 keys
 constexpr int kBwdThreads = kBwdWarps * 32;
+constexpr int kBwdMinBlocks = kBwdBN == 64 ? 2 : 1;  // CTAs per SM the registers allow
+static_assert(kBwdBN == 64 || kBwdBN == 128, "64 or 128 keys per CTA");
 
 template <typename T> struct Mma16;
 template <> struct Mma16<__nv_bfloat16> {
@@ -171,12 +176,12 @@ __device__ __forceinline__ void stage_rows_async(uint16_t* dst, const uint16_t* 
 }
 
 template <typename T, int D>
-__global__ void __launch_bounds__(kBwdThreads, 1) attn_bwd_kernel(const BwdParams p) {
+__global__ void __launch_bounds__(kBwdThreads, kBwdMinBlocks) attn_bwd_kernel(const BwdParams p) {
   using SM = BwdSmem<D>;
   constexpr int LDK = SM::LDK, LDS = SM::LDS;
   constexpr int NT_D = D / 8;          // n-tiles over the head dim
   constexpr int NT_Q = kBwdBM / 8;     // n-tiles over a query tile
-  constexpr int NQ = NT_D / 4;         // dQ n-tiles per warp (2 m-tiles x 4 warp columns)
+  constexpr int NQ = NT_D / (kBwdWarps / 2);  // dQ n-tiles per warp (2 m-tiles x warps/2 columns)
   static_assert(NT_Q % 2 == 0 && NQ % 2 == 0, "n-tiles are loaded in pairs");
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint16_t* sh = reinterpret_cast<uint16_t*>(smem_raw);
@@ -344,7 +349,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) attn_bwd_kernel(const BwdParam
     }
     __syncthreads();
 
-    // dQ (32 x D) = dS (32 x 128 keys) K (128 x D): warp -> m-tile (warp & 1), NQ n-tiles
+    // dQ (32 x D) = dS (32 x BN keys) K (BN x D): warp -> m-tile (warp & 1), NQ n-tiles
     {
       const int mt = warp & 1, nb = (warp >> 1) * NQ;
       //   A = dS from the [key][query] tile, transposed: (keys +0/+8) x (queries +0/+8)
