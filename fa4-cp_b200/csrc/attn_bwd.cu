@@ -261,7 +261,7 @@ __global__ void __launch_bounds__(kBwdThreads, kBwdMinBlocks) attn_bwd_kernel(co
   for (int t = 0; t < n_tiles; ++t) {
     const int buf = t & 1;
     if (t + 1 < n_tiles) {
-      stage_tile(t + 1, buf ^ 1);  // its buffer's last readers finished before the last barrier
+      stage_tile(t + 1, buf ^ 1);  // its last readers (tile t-1) passed tile t-1's dS barrier
       cp_async_wait<1>();
     } else {
       cp_async_wait<0>();
@@ -384,7 +384,10 @@ __global__ void __launch_bounds__(kBwdThreads, kBwdMinBlocks) attn_bwd_kernel(co
         }
       }
     }
-    __syncthreads();  // buffer `buf`, sL/sD[buf] and sS are free for the next tiles
+    // no barrier here: the next prefetch into buffer `buf` starts after the barrier above,
+    // which every thread reaches after its last read of `buf` (and sL / sD[buf]); the next
+    // write of sS comes after the next tile's first barrier, which every thread reaches
+    // after this dQ pass
   }
 
   // dK, dV of this thread's two key rows into the fp32 accumulators
