@@ -30,6 +30,7 @@
 #include <string.h>
 
 #include <mutex>
+#include <unordered_set>
 #include <vector>
 
 #include "common.cuh"
@@ -102,6 +103,27 @@ struct RingComm {
   cudaStream_t cstream[4] = {};          // [1] K copy, [2] V copy, [3] release ([0]: caller's)
   std::vector<cudaEvent_t> cev;          // plan events
 };
+
+// live ring handles: every entry point checks its handle here, so a destroyed, foreign or
+// garbage handle is an argument error instead of a dereference
+std::mutex g_rings_mu;
+std::unordered_set<const RingComm*>& live_rings() {
+  static std::unordered_set<const RingComm*> rings;
+  return rings;
+}
+void register_ring(const RingComm* rc) {
+  std::lock_guard<std::mutex> lock(g_rings_mu);
+  live_rings().insert(rc);
+}
+bool unregister_ring(const RingComm* rc) {
+  std::lock_guard<std::mutex> lock(g_rings_mu);
+  return live_rings().erase(rc) > 0;
+}
+RingComm* ring_of(int64_t handle) {
+  std::lock_guard<std::mutex> lock(g_rings_mu);
+  RingComm* rc = reinterpret_cast<RingComm*>(handle);
+  return live_rings().count(rc) ? rc : nullptr;
+}
 
 // restores the calling thread's SM reserve when a ring call returns
 struct SmReserveScope {
@@ -329,13 +351,15 @@ extern "C" int fa4cp_ring_comm_init(const uint8_t* id, int32_t nranks, int32_t r
       return nccl_fail(api, "ncclCommInitRank", r);
     }
   }
+  register_ring(rc);
   *handle_out = reinterpret_cast<int64_t>(rc);
   return FA4CP_OK;
 }
 
 extern "C" int fa4cp_ring_comm_destroy(int64_t handle) {
   FA4CP_CHECK_ARG(handle != 0, "null ring handle");
-  RingComm* rc = reinterpret_cast<RingComm*>(handle);
+  RingComm* rc = ring_of(handle);
+  FA4CP_CHECK_ARG(rc != nullptr && unregister_ring(rc), "unknown ring handle");
   NcclApi* api = nccl_api();
   cudaStreamSynchronize(rc->stream);
   if (api != nullptr && rc->comm != nullptr) api->CommDestroy(rc->comm);
@@ -347,7 +371,8 @@ extern "C" int fa4cp_ring_ipc_alloc(int64_t handle, int64_t kv_capacity, uint8_t
   FA4CP_CHECK_ARG(handle != 0 && ipc_out != nullptr, "null argument");
   FA4CP_CHECK_ARG(kv_capacity > 0 && kv_capacity <= (int64_t(1) << 40), "bad kv_capacity");
   static_assert(sizeof(cudaIpcMemHandle_t) == 64, "CUDA IPC handles are 64 bytes");
-  RingComm* rc = reinterpret_cast<RingComm*>(handle);
+  RingComm* rc = ring_of(handle);
+  FA4CP_CHECK_ARG(rc != nullptr, "unknown ring handle");
   FA4CP_CHECK_CUDA(cudaDeviceSynchronize());
   close_peers(rc);
   if (rc->area) {
@@ -372,7 +397,8 @@ extern "C" int fa4cp_ring_ipc_alloc(int64_t handle, int64_t kv_capacity, uint8_t
 extern "C" int fa4cp_ring_ipc_open(int64_t handle, const uint8_t* left_ipc,
                                    const uint8_t* right_ipc) {
   FA4CP_CHECK_ARG(handle != 0 && left_ipc != nullptr && right_ipc != nullptr, "null argument");
-  RingComm* rc = reinterpret_cast<RingComm*>(handle);
+  RingComm* rc = ring_of(handle);
+  FA4CP_CHECK_ARG(rc != nullptr, "unknown ring handle");
   FA4CP_CHECK_ARG(rc->nranks > 1, "a ring of one rank has no neighbours");
   FA4CP_CHECK_ARG(rc->area != nullptr, "fa4cp_ring_ipc_alloc must come first");
   FA4CP_CHECK_ARG(stream_mem_ops() != nullptr,
@@ -402,7 +428,8 @@ extern "C" int fa4cp_ring_ipc_open(int64_t handle, const uint8_t* left_ipc,
 
 extern "C" int fa4cp_ring_ipc_close(int64_t handle) {
   FA4CP_CHECK_ARG(handle != 0, "null ring handle");
-  RingComm* rc = reinterpret_cast<RingComm*>(handle);
+  RingComm* rc = ring_of(handle);
+  FA4CP_CHECK_ARG(rc != nullptr, "unknown ring handle");
   FA4CP_CHECK_CUDA(cudaDeviceSynchronize());
   close_peers(rc);
   return FA4CP_OK;
@@ -412,7 +439,8 @@ extern "C" int fa4cp_ring_timing(int64_t handle, int32_t max_launches) {
   FA4CP_CHECK_ARG(handle != 0, "null ring handle");
   FA4CP_CHECK_ARG(max_launches >= 0 && max_launches <= (1 << 16), "bad max_launches %d",
                   max_launches);
-  RingComm* rc = reinterpret_cast<RingComm*>(handle);
+  RingComm* rc = ring_of(handle);
+  FA4CP_CHECK_ARG(rc != nullptr, "unknown ring handle");
   destroy_timing(rc);
   rc->tev.assign(2 * size_t(max_launches), nullptr);
   rc->hev.assign(2 * size_t(max_launches), nullptr);
@@ -432,14 +460,18 @@ extern "C" int fa4cp_ring_timing(int64_t handle, int32_t max_launches) {
 extern "C" int fa4cp_ring_set_fused(int64_t handle, int32_t fused) {
   FA4CP_CHECK_ARG(handle != 0, "null ring handle");
   FA4CP_CHECK_ARG(fused >= 0 && fused <= 2, "fused mode %d not in 0..2", fused);
-  reinterpret_cast<RingComm*>(handle)->fused = fused;
+  RingComm* rc = ring_of(handle);
+  FA4CP_CHECK_ARG(rc != nullptr, "unknown ring handle");
+  rc->fused = fused;
   return FA4CP_OK;
 }
 
 extern "C" int fa4cp_ring_set_sm_reserve(int64_t handle, int32_t sm_reserve) {
   FA4CP_CHECK_ARG(handle != 0, "null ring handle");
   FA4CP_CHECK_ARG(sm_reserve >= 0 && sm_reserve <= 64, "sm_reserve %d out of [0, 64]", sm_reserve);
-  reinterpret_cast<RingComm*>(handle)->sm_reserve = sm_reserve;
+  RingComm* rc = ring_of(handle);
+  FA4CP_CHECK_ARG(rc != nullptr, "unknown ring handle");
+  rc->sm_reserve = sm_reserve;
   return FA4CP_OK;
 }
 
@@ -447,7 +479,8 @@ extern "C" int fa4cp_ring_timeline(int64_t handle, float* attn_ms, int32_t max_a
                                    float* hop_ms, int32_t max_hops, int32_t* n_attn,
                                    int32_t* n_hops) {
   FA4CP_CHECK_ARG(handle != 0 && n_attn != nullptr && n_hops != nullptr, "null argument");
-  RingComm* rc = reinterpret_cast<RingComm*>(handle);
+  RingComm* rc = ring_of(handle);
+  FA4CP_CHECK_ARG(rc != nullptr, "unknown ring handle");
   *n_attn = *n_hops = 0;
   if (rc->t_used == 0) return FA4CP_OK;
   cudaEvent_t t0 = rc->tev[0];
@@ -472,7 +505,8 @@ extern "C" int fa4cp_ring_timeline(int64_t handle, float* attn_ms, int32_t max_a
 
 extern "C" int fa4cp_ring_timing_read(int64_t handle, double* total_ms, int32_t* launches) {
   FA4CP_CHECK_ARG(handle != 0 && total_ms != nullptr && launches != nullptr, "null argument");
-  RingComm* rc = reinterpret_cast<RingComm*>(handle);
+  RingComm* rc = ring_of(handle);
+  FA4CP_CHECK_ARG(rc != nullptr, "unknown ring handle");
   double sum = 0.0;
   for (int i = 0; i < rc->t_used; ++i) {
     FA4CP_CHECK_CUDA(cudaEventSynchronize(rc->tev[2 * i + 1]));
@@ -575,7 +609,8 @@ extern "C" int fa4cp_ring_attn_fwd(int64_t handle, const void* q, const void* k,
                                    const float* k_descales, const float* v_descales,
                                    void* workspace, int64_t workspace_bytes, void* stream) {
   FA4CP_CHECK_ARG(handle != 0, "null ring handle");
-  RingComm* rc = reinterpret_cast<RingComm*>(handle);
+  RingComm* rc = ring_of(handle);
+  FA4CP_CHECK_ARG(rc != nullptr, "unknown ring handle");
   const int S = rc->nranks, rank = rc->rank;
   FA4CP_CHECK_ARG(q && k && v && out && lse && cu, "null tensor pointer");
   FA4CP_CHECK_ARG(total >= 0 && nseq >= 1 && max_seqlen >= 0, "bad sizes");

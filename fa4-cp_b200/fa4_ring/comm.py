@@ -400,4 +400,5 @@ def close_native_rings() -> None:
         dist.barrier()
     for ring in rings:
         ring.close()
+    _NATIVE_RINGS.clear()  # a later call on the same group builds a new ring
     _NATIVE_RINGS.clear()

@@ -41,7 +41,10 @@ def merge_state_in_place(v: torch.Tensor, s: torch.Tensor, v_other: torch.Tensor
     _lib.check(_lib.load().fa4cp_merge_state_inplace(
         v.data_ptr(), s.data_ptr(), v_other.data_ptr(), s_other.data_ptr(), T, H, D,
         _lib.dtype_code(v.dtype), _lib.stream_of(v)), "merge_state_in_place")
-    _lib.count_launches(2)
+    # one pass when a head's 16-byte vectors are a power of two <= 32, else values + LSE
+    vph = D // (4 if v.dtype == torch.float32 else 8)
+    if T > 0:
+        _lib.count_launches(1 if 0 < vph <= 32 and (vph & (vph - 1)) == 0 else 2)
 
 
 def merge_states(outs: List[torch.Tensor], lses: List[torch.Tensor], *, out: torch.Tensor = None,

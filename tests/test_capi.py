@@ -89,6 +89,19 @@ def test_backward_argument_validation(lib):
     assert lib.fa4cp_convert_f32(dummy, dummy, 4, 3, None) == -1              # no e4m3 target
 
 
+def test_ring_handles_are_checked(lib):
+    """A handle the library did not hand out (or already destroyed) is an argument error,
+    never dereferenced."""
+    bogus = 0x7F00DEADBEE0
+    for call in (lambda: lib.fa4cp_ring_set_fused(bogus, 1),
+                 lambda: lib.fa4cp_ring_set_sm_reserve(bogus, 4),
+                 lambda: lib.fa4cp_ring_ipc_close(bogus),
+                 lambda: lib.fa4cp_ring_timing(bogus, 4),
+                 lambda: lib.fa4cp_ring_comm_destroy(bogus)):
+        assert call() == -1
+        assert b"unknown ring handle" in lib.fa4cp_last_error()
+
+
 def test_zigzag_argument_validation(lib):
     dummy = ctypes.c_void_p(16)
     assert lib.fa4cp_zigzag_shard(dummy, dummy, None, 1, 10, 0, 2, 4, None) == -1  # 10 % 4 != 0
