@@ -86,3 +86,40 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path):
     monkeypatch.setattr(_lib, "LIB_PATH", str(tmp_path / "absent.so"))
     with pytest.raises(RuntimeError, match="not built"):
         _lib.load()
+
+
+def test_local_cu_args_validates_like_the_forward():
+    import torch
+
+    from fa4_ring.ring_attention import local_cu_args
+    dev = torch.device("cpu")
+    cu, nseq, mx = local_cu_args(8, dev, None, None)
+    assert cu.tolist() == [0, 8] and nseq == 1 and mx == 8
+    with pytest.raises(AssertionError, match="even"):
+        local_cu_args(7, dev, None, None)
+    with pytest.raises(AssertionError, match="max_seqlen"):
+        local_cu_args(8, dev, torch.tensor([0, 4, 8], dtype=torch.int32), None)
+    with pytest.raises(AssertionError, match="even"):
+        local_cu_args(8, dev, torch.tensor([0, 3, 8], dtype=torch.int32), 5)
+    cu, nseq, mx = local_cu_args(8, dev, torch.tensor([0, 2, 8]), 6)
+    assert cu.dtype == torch.int32 and nseq == 2 and mx == 6
+
+
+def test_backward_step_key_bounds():
+    """The per-step key-count bound sizes the backward grid: half the local length for
+    the front-half pattern, the whole length otherwise."""
+    from fa4_ring.attn_backend import PATTERN_BACK_Q, PATTERN_FRONT_KV, PATTERN_VARLEN
+    from fa4_ring.ring_backward import step_max_k
+    assert step_max_k(PATTERN_VARLEN, 512) == 512
+    assert step_max_k(PATTERN_BACK_Q, 512) == 512
+    assert step_max_k(PATTERN_FRONT_KV, 512) == 256
+    assert step_max_k(PATTERN_FRONT_KV, 514) == 257
+
+
+def test_backward_argument_check_refuses_cpu_tensors():
+    import torch
+
+    from fa4_ring.ring_backward import _check_bwd
+    t = torch.zeros(4, 2, 64, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        _check_bwd(t, t, t, t, t, torch.zeros(4, 2))
