@@ -10,12 +10,17 @@ sm_100a behind the C ABI of ``include/fa4cp_b200.h``:
     zigzag_shard / zigzag_unshard - shard a full sequence / stitch shards back
     IncrementalMerger / BatchedMerger / make_merger - LSE mergers
 
+Beyond the reference (which is forward-only): ``ring_flash_attn`` is differentiable, and
+``ring_flash_attn_with_lse`` / ``ring_flash_attn_backward`` run the forward (returning the
+LSE) and the ring backward explicitly.
+
 There is no CPU fallback: every op needs the built CUDA library and CUDA tensors.
 """
 
 from .config import MERGE_MODES, RingConfig
 from .merge import BatchedMerger, IncrementalMerger, make_merger
-from .ring_attention import Descales, ring_flash_attn
+from .ring_attention import Descales, ring_flash_attn, ring_flash_attn_with_lse
+from .ring_backward import ring_flash_attn_backward
 from .zigzag import zigzag_shard, zigzag_unshard
 
 __all__ = [
@@ -27,4 +32,6 @@ __all__ = [
     "IncrementalMerger",
     "BatchedMerger",
     "make_merger",
+    "ring_flash_attn_with_lse",
+    "ring_flash_attn_backward",
 ]
