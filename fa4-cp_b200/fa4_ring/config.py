@@ -18,7 +18,9 @@ class RingConfig:
     causal: bool = True
     softmax_scale: Optional[float] = None  # default: 1/sqrt(head_dim)
     merge_mode: str = "incremental"
-    deterministic: bool = False  # accepted for API parity; every kernel here is deterministic
+    # accepted for API parity (the reference only declares it); the forward kernels are
+    # deterministic, the backward sums dQ with atomics and refuses deterministic=True
+    deterministic: bool = False
 
     def __post_init__(self):
         assert self.merge_mode in MERGE_MODES, (
