@@ -207,6 +207,41 @@ def cpu_sample(rank_steps=None, threads=None):
     return flops, dt, threads
 
 
+def cpu_sample_bwd(threads=None, heads=32, steps=1):
+    """Time the backward oracle (the gradient of the reference's CPU ring algorithm,
+    ``oracle/bwd_oracle.py``, fp32) on a bounded sample of the cfg2 ring backward at cp=8:
+    the first ``steps`` steps of rank 0 for ``heads`` query heads.  Returns (flops, seconds,
+    threads); flops count 5 matmuls of the step's size (2.5x the forward's)."""
+    from threadpoolctl import threadpool_info, threadpool_limits
+
+    from oracle import bwd_oracle as bo
+    from oracle import ring_oracle as orc
+    threads = threads or os.cpu_count() or 1
+    limiter = threadpool_limits(limits=threads)
+    info = threadpool_info()
+    threads = max([i.get("num_threads", 1) for i in info if i.get("user_api") == "blas"] or [1])
+    N, Hq, Hkv, D = CFG2["N"], CFG2["Hq"], CFG2["Hkv"], CFG2["D"]
+    cp, rank = 8, 0
+    T = N // cp
+    hq = min(heads, Hq)
+    hkv = max(1, hq * Hkv // Hq)
+    rng = np.random.default_rng(0)
+    q, dout = (rng.standard_normal((T, hq, D), dtype=np.float32) for _ in range(2))
+    k, v = (rng.standard_normal((T, hkv, D), dtype=np.float32) for _ in range(2))
+    lse = rng.standard_normal((T, hq), dtype=np.float32) + 8.0
+    delta = rng.standard_normal((T, hq), dtype=np.float32)
+    scale = 1.0 / math.sqrt(D)
+    sched = orc.ring_schedule(rank, cp)[:steps]
+    flops = 0.0
+    t0 = time.perf_counter()
+    for (_step, _src, pat) in sched:
+        bo.ring_step_bwd(q, k, v, dout, lse, delta, [0, T], pat, scale, np.float32)
+        flops += 2.5 * 2.0 * T * T * hq * D
+    dt = time.perf_counter() - t0
+    limiter.restore_original_limits()
+    return flops, dt, threads
+
+
 # --------------------------------------------------------------------------- GPU arm
 def gpu_main(args, rank, world, local_rank):
     from fa4_ring import RingConfig, ring_flash_attn, zigzag_shard
@@ -581,7 +616,18 @@ def bwd_main(args, rank, world, local_rank):
                      "traffic": None, "note": f"whole backward step per GPU (all kernels), "
                      f"of {peaks_kind} bf16 burst peak"},
         "gpu_launches": launches, "clocks": clk.summary(), "device_status": int(status),
+        **({"cpu_baseline": _bwd_cpu_baseline()} if world == 1 else {}),
     }
+
+
+def _bwd_cpu_baseline():
+    flops, secs, threads = cpu_sample_bwd()
+    return {"value": round(flops / secs / 1e12, 5), "unit": "TFLOP/s", "cores": threads,
+            "kind": "port",
+            "sample": "backward oracle (gradient of the reference's CPU ring algorithm, fp32) "
+                      "on rank 0 of cfg2 at cp=8: its first ring step (local causal), all 32 "
+                      "query heads, "
+                      f"T=4096 local tokens; {flops:.3e} FLOP in {secs:.1f} s"}
 
 
 def _traffic_from_profile(config, world):

@@ -73,8 +73,8 @@ def attn_bwd_chunk(q, k, v, dout, lse, delta, causal: bool, scale: float, dtype=
         dp = np.matmul(doh, vh.T)                   # [g, Tq, Tk]
         ds = p * (dp - dh)
         dq[:, sl, :] = (np.matmul(ds, kh) * dtype(scale)).transpose(1, 0, 2)
-        dk[:, hk, :] = np.einsum("gij,gid->jd", ds, qh) * dtype(scale)
-        dv[:, hk, :] = np.einsum("gij,gid->jd", p, doh)
+        dk[:, hk, :] = np.matmul(ds.transpose(0, 2, 1), qh).sum(0) * dtype(scale)
+        dv[:, hk, :] = np.matmul(p.transpose(0, 2, 1), doh).sum(0)
     return dq, dk, dv
 
 
