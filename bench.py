@@ -246,6 +246,7 @@ def cpu_sample_bwd(threads=None, heads=32, steps=1):
 def gpu_main(args, rank, world, local_rank):
     from fa4_ring import RingConfig, ring_flash_attn, zigzag_shard
     from fa4_ring import _lib, attn_backend, ring_attention
+    from fa4_ring.ring_attention import ring_flash_attn_with_lse
     from fa4_ring.comm import native_ring
 
     from fa4_ring import Descales
@@ -296,8 +297,8 @@ def gpu_main(args, rank, world, local_rank):
             dist.barrier()
 
     def run():
-        return ring_flash_attn(lq, lk, lv, cfg, descales=desc, cu_seqlens=cu_arg,
-                               max_seqlen=max_local if varlen else None)
+        return ring_flash_attn_with_lse(lq, lk, lv, cfg, descales=desc, cu_seqlens=cu_arg,
+                                        max_seqlen=max_local if varlen else None)
 
     # ---- warm-up
     for _ in range(args.warmup):
@@ -327,7 +328,7 @@ def gpu_main(args, rank, world, local_rank):
             flush.zero_()
             ev[i][0].record()
             h0 = time.perf_counter()
-            run()
+            timed_out = run()
             host_s += time.perf_counter() - h0
             ev[i][1].record()
         torch.cuda.synchronize()
@@ -356,6 +357,9 @@ def gpu_main(args, rank, world, local_rank):
     # (K/V hops not hidden under attention, plus launch gaps), this rank; max over ranks
     exposed_local = max(0.0, (ms_local - attn_ms_local) / ms_local * 100.0) if world > 1 else 0.0
 
+    parity = sampled_parity(timed_out, C, lens, rank, cp, dev, desc, world)
+    del timed_out
+
     if args.quick:  # profiling runs: timed loop only
         vals = torch.tensor([ms_local, attn_ms_local, exposed_local], dtype=torch.float64,
                             device=dev)
@@ -375,7 +379,7 @@ def gpu_main(args, rank, world, local_rank):
                     "attn_ms": round(vals[1].item() / args.steps, 4), "gpu_launches": gpu_launches,
                     "exposed_comm_pct": round(vals[2].item(), 2),
                     "host_issue_ms_per_step": round(host_s * 1e3 / args.steps, 3),
-                    "device_status": status}
+                    "parity": parity, "device_status": status}
         return None
 
     # ---- end to end through the public API: pinned host in, host out
@@ -498,7 +502,7 @@ def gpu_main(args, rank, world, local_rank):
         "exposed_comm_def": "100 * (step time - summed attention-kernel time) / step time, "
                             "max over ranks",
         "executor": (f"native (fa4cp_ring_attn_fwd), {nring.transport} transport, "
-                     f"{'one ring-kernel launch per forward' if n_attn_local == args.steps else 'per-step kernels'}"
+                     f"{'the ring kernel once per forward (e4m3: a main and a split pass)' if n_attn_local == args.steps else 'per-step kernels'}"
                      if nring is not None else "python step loop"),
         "roofline": {"bound": "tensor", "kernel": "fa4cp attn_fwd (tcgen05)",
                      "achieved": None if achieved is None else round(achieved, 1),
@@ -518,6 +522,7 @@ def gpu_main(args, rank, world, local_rank):
                 "serial": {"value": round(step_flops / (e2e_serial_ms * 1e-3) / 1e12, 2),
                            "ms_per_step": round(e2e_serial_ms, 3),
                            "how": "copy in, forward, copy out, one step at a time"}},
+        "parity": parity,
         "gpu_launches": gpu_launches,
         "host_issue_ms_per_step": round(host_s * 1e3 / args.steps, 3),
         "clocks": clocks,
@@ -537,6 +542,90 @@ def gpu_main(args, rank, world, local_rank):
     if traffic is not None:
         line["roofline"]["traffic"] = traffic
     return line
+
+
+def zigzag_positions(n, rank, cp, local_rows):
+    """Global positions, within a sequence of n tokens, of local rows of a zig-zag shard
+    (rank r holds chunks r and 2*cp-1-r of h = n / (2*cp) tokens)."""
+    h = n // (2 * cp)
+    local_rows = np.asarray(local_rows, dtype=np.int64)
+    return np.where(local_rows < h, rank * h + local_rows, (2 * cp - 1 - rank) * h + local_rows - h)
+
+
+def sampled_parity(result, C, lens, rank, cp, dev, desc, world, n_rand=24):
+    """Checks the timed forward's own output: sampled local rows (the first 4 and last 2 rows
+    of each half of each sequence, plus seeded random rows) x all heads, out and LSE, against
+    dense causal attention of those rows computed here in float64 with torch on the device
+    from the same seeded inputs (e4m3 operands: dequantised, per-rank scales as the run used
+    them).  Returns the max errors over ranks and whether they meet the tolerances (out 2e-2
+    bf16 / 6e-2 e4m3 operands, LSE 1e-3)."""
+    from fa4_ring.fp8 import quantize_e4m3
+    from fa4_ring.zigzag import zigzag_shard_varlen
+    out, lse = result
+    Hq, Hkv, D = C["Hq"], C["Hkv"], C["D"]
+    full_cu = [0] + [int(x) for x in np.cumsum(lens)]
+    N = full_cu[-1]
+    g = torch.Generator(device=dev).manual_seed(1234)  # the inputs gpu_main made
+    full = []
+    for h in (Hq, Hkv, Hkv):
+        x = torch.randn(N, h, D, generator=g, device=dev, dtype=torch.bfloat16)
+        full.append(x.mul_(C["amp"]) if C["amp"] != 1.0 else x)
+
+    def operand(x, quant, r_only=None):
+        """x as the kernels saw it, in float64: bf16, or each rank's e4m3 shard x its scale."""
+        if not quant:
+            return x.double()
+        y = torch.empty(x.shape, dtype=torch.float64, device=dev)
+        for r in range(cp) if r_only is None else [r_only]:
+            rows = torch.from_numpy(np.concatenate(
+                [a + zigzag_positions(b - a, r, cp, np.arange((b - a) // cp))
+                 for a, b in zip(full_cu[:-1], full_cu[1:])])).to(dev)
+            x8, sc = quantize_e4m3(zigzag_shard_varlen(x, full_cu, r, cp)[0])
+            y[rows] = x8.double() * sc.double()
+        return y
+
+    kv8 = C["kind"] in ("e4m3", "mixed")
+    qf = operand(full[0], C["kind"] == "e4m3", r_only=rank)
+    kf, vf = operand(full[1], kv8), operand(full[2], kv8)
+    del full
+    rng = np.random.default_rng(rank)
+    scale = 1.0 / math.sqrt(D)
+    err_o = err_l = 0.0
+    n_rows = 0
+    lstart = 0
+    n_rand_seq = max(1, n_rand // len(lens))
+    for j, n in enumerate(lens):
+        h = n // (2 * cp)
+        loc = sorted(set(list(range(min(4, h))) + list(range(max(0, h - 2), h))
+                         + list(range(h, h + min(4, h))) + list(range(2 * h - 2, 2 * h))
+                         + rng.integers(0, 2 * h, size=n_rand_seq).tolist()))
+        pos = torch.from_numpy(zigzag_positions(n, rank, cp, loc)).to(dev)
+        lrows = torch.tensor(loc, device=dev) + lstart
+        a = full_cu[j]
+        R, grp = len(loc), Hq // Hkv
+        q = qf[pos + a].view(R, Hkv, grp, D)                      # head = kv head * grp + i
+        s = torch.einsum("rkgd,nkd->kgrn", q, kf[a:a + n]) * scale
+        s.masked_fill_(torch.arange(n, device=dev) > pos[:, None], -math.inf)
+        want_l = torch.logsumexp(s, dim=-1)                      # [Hkv, grp, R]
+        s.sub_(want_l[..., None]).exp_()
+        want_o = torch.einsum("kgrn,nkd->rkgd", s, vf[a:a + n]).reshape(R, Hq, D)
+        err_o = max(err_o, float((out[lrows].double() - want_o).abs().max()))
+        err_l = max(err_l, float((lse[lrows].double() - want_l.reshape(Hq, R).t()).abs().max()))
+        n_rows += R
+        lstart += 2 * h
+        del s
+    vals = torch.tensor([err_o, err_l], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    err_o, err_l = vals.tolist()
+    tol_o = 2e-2 if C["kind"] == "bf16" else 6e-2
+    return {"max_abs_out": round(err_o, 6), "max_abs_lse": round(err_l, 6),
+            "rows_per_rank": n_rows, "heads": Hq, "tol_out": tol_o, "tol_lse": 1e-3,
+            "pass": bool(err_o <= tol_o and err_l <= 1e-3),
+            "how": "the last timed forward's output on sampled rows (first/last rows of every "
+                   "half of every sequence + seeded random rows) x all heads, against float64 "
+                   "dense causal attention of the same seeded inputs computed with torch on the "
+                   "device; max over ranks"}
 
 
 def bwd_main(args, rank, world, local_rank):

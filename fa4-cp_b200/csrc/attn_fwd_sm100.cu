@@ -17,6 +17,7 @@
 // while the softmax warps turn S_j into P_j.  O is rescaled lazily: only when a
 // row's running max grows by more than 2^8 (log2 domain), so P <= 256.
 #include <atomic>
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -639,6 +640,17 @@ __device__ __forceinline__ bool tile_work(const Params& p, int tile, int BN, Til
   return true;
 }
 
+// e4m3 only: the first K/V tile of query tile t goes to the PV MMA as two e4m3 terms
+// (fp8_p_to_tmem) when some row of the tile sees fewer than 128 keys in all -- causal: its
+// first row; otherwise every row sees k_len keys.  Such a row's keys all lie in that tile,
+// and over few keys the rounding of an e4m3 P does not average out; a row with 128 or more
+// keys needs no split.  Only tiles at the start of a short key range qualify, so the extra
+// MMAs (measured 3% when every causal diagonal tile was split, cfg3 N=131072) vanish.  The
+// softmax warps and the MMA warp evaluate it alike.
+__device__ __forceinline__ bool fp8_split_first(const Params& p, const TileWork& w, int t) {
+  return p.causal ? (w.q0 + t * BM + w.diag + 1 < 128) : (w.g.k_len < 128);
+}
+
 inline int persistent_tiles(int n_qtiles, int Hq, int nseq) {
   const int ch = n_qtiles < kQtileChunk ? n_qtiles : kQtileChunk;
   return (n_qtiles + ch - 1) / ch * ch * Hq * nseq;
@@ -649,6 +661,62 @@ template <class TR>
 __device__ __forceinline__ uint64_t exp2_pair(int pair, uint64_t x) {
   if ((pair & 7) < TR::EXP2_EMU_PER_8) return TR::FP8 ? exp2_poly2_x2(x) : exp2_poly_x2(x);
   return f2pack(ex2_approx(f2lo(x)), ex2_approx(f2hi(x)));
+}
+
+// e4m3 P of one 128-key tile into TMEM, the A operand of the PV MMA.  x = exp2(S * scale - m)
+// per key; hi = e4m3(x) goes to the 32 columns at `taddr`.  With SPLIT, lo = e4m3(x - hi)
+// goes to the next 32 columns and the MMA warp runs that tile's PV MMA twice (hi, then lo),
+// so P carries about 7 significant bits instead of 4 (|hi + lo - x| <= 0.002 max(x, 1) against
+// 0.06 max(x, 1) for hi alone).  The kernels split the tiles of rows that see fewer than 128
+// keys in all: over few keys the rounding of P does not average out (a row seeing 2 keys errs
+// by up to ~0.03 |v| with hi alone).  Returns the fp32 row sum of x (a pair).
+// SPLIT is a template argument: the callers compile their per-tile softmax step twice and
+// run the split tiles outside the loop over the common ones (a branch inside the step
+// measured slower on the unsplit tiles).
+template <class TR, bool SPLIT>
+__device__ __forceinline__ uint64_t fp8_p_to_tmem(uint32_t (&sr)[TR::BN / 32][32], uint64_t scale2,
+                                                  uint64_t negm2, uint32_t taddr) {
+  static_assert(TR::FP8 && TR::BN == 128, "e4m3 P of 128 keys (32 TMEM columns)");
+  uint64_t rs2[2] = {0ull, 0ull};
+  if constexpr (!SPLIT) {
+    uint32_t pw[32];
+#pragma unroll
+    for (int c = 0; c < TR::BN / 32; ++c) {
+#pragma unroll
+      for (int e = 0; e < 32; e += 4) {
+        const uint64_t a = ffma2(f2pack(__uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1])), scale2, negm2);
+        const uint64_t b = ffma2(f2pack(__uint_as_float(sr[c][e + 2]), __uint_as_float(sr[c][e + 3])), scale2, negm2);
+        const uint64_t ea = exp2_pair<TR>((c * 32 + e) / 2, a);
+        const uint64_t eb = exp2_pair<TR>((c * 32 + e) / 2 + 1, b);
+        rs2[0] = fadd2(rs2[0], ea);
+        rs2[1] = fadd2(rs2[1], eb);
+        pw[(c * 32 + e) / 4] = pack_e4m3x4(f2lo(ea), f2hi(ea), f2lo(eb), f2hi(eb));
+      }
+    }
+    tmem_st32(taddr, pw);
+  } else {
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {  // 64 keys at a time: 16 columns of hi, 16 of lo
+      uint32_t hi[16], lo[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int key = hf * 64 + 4 * i, c = key >> 5, e = key & 31;
+        const uint64_t a = ffma2(f2pack(__uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1])), scale2, negm2);
+        const uint64_t b = ffma2(f2pack(__uint_as_float(sr[c][e + 2]), __uint_as_float(sr[c][e + 3])), scale2, negm2);
+        const uint64_t ea = exp2_pair<TR>(key / 2, a);
+        const uint64_t eb = exp2_pair<TR>(key / 2 + 1, b);
+        rs2[0] = fadd2(rs2[0], ea);
+        rs2[1] = fadd2(rs2[1], eb);
+        hi[i] = pack_e4m3x4(f2lo(ea), f2hi(ea), f2lo(eb), f2hi(eb));
+        float h0, h1, h2, h3;
+        unpack_e4m3x4(hi[i], h0, h1, h2, h3);
+        lo[i] = pack_e4m3x4(f2lo(ea) - h0, f2hi(ea) - h1, f2lo(eb) - h2, f2hi(eb) - h3);
+      }
+      tmem_st16(taddr + uint32_t(hf * 16), hi);
+      tmem_st16(taddr + uint32_t(32 + hf * 16), lo);
+    }
+  }
+  return fadd2(rs2[0], rs2[1]);
 }
 
 template <class TR>
@@ -824,6 +892,16 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
             mma_f16_ts(tmem + uint32_t(TR::tm_o(t)), a_tmem, bdesc, idesc_pv, acc);
         }
       };
+      // e4m3 split tile: the second PV term, lo = P - hi, from the next 32 TMEM columns
+      auto issue_pv_lo = [&](int t, int stage) {
+        const uint32_t sV = smem_u32(smem + TR::OFF_V + stage * TR::KV_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < BN / TR::MMA_K; ++kk) {
+          const uint64_t bdesc = make_desc_sw128(sV + kk * TR::MMA_K * 128, TR::KV_CHUNK_BYTES, 1024);
+          mma_f8_ts(tmem + uint32_t(TR::tm_o(t)), tmem + uint32_t(TR::tm_s(t) + 32 + kk * 8), bdesc,
+                    idesc_pv, 1u);
+        }
+      };
       int kv_it = 0, tile_it = 0;
       int p_cnt[2] = {0, 0};          // P hand-offs consumed per query tile (p_full phases)
       int ofree_cnt[2] = {0, 0};      // epilogues that read O_t (o_free phases) ...
@@ -864,6 +942,9 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
               issue_pv_slice(t, s, j == 0, h);
             }
             if (!ok) break;
+            if constexpr (TR::FP8) {
+              if (j == 0 && fp8_split_first(p, w, t)) issue_pv_lo(t, s);
+            }
             ++p_cnt[t];
             tc_commit(o_done(t));
             if (j + 1 < w.n_t[t]) {
@@ -922,9 +1003,12 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
       const uint64_t scale2 = f2pack(scale, scale);
       float m = kNegInf, l = 0.f;
 
-      for (int j = 0; j < n; ++j) {
+      // one K/V tile of the online softmax (SPLIT: its e4m3 P as two terms, fp8_p_to_tmem);
+      // false when a bounded wait gave up
+      auto softmax_tile = [&](int j, auto split_tag) -> bool {
+        constexpr bool SPLIT = decltype(split_tag)::value;
         bool ok = mbar_wait(s_full(t), s_cnt & 1, abort, kErrSFull, status);
-        if (!__all_sync(0xffffffffu, ok)) { aborted = true; break; }
+        if (!__all_sync(0xffffffffu, ok)) return false;
         ++s_cnt;
         tc_fence_after();
         uint32_t sr[BN / 32][32];
@@ -984,22 +1068,7 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
         const uint64_t negm2 = f2pack(neg_m, neg_m);
         uint64_t rs2[2] = {0ull, 0ull};
         if constexpr (TR::FP8) {
-          uint32_t pw[32];
-#pragma unroll
-          for (int c = 0; c < BN / 32; ++c) {
-#pragma unroll
-            for (int e = 0; e < 32; e += 4) {
-              const uint64_t a = ffma2(f2pack(__uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1])), scale2, negm2);
-              const uint64_t b = ffma2(f2pack(__uint_as_float(sr[c][e + 2]), __uint_as_float(sr[c][e + 3])), scale2, negm2);
-              const uint64_t ea = exp2_pair<TR>((c * 32 + e) / 2, a);
-              const uint64_t eb = exp2_pair<TR>((c * 32 + e) / 2 + 1, b);
-              rs2[0] = fadd2(rs2[0], ea);
-              rs2[1] = fadd2(rs2[1], eb);
-              pw[(c * 32 + e) / 4] = pack_e4m3x4(f2lo(ea), f2hi(ea), f2lo(eb), f2hi(eb));
-            }
-          }
-          static_assert(!TR::FP8 || BN == 128, "FP8 P store assumes 128 keys (32 columns)");
-          tmem_st32(t_lane + uint32_t(TR::tm_s(t)), pw);
+          rs2[0] = fp8_p_to_tmem<TR, SPLIT>(sr, scale2, negm2, t_lane + uint32_t(TR::tm_s(t)));
           tmem_wait_st();
           tc_fence_before();
 #pragma unroll
@@ -1043,6 +1112,19 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
         }
         const uint64_t rs = fadd2(rs2[0], rs2[1]);
         l += f2lo(rs) + f2hi(rs);
+        return true;
+      };
+      // e4m3: the first tile may be split (fp8_split_first); it runs before the loop, so
+      // that the loop holds one copy of the step
+      int j0 = 0;
+      if constexpr (TR::FP8) {
+        if (n > 0 && fp8_split_first(p, w, t)) {
+          if (!softmax_tile(0, std::true_type{})) aborted = true;
+          j0 = 1;
+        }
+      }
+      for (int j = j0; !aborted && j < n; ++j) {
+        if (!softmax_tile(j, std::false_type{})) aborted = true;
       }
       if (aborted) break;
 
@@ -1322,13 +1404,18 @@ int launch_ring_fused(const void* q, const void* k, const void* v, const void* s
                       const RingFusedParams& p0, cudaStream_t stream) {
   using KernelFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap,
                            RingFusedParams);
-  KernelFn kernel;
-  if constexpr (TR::PERSISTENT)
-    kernel = ring_fused_persistent_kernel<TR>;
-  else
+  KernelFn kernel, split_kernel = nullptr;
+  if constexpr (TR::PERSISTENT) {
+    kernel = ring_fused_persistent_kernel<TR, false>;
+    if constexpr (TR::FP8) split_kernel = ring_fused_persistent_kernel<TR, true>;
+  } else {
     kernel = ring_fused_kernel<TR>;
-  static std::atomic<uint64_t> optin{0};
+  }
+  static std::atomic<uint64_t> optin{0}, optin_split{0};
   if (int rc0 = smem_optin(kernel, TR::SMEM_BYTES, optin)) return rc0;
+  if (split_kernel != nullptr) {
+    if (int rc0 = smem_optin(split_kernel, TR::SMEM_BYTES, optin_split)) return rc0;
+  }
   RingFusedParams p = p0;
   p.n_pairs = (max_seqlen / 2 + 2 * BM - 1) / (2 * BM);
   if (p.n_pairs <= 0 || total <= 0) return FA4CP_OK;
@@ -1358,7 +1445,19 @@ int launch_ring_fused(const void* q, const void* k, const void* v, const void* s
   // persistent (FP8): one CTA per SM walking the tile list; otherwise one CTA per tile
   const int grid = (TR::PERSISTENT && p.n_tiles > sms) ? sms : p.n_tiles;
   kernel<<<grid, TR::THREADS, TR::SMEM_BYTES, stream>>>(mq, mk0, mv0, mks, mvs, p);
-  return check_launch("ring_fused");
+  if (int rc = check_launch("ring_fused")) return rc;
+  // e4m3: the CTA tiles with a short-keyed row (ring_split_all), P split in two terms.  With one
+  // sequence the host knows whether any exists: the early-half pair 0 sees 1 + rank * h keys,
+  // the late-half pair 0 h + 1 or more (h = half length); packed sequences always run the pass.
+  // It holds few tiles (one pair per head for a long sequence), so a small grid walks the list.
+  const int64_t hh = total / 2;
+  const bool need_split = p.nseq > 1 || int64_t(p.rank) * hh + 1 < 128 || hh + 1 < 128;
+  if (split_kernel != nullptr && need_split) {
+    const int grid_split = p.n_tiles < 64 ? p.n_tiles : 64;
+    split_kernel<<<grid_split, TR::THREADS, TR::SMEM_BYTES, stream>>>(mq, mk0, mv0, mks, mvs, p);
+    return check_launch("ring_fused (split pass)");
+  }
+  return FA4CP_OK;
 }
 
 }  // namespace
@@ -1366,14 +1465,18 @@ int launch_ring_fused(const void* q, const void* k, const void* v, const void* s
 
 using namespace fa4cp;
 
-extern "C" int fa4cp_attn_fwd(const void* q, const void* k, const void* v, void* out, float* lse,
-                              const int32_t* cu_q, const int32_t* cu_k, int32_t nseq,
-                              int32_t max_seqlen_q, int64_t total_q, int64_t total_k,
-                              int32_t num_heads_q, int32_t num_heads_kv, int32_t head_dim,
-                              int32_t in_dtype, int32_t out_dtype, int32_t pattern,
-                              int32_t causal, float softmax_scale, const float* q_descale,
-                              const float* k_descale, const float* v_descale, int32_t accumulate,
-                              void* stream) {
+namespace fa4cp {
+namespace {
+// fa4cp_attn_fwd without its check that descales come with e4m3 operands only: the bf16 x
+// e4m3-K/V path (fa4cp_attn_fwd_kv8) converts K/V to bf16 exactly and hands the descales to
+// the kernel, which folds them into its fp32 score scale and output factor.
+int attn_fwd_impl(const void* q, const void* k, const void* v, void* out, float* lse,
+                  const int32_t* cu_q, const int32_t* cu_k, int32_t nseq, int32_t max_seqlen_q,
+                  int64_t total_q, int64_t total_k, int32_t num_heads_q, int32_t num_heads_kv,
+                  int32_t head_dim, int32_t in_dtype, int32_t out_dtype, int32_t pattern,
+                  int32_t causal, float softmax_scale, const float* q_descale,
+                  const float* k_descale, const float* v_descale, int32_t accumulate,
+                  void* stream) {
   FA4CP_CHECK_ARG(nseq >= 1 && cu_q != nullptr, "cu_seqlens_q must describe >= 1 sequence");
   FA4CP_CHECK_ARG(pattern >= FA4CP_PATTERN_VARLEN && pattern <= FA4CP_PATTERN_BACK_Q,
                   "unknown pattern %d", pattern);
@@ -1387,8 +1490,6 @@ extern "C" int fa4cp_attn_fwd(const void* q, const void* k, const void* v, void*
   const bool fp8 = in_dtype == FA4CP_DTYPE_E4M3;
   FA4CP_CHECK_ARG(fp8 || in_dtype == FA4CP_DTYPE_BF16 || in_dtype == FA4CP_DTYPE_F16,
                   "input dtype must be f16, bf16 or e4m3");
-  FA4CP_CHECK_ARG(fp8 || (q_descale == nullptr && k_descale == nullptr && v_descale == nullptr),
-                  "descales apply to e4m3 inputs only");
   if (total_q == 0) return FA4CP_OK;
   FA4CP_CHECK_ARG(q && out && lse && (total_k == 0 || (k && v)), "null tensor pointer");
   FA4CP_CHECK_ARG(aligned16(q) && aligned16(k) && aligned16(v) && aligned16(out),
@@ -1426,6 +1527,24 @@ extern "C" int fa4cp_attn_fwd(const void* q, const void* k, const void* v, void*
   }
   set_last_error("head_dim %d with dtype %d is not supported", head_dim, in_dtype);
   return FA4CP_ERR_UNSUPPORTED;
+}
+}  // namespace
+}  // namespace fa4cp
+
+extern "C" int fa4cp_attn_fwd(const void* q, const void* k, const void* v, void* out, float* lse,
+                              const int32_t* cu_q, const int32_t* cu_k, int32_t nseq,
+                              int32_t max_seqlen_q, int64_t total_q, int64_t total_k,
+                              int32_t num_heads_q, int32_t num_heads_kv, int32_t head_dim,
+                              int32_t in_dtype, int32_t out_dtype, int32_t pattern,
+                              int32_t causal, float softmax_scale, const float* q_descale,
+                              const float* k_descale, const float* v_descale, int32_t accumulate,
+                              void* stream) {
+  FA4CP_CHECK_ARG(in_dtype == FA4CP_DTYPE_E4M3 ||
+                      (q_descale == nullptr && k_descale == nullptr && v_descale == nullptr),
+                  "descales apply to e4m3 inputs only");
+  return attn_fwd_impl(q, k, v, out, lse, cu_q, cu_k, nseq, max_seqlen_q, total_q, total_k,
+                       num_heads_q, num_heads_kv, head_dim, in_dtype, out_dtype, pattern, causal,
+                       softmax_scale, q_descale, k_descale, v_descale, accumulate, stream);
 }
 
 extern "C" int fa4cp_ring_attn_fused(const void* q, const void* k, const void* v,
@@ -1586,7 +1705,9 @@ extern "C" int fa4cp_device_status(int32_t* status, int32_t clear) {
 extern "C" int64_t fa4cp_attn_kv8_workspace_bytes(int64_t total_k, int32_t num_heads_kv,
                                                   int32_t head_dim) {
   if (total_k < 0 || num_heads_kv <= 0 || head_dim <= 0) return -1;
-  return 2 * total_k * int64_t(num_heads_kv) * head_dim * 2;
+  const int64_t per_row = int64_t(4) * num_heads_kv * head_dim;  // bf16 K and V of one row
+  if (total_k > INT64_MAX / per_row) return -1;                   // the size would overflow
+  return total_k * per_row;
 }
 
 extern "C" int fa4cp_attn_fwd_kv8(const void* q, const void* k8, const void* v8, void* out,
@@ -1601,22 +1722,26 @@ extern "C" int fa4cp_attn_fwd_kv8(const void* q, const void* k8, const void* v8,
                   "kv8 attention takes an f16 or bf16 query");
   FA4CP_CHECK_ARG(num_heads_kv > 0 && head_dim > 0 && total_k >= 0, "bad sizes");
   const int64_t need = fa4cp_attn_kv8_workspace_bytes(total_k, num_heads_kv, head_dim);
+  FA4CP_CHECK_ARG(need >= 0, "K/V of %lld x %d x %d elements: the workspace size overflows",
+                  (long long)total_k, num_heads_kv, head_dim);
   FA4CP_CHECK_ARG(workspace_bytes >= need, "workspace too small: %lld < %lld bytes",
                   (long long)workspace_bytes, (long long)need);
   FA4CP_CHECK_ARG(need == 0 || workspace != nullptr, "workspace is NULL");
-  FA4CP_CHECK_ARG(q_dtype == FA4CP_DTYPE_BF16, "kv8 attention dequantises K/V to bf16; use a bf16 query");
+  FA4CP_CHECK_ARG(q_dtype == FA4CP_DTYPE_BF16, "kv8 attention converts K/V to bf16; use a bf16 query");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   uint8_t* kb = static_cast<uint8_t*>(workspace);
   uint8_t* vb = kb + need / 2;
   if (total_k > 0) {
-    int rc = launch_dequant_e4m3(k8, k_descale, kb, total_k, num_heads_kv, head_dim, st);
+    // e4m3 -> bf16 is exact (3 mantissa bits, exponents inside bf16's range); the descales
+    // stay fp32 and the kernel applies them to the scores and to O
+    int rc = launch_dequant_e4m3(k8, nullptr, kb, total_k, num_heads_kv, head_dim, st);
     if (rc) return rc;
-    rc = launch_dequant_e4m3(v8, v_descale, vb, total_k, num_heads_kv, head_dim, st);
+    rc = launch_dequant_e4m3(v8, nullptr, vb, total_k, num_heads_kv, head_dim, st);
     if (rc) return rc;
   }
-  return fa4cp_attn_fwd(q, kb, vb, out, lse, cu_q, cu_k, nseq, max_seqlen_q, total_q, total_k,
-                        num_heads_q, num_heads_kv, head_dim, q_dtype, q_dtype, pattern, causal,
-                        softmax_scale, nullptr, nullptr, nullptr, accumulate, stream);
+  return attn_fwd_impl(q, kb, vb, out, lse, cu_q, cu_k, nseq, max_seqlen_q, total_q, total_k,
+                       num_heads_q, num_heads_kv, head_dim, q_dtype, q_dtype, pattern, causal,
+                       softmax_scale, nullptr, k_descale, v_descale, accumulate, stream);
 }
 
 extern "C" int fa4cp_selftest_wait_expiry(const void* q, const void* k, const void* v, void* out,

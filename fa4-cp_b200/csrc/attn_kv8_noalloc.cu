@@ -72,6 +72,13 @@ extern "C" int fa4cp_attn_fwd_kv8_noalloc(const void* q, const void* k8, const v
                                           const float* k_descale, const float* v_descale,
                                           int32_t accumulate, void* stream) {
   FA4CP_CHECK_ARG(total_k >= 0 && num_heads_kv > 0 && head_dim > 0, "bad sizes");
+  // bound the row count by division first, so that the byte count below cannot overflow
+  FA4CP_CHECK_ARG(total_k <= kNoAllocScratchBytes / 4 / (int64_t(num_heads_kv) * head_dim),
+                  "no-alloc kv8 attention: K/V of %lld x %d x %d elements exceed its fixed "
+                  "scratch of %lld bytes (K and V of at most %lld elements each); use "
+                  "fa4cp_attn_fwd_kv8 with a caller workspace",
+                  (long long)total_k, num_heads_kv, head_dim, (long long)kNoAllocScratchBytes,
+                  (long long)(kNoAllocScratchBytes / 4));
   const int64_t need = fa4cp_attn_kv8_workspace_bytes(total_k, num_heads_kv, head_dim);
   FA4CP_CHECK_ARG(need >= 0 && need <= kNoAllocScratchBytes,
                   "no-alloc kv8 attention needs %lld bytes of scratch for K/V of %lld x %d x %d "

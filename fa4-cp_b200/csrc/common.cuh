@@ -463,5 +463,14 @@ __device__ __forceinline__ uint32_t pack_e4m3x4(float a, float b, float c, float
   asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(hi) : "f"(d), "f"(c));
   return uint32_t(lo) | (uint32_t(hi) << 16);
 }
+// inverse of pack_e4m3x4 (exact: every e4m3 value is an f16 value)
+__device__ __forceinline__ void unpack_e4m3x4(uint32_t w, float& a, float& b, float& c, float& d) {
+  uint32_t lo, hi;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(lo) : "h"(uint16_t(w & 0xFFFFu)));
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(hi) : "h"(uint16_t(w >> 16)));
+  const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&lo));
+  const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&hi));
+  a = f0.x; b = f0.y; c = f1.x; d = f1.y;
+}
 
 }  // namespace fa4cp

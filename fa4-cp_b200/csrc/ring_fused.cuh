@@ -173,6 +173,19 @@ __device__ __forceinline__ bool ring_tile_geo(const RingFusedParams& p, int tile
   return true;
 }
 
+// e4m3 only: every K/V tile of a CTA goes to the PV MMA as two e4m3 terms (fp8_p_to_tmem)
+// when a row of its query tiles sees fewer than 128 keys over the whole ring -- the first row
+// of the lower query tile: step 0 (causal) plus every remote step.  Over few keys the rounding
+// of an e4m3 P does not average out; only the first early-half pair of rank 0 and the pairs of
+// tiny sequences qualify; they run in the kernel's split pass (SPLIT_PASS), the rest in the
+// main pass.  All three roles of both passes evaluate it alike.
+__device__ __forceinline__ bool ring_split_all(const RingTileGeo& x, int S) {
+  // sum of RingSegs::len(s) over s = 1 .. S-1: h for s <= rank, 2h (late half) or 0 after
+  const int64_t remote = int64_t(x.g.rank) * x.g.hh +
+                         (x.g.half ? int64_t(S - 1 - x.g.rank) * 2 * x.g.hh : 0);
+  return int64_t(x.q0) + x.g.diag + 1 + remote < 128;
+}
+
 // One tile per CTA (f16 / bf16): the straight-line form, measured 3% faster than the tile
 // loop below run for a single tile.
 template <class TR>
@@ -182,7 +195,7 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
                       const __grid_constant__ CUtensorMap tmV0,
                       const __grid_constant__ CUtensorMap tmKs,
                       const __grid_constant__ CUtensorMap tmVs, const RingFusedParams p) {
-  static_assert(!TR::PERSISTENT, "the one-tile ring kernel");
+  static_assert(!TR::PERSISTENT && !TR::FP8, "the one-tile ring kernel (f16 / bf16)");
   constexpr int D = TR::D, BN = TR::BN, ST = TR::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -491,55 +504,33 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
         const uint64_t negm2 = f2pack(neg_m, neg_m);
         const uint64_t scale2 = f2pack(scale, scale);
         uint64_t rs2[2] = {0ull, 0ull};
-        if constexpr (TR::FP8) {
+        // P in 64-key halves: exps of a half are kept (as fp32 bits, in place of S) for the
+        // row sum, which is added up after P has been handed to the MMA warp
+#pragma unroll
+        for (int half = 0; half < BN / 64; ++half) {
           uint32_t pw[32];
 #pragma unroll
-          for (int c = 0; c < BN / 32; ++c) {
-#pragma unroll
-            for (int e = 0; e < 32; e += 4) {
-              const uint64_t a = ffma2(f2pack(__uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1])), scale2, negm2);
-              const uint64_t b = ffma2(f2pack(__uint_as_float(sr[c][e + 2]), __uint_as_float(sr[c][e + 3])), scale2, negm2);
-              const uint64_t ea = exp2_pair<TR>((c * 32 + e) / 2, a);
-              const uint64_t eb = exp2_pair<TR>((c * 32 + e) / 2 + 1, b);
-              rs2[0] = fadd2(rs2[0], ea);
-              rs2[1] = fadd2(rs2[1], eb);
-              pw[(c * 32 + e) / 4] = pack_e4m3x4(f2lo(ea), f2hi(ea), f2lo(eb), f2hi(eb));
-            }
+          for (int e = 0; e < 64; e += 2) {
+            const int c = half * 2 + (e >> 5), ee = e & 31;
+            const uint64_t a = ffma2(f2pack(__uint_as_float(sr[c][ee]), __uint_as_float(sr[c][ee + 1])), scale2, negm2);
+            const uint64_t ex = exp2_pair<TR>(half * 32 + (e >> 1), a);
+            const float x0 = f2lo(ex), x1 = f2hi(ex);
+            sr[c][ee] = __float_as_uint(x0);
+            sr[c][ee + 1] = __float_as_uint(x1);
+            pw[e >> 1] = p.in_fmt ? pack_bf16x2(x0, x1) : pack_f16x2(x0, x1);
           }
-          static_assert(!TR::FP8 || BN == 128, "FP8 P store assumes 128 keys (32 columns)");
-          tmem_st32(t_lane + uint32_t(TR::tm_s(t)), pw);
-          tmem_wait_st();
-          tc_fence_before();
-          mbar_arrive(p_full(t));
-        } else {
-          // P in 64-key halves: exps of a half are kept (as fp32 bits, in place of S) for the
-          // row sum, which is added up after P has been handed to the MMA warp
-#pragma unroll
-          for (int half = 0; half < BN / 64; ++half) {
-            uint32_t pw[32];
-#pragma unroll
-            for (int e = 0; e < 64; e += 2) {
-              const int c = half * 2 + (e >> 5), ee = e & 31;
-              const uint64_t a = ffma2(f2pack(__uint_as_float(sr[c][ee]), __uint_as_float(sr[c][ee + 1])), scale2, negm2);
-              const uint64_t ex = exp2_pair<TR>(half * 32 + (e >> 1), a);
-              const float x0 = f2lo(ex), x1 = f2hi(ex);
-              sr[c][ee] = __float_as_uint(x0);
-              sr[c][ee + 1] = __float_as_uint(x1);
-              pw[e >> 1] = p.in_fmt ? pack_bf16x2(x0, x1) : pack_f16x2(x0, x1);
-            }
-            tmem_st32(t_lane + uint32_t(TR::tm_s(t) + half * 32), pw);
-          }
-          tmem_wait_st();
-          tc_fence_before();
-          mbar_arrive(p_full(t));
-#pragma unroll
-          for (int c = 0; c < BN / 32; ++c)
-#pragma unroll
-            for (int e = 0; e < 32; e += 4) {
-              rs2[0] = fadd2(rs2[0], f2pack(__uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1])));
-              rs2[1] = fadd2(rs2[1], f2pack(__uint_as_float(sr[c][e + 2]), __uint_as_float(sr[c][e + 3])));
-            }
+          tmem_st32(t_lane + uint32_t(TR::tm_s(t) + half * 32), pw);
         }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(p_full(t));
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c)
+#pragma unroll
+          for (int e = 0; e < 32; e += 4) {
+            rs2[0] = fadd2(rs2[0], f2pack(__uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1])));
+            rs2[1] = fadd2(rs2[1], f2pack(__uint_as_float(sr[c][e + 2]), __uint_as_float(sr[c][e + 3])));
+          }
         const uint64_t rs = fadd2(rs2[0], rs2[1]);
         l += f2lo(rs) + f2hi(rs);
       }
@@ -594,7 +585,11 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
 // refilled once the previous tile's S MMAs completed (q_empty), and PV_t of a new tile waits
 // until the previous tile's epilogue has read O_t (o_free).  Measured on one GPU (cfg3
 // shapes): 6% faster than one tile per CTA.
-template <class TR>
+// e4m3 runs in two passes over the same tile list: SPLIT_PASS = false takes every tile whose
+// rows all see 128 or more keys and SPLIT_PASS = true the few others (ring_split_all), with
+// every P split into two e4m3 terms.  The split code lives only in the second instantiation:
+// compiled into the main kernel, even unused, it cost 5.6% (cfg3 ring shapes).
+template <class TR, bool SPLIT_PASS>
 __global__ void __launch_bounds__(TR::THREADS, 1)
     ring_fused_persistent_kernel(const __grid_constant__ CUtensorMap tmQ,
                       const __grid_constant__ CUtensorMap tmK0,
@@ -614,6 +609,12 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
   auto snake_tile = [&](int k) -> int {
     return k * G + ((k & 1) ? G - 1 - int(blockIdx.x) : int(blockIdx.x));
   };
+  // the tiles of this pass (e4m3: split or not, ring_split_all; otherwise all)
+  auto in_pass = [&](const RingTileGeo& x) -> bool {
+    if constexpr (TR::FP8) return ring_split_all(x, p.S) == SPLIT_PASS;
+    return true;
+  };
+  static_assert(TR::FP8 || !SPLIT_PASS, "only e4m3 has a split pass");
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TR::OFF_BAR);
   const uint32_t bar0 = smem_u32(bars);
@@ -681,7 +682,7 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
       bool ok = true;
       for (int it_tile = 0, tile = snake_tile(0); (TR::PERSISTENT || it_tile == 0) && ok && tile < n_tiles; tile = snake_tile(++it_tile)) {
         RingTileGeo x;
-        if (!ring_tile_geo(p, tile, BN, x)) continue;
+        if (!ring_tile_geo(p, tile, BN, x) || !in_pass(x)) continue;
         // the Q buffers are free once every S MMA of the previous tile has completed
         if (tile_it > 0 && !mbar_wait(q_empty, (tile_it - 1) & 1, abort, kErrQ, status)) break;
         mbar_arrive_expect_tx(q_full, 2 * TR::Q_TILE_BYTES);
@@ -772,6 +773,16 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
             mma_f16_ts(tmem + uint32_t(TR::tm_o(t)), a_tmem, bdesc, idesc_pv, acc);
         }
       };
+      // e4m3 split tile: the second PV term, lo = P - hi, from the next 32 TMEM columns
+      auto issue_pv_lo = [&](int t, int stage) {
+        const uint32_t sV = smem_u32(smem + TR::OFF_V + stage * TR::KV_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < BN / TR::MMA_K; ++kk) {
+          const uint64_t bdesc = make_desc_sw128(sV + kk * TR::MMA_K * 128, TR::KV_CHUNK_BYTES, 1024);
+          mma_f8_ts(tmem + uint32_t(TR::tm_o(t)), tmem + uint32_t(TR::tm_s(t) + 32 + kk * 8), bdesc,
+                    idesc_pv, 1u);
+        }
+      };
       int kv_it = 0, tile_it = 0;
       int p_cnt[2] = {0, 0};       // P hand-offs consumed per query tile (p_full phases)
       int ofree_cnt[2] = {0, 0};   // epilogues that read O_t (o_free phases) ...
@@ -779,7 +790,7 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
       bool ok = true;
       for (int it_tile = 0, tile = snake_tile(0); (TR::PERSISTENT || it_tile == 0) && ok && tile < n_tiles; tile = snake_tile(++it_tile)) {
         RingTileGeo x;
-        if (!ring_tile_geo(p, tile, BN, x)) continue;
+        if (!ring_tile_geo(p, tile, BN, x) || !in_pass(x)) continue;
         const int nmax = max(x.n_t[0], x.n_t[1]);
         if (!mbar_wait(q_full, tile_it & 1, abort, kErrQ, status)) { ok = false; break; }
         tc_fence_after();
@@ -809,6 +820,7 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
             if (!mbar_wait(p_full(t), p_cnt[t] & 1, abort, kErrPFull, status)) { ok = false; break; }
             tc_fence_after();
             issue_pv(t, s, j == 0);
+            if constexpr (SPLIT_PASS) issue_pv_lo(t, s);
             ++p_cnt[t];
             tc_commit(o_done(t));
             if (j + 1 < x.n_t[t]) {
@@ -854,7 +866,7 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
 
     for (int it_tile = 0, tile = snake_tile(0); (TR::PERSISTENT || it_tile == 0) && !aborted && tile < n_tiles; tile = snake_tile(++it_tile)) {
       RingTileGeo x;
-      if (!ring_tile_geo(p, tile, BN, x)) continue;
+      if (!ring_tile_geo(p, tile, BN, x) || !in_pass(x)) continue;
       const int nn = x.n_t[t];
       if (nn == 0) continue;  // this query tile lies past the half's end
       const int first = x.q0 + t * BM;
@@ -874,21 +886,13 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
       step_scales(0, scale, vscale);
       int step = 0;
       float m = kNegInf, l = 0.f;  // m: running max of the scaled scores (log2 units)
-      SegCursor cur;
-      cur.start(x.g, BN);
 
-      for (int j = 0; j < nn; ++j) {
-        cur.seek(x.g, j, BN);
-        float fo = 1.0f;  // O factor when the V descale changes with the step
-        if (cur.s != step) {
-          step = cur.s;
-          float vs_new;
-          step_scales(step, scale, vs_new);
-          fo = vscale / vs_new;
-          vscale = vs_new;
-        }
+      // one K/V tile of the online softmax (SPLIT: its e4m3 P as two terms, fp8_p_to_tmem);
+      // fo: O factor when the V descale changes with the step; false when a wait gave up
+      auto softmax_tile = [&](int j, int kbase, int seg, float fo, auto split_tag) -> bool {
+        constexpr bool SPLIT = decltype(split_tag)::value;
         bool ok = mbar_wait(s_full(t), s_cnt & 1, abort, kErrSFull, status);
-        if (!__all_sync(0xffffffffu, ok)) { aborted = true; break; }
+        if (!__all_sync(0xffffffffu, ok)) return false;
         ++s_cnt;
         tc_fence_after();
         uint32_t sr[BN / 32][32];
@@ -898,9 +902,8 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
 #pragma unroll
         for (int c = 0; c < BN / 32; ++c) reg_fence32(sr[c]);
 
-        const int kbase = (j - cur.first) * BN;
-        const int seg_len = x.g.len(cur.s);
-        const bool causal = cur.s == 0;
+        const int seg_len = x.g.len(seg);
+        const bool causal = seg == 0;
         const bool need_mask = (kbase + BN > seg_len) || (causal && kbase + BN - 1 > first + x.g.diag);
         if (need_mask) {
 #pragma unroll
@@ -950,22 +953,7 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
         const uint64_t scale2 = f2pack(scale, scale);
         uint64_t rs2[2] = {0ull, 0ull};
         if constexpr (TR::FP8) {
-          uint32_t pw[32];
-#pragma unroll
-          for (int c = 0; c < BN / 32; ++c) {
-#pragma unroll
-            for (int e = 0; e < 32; e += 4) {
-              const uint64_t a = ffma2(f2pack(__uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1])), scale2, negm2);
-              const uint64_t b = ffma2(f2pack(__uint_as_float(sr[c][e + 2]), __uint_as_float(sr[c][e + 3])), scale2, negm2);
-              const uint64_t ea = exp2_pair<TR>((c * 32 + e) / 2, a);
-              const uint64_t eb = exp2_pair<TR>((c * 32 + e) / 2 + 1, b);
-              rs2[0] = fadd2(rs2[0], ea);
-              rs2[1] = fadd2(rs2[1], eb);
-              pw[(c * 32 + e) / 4] = pack_e4m3x4(f2lo(ea), f2hi(ea), f2lo(eb), f2hi(eb));
-            }
-          }
-          static_assert(!TR::FP8 || BN == 128, "FP8 P store assumes 128 keys (32 columns)");
-          tmem_st32(t_lane + uint32_t(TR::tm_s(t)), pw);
+          rs2[0] = fp8_p_to_tmem<TR, SPLIT>(sr, scale2, negm2, t_lane + uint32_t(TR::tm_s(t)));
           tmem_wait_st();
           tc_fence_before();
           mbar_arrive(p_full(t));
@@ -1000,7 +988,27 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
         }
         const uint64_t rs = fadd2(rs2[0], rs2[1]);
         l += f2lo(rs) + f2hi(rs);
-      }
+        return true;
+      };
+      // the tile walk of this CTA tile (SPLIT_PASS: every tile's P split in two)
+      auto walk = [&](auto split_tag) -> bool {
+        SegCursor cur;
+        cur.start(x.g, BN);
+        for (int j = 0; j < nn; ++j) {
+          cur.seek(x.g, j, BN);
+          float fo = 1.0f;
+          if (cur.s != step) {
+            step = cur.s;
+            float vs_new;
+            step_scales(step, scale, vs_new);
+            fo = vscale / vs_new;
+            vscale = vs_new;
+          }
+          if (!softmax_tile(j, (j - cur.first) * BN, cur.s, fo, split_tag)) return false;
+        }
+        return true;
+      };
+      if (!walk(std::integral_constant<bool, SPLIT_PASS>{})) aborted = true;
       if (aborted) break;
 
       // ---------------------------------------------------------- epilogue of this tile

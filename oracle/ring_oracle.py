@@ -308,6 +308,38 @@ def dense_causal(q, k, v, scale, dtype=np.float32):
     return attn(q, k, v, True, scale, dtype)
 
 
+def dense_causal_rows(q_rows, pos, k, v, scale, chunk=32):
+    """tests/test_algorithm_cpu.py:93-95 (the dense causal reference) evaluated on chosen query
+    rows of ONE sequence: ``q_rows [R, H, D]`` holds the rows at positions ``pos [R]`` of the
+    sequence, ``k``/``v [N, Hkv, D]`` the whole sequence; row ``pos[i]`` sees keys
+    ``[0, pos[i]]`` (GQA: head h reads kv head ``h // (H / Hkv)``).  Returns
+    ``(out [R, H, D], lse [R, H])`` in float64, equal to :func:`dense_causal` on those rows,
+    without forming the ``[N, N]`` score matrix, so that full-size configurations (N up to
+    262144) can be checked row by row.  Scores are float32 products (BLAS), the softmax and
+    the P V sum run in float64."""
+    pos = np.asarray(pos, dtype=np.int64)
+    R, H, D = q_rows.shape
+    Hkv = k.shape[1]
+    g = H // Hkv
+    n_max = int(pos.max()) + 1 if R else 0
+    out = np.zeros((R, H, D), np.float64)
+    lse = np.full((R, H), -np.inf, np.float64)
+    for kh in range(Hkv):
+        kk = np.ascontiguousarray(k[:n_max, kh, :], dtype=np.float32)
+        vv = np.ascontiguousarray(v[:n_max, kh, :], dtype=np.float64)
+        for h in range(kh * g, (kh + 1) * g):
+            for a in range(0, R, chunk):
+                b = min(R, a + chunk)
+                s = (np.asarray(q_rows[a:b, h, :], np.float32) @ kk.T).astype(np.float64) * scale
+                s[np.arange(n_max)[None, :] > pos[a:b, None]] = -np.inf
+                m = s.max(-1, keepdims=True)
+                p = np.exp(s - m)
+                l = p.sum(-1, keepdims=True)
+                out[a:b, h, :] = (p @ vv) / l
+                lse[a:b, h] = (np.log(l) + m)[:, 0]
+    return out, lse
+
+
 def default_scale(head_dim: int) -> float:
     """fa4_ring/fa4_backend.py:88-89: softmax_scale=None -> 1/sqrt(D)."""
     return 1.0 / math.sqrt(head_dim)

@@ -41,3 +41,32 @@ def test_peaks_table():
     peaks, kind = bench.load_peaks()
     assert kind in ("measured", "fallback")
     assert peaks["bf16_tflops"] > 1000 and peaks["hbm_gbs"] > 5000
+
+
+@pytest.mark.parametrize("lens,cp,rank", [([64], 2, 1), ([32, 96, 16], 4, 2)])
+def test_bench_parity_checker_agrees_with_the_oracle(lens, cp, rank):
+    """bench.sampled_parity (the bench line's `parity` key) on CPU tensors: fed the oracle's
+    own rank output for the same seeded inputs, it reports errors at rounding level, and a
+    planted error in one sampled row is reported."""
+    import math
+    import numpy as np
+    import torch
+    C = dict(kind="bf16", Hq=4, Hkv=2, D=32, amp=1.0)
+    dev = torch.device("cpu")
+    full_cu = [0] + [int(x) for x in np.cumsum(lens)]
+    N = full_cu[-1]
+    g = torch.Generator(device=dev).manual_seed(1234)
+    q, k, v = (torch.randn(N, h, C["D"], generator=g, dtype=torch.bfloat16).float().numpy()
+               for h in (C["Hq"], C["Hkv"], C["Hkv"]))
+    scale = 1.0 / math.sqrt(C["D"])
+    lq, lcu = orc.zigzag_shard_varlen(q, full_cu, rank, cp)
+    ks = [orc.zigzag_shard_varlen(k, full_cu, r, cp)[0] for r in range(cp)]
+    vs = [orc.zigzag_shard_varlen(v, full_cu, r, cp)[0] for r in range(cp)]
+    o, l = orc.ring_rank(lq, ks, vs, rank, cp, scale, [int(c) for c in lcu], dtype=np.float64)
+    res = bench.sampled_parity((torch.from_numpy(o), torch.from_numpy(l)), C, lens, rank, cp, dev,
+                               None, 1)
+    assert res["pass"] and res["max_abs_out"] < 1e-5 and res["max_abs_lse"] < 1e-5
+    o[0, 1, 3] += 0.5  # local row 0 is always sampled
+    res = bench.sampled_parity((torch.from_numpy(o), torch.from_numpy(l)), C, lens, rank, cp, dev,
+                               None, 1)
+    assert not res["pass"] and abs(res["max_abs_out"] - 0.5) < 1e-4

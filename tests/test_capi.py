@@ -72,6 +72,26 @@ def test_attn_argument_validation(lib, args, needle):
     assert needle in lib.fa4cp_last_error()
 
 
+def test_kv8_sizes_that_would_overflow_are_rejected(lib):
+    """A K/V row count whose bf16 byte count overflows int64 (2^56 rows x 1 head x 64 dims
+    x 4 bytes = 2^64) gives -1 from the workspace-size helper, and both kv8 entry points
+    reject it before any device work (the no-alloc one by its division bound)."""
+    big = 1 << 56
+    assert lib.fa4cp_attn_kv8_workspace_bytes(big, 1, 64) == -1
+    assert lib.fa4cp_attn_kv8_workspace_bytes((1 << 20), 8, 128) == (1 << 20) * 8 * 128 * 4
+    assert lib.fa4cp_attn_kv8_workspace_bytes(-1, 8, 128) == -1
+    dummy = ctypes.c_void_p(256)
+    common = [dummy] * 7 + [1, 128, 128, big, 8, 1, 64, 1, 0, 1, 0.125, None, None, 0]
+    rc = lib.fa4cp_attn_fwd_kv8(*common, dummy, 1 << 40, None)
+    assert rc == -1 and b"overflow" in lib.fa4cp_last_error()
+    rc = lib.fa4cp_attn_fwd_kv8_noalloc(*common, None)
+    assert rc == -1 and b"scratch" in lib.fa4cp_last_error()
+    # one element past the 32 MiB scratch: K and V of 8,388,608 + 1 elements each
+    common[10] = (1 << 23) // 64 + 1
+    rc = lib.fa4cp_attn_fwd_kv8_noalloc(*common, None)
+    assert rc == -1 and b"scratch" in lib.fa4cp_last_error()
+
+
 def test_backward_argument_validation(lib):
     dummy = ctypes.c_void_p(16)
 

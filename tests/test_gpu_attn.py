@@ -114,7 +114,7 @@ def test_attn_fp8_e4m3_with_descales():
     assert out.dtype == torch.bfloat16
     wo, wl = orc.attn(dequant(q8, qs), dequant(k8, ks), dequant(v8, vs), True, scale)
     np.testing.assert_allclose(to_np(out), wo, atol=OUT_TOL[torch.float8_e4m3fn], rtol=0)
-    np.testing.assert_allclose(to_np(lse), wl, atol=1e-2, rtol=0)
+    np.testing.assert_allclose(to_np(lse), wl, atol=LSE_TOL, rtol=0)
     assert_device_ok()
 
 
@@ -185,7 +185,7 @@ def test_attn_bf16_query_e4m3_kv(D, causal):
     assert out.dtype == torch.bfloat16
     wo, wl = orc.attn(to_np(q), dequant(k8, ks), dequant(v8, vs), causal, scale)
     np.testing.assert_allclose(to_np(out), wo, atol=OUT_TOL[torch.float8_e4m3fn], rtol=0)
-    np.testing.assert_allclose(to_np(lse), wl, atol=1e-2, rtol=0)
+    np.testing.assert_allclose(to_np(lse), wl, atol=LSE_TOL, rtol=0)
     assert_device_ok()
 
 
@@ -234,5 +234,5 @@ def test_attn_fp8_many_tiles_per_cta():
                          q_descale=qs.cuda(), k_descale=ks.cuda(), v_descale=vs.cuda())
     wo, wl = orc.attn(dequant(q8, qs), dequant(k8, ks), dequant(v8, vs), True, scale)
     np.testing.assert_allclose(to_np(out), wo, atol=OUT_TOL[torch.float8_e4m3fn], rtol=0)
-    np.testing.assert_allclose(to_np(lse), wl, atol=1e-2, rtol=0)
+    np.testing.assert_allclose(to_np(lse), wl, atol=LSE_TOL, rtol=0)
     assert_device_ok()

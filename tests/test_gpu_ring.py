@@ -25,7 +25,8 @@ pytestmark = pytest.mark.gpu
 
 def simulate_on_gpu(q, k, v, cp, merge_mode="incremental", full_cu=None, descales=None,
                     fp8_scales=None):
-    """Run every rank's ring steps on one GPU; return the stitched [N, H, D] output."""
+    """Run every rank's ring steps on one GPU; return the stitched output [N, H, D] and
+    final LSE [N, H]."""
     from fa4_ring import RingConfig
     from fa4_ring.ring_attention import ring_forward
     from fa4_ring.zigzag import zigzag_shard_varlen, zigzag_unshard_varlen
@@ -39,7 +40,7 @@ def simulate_on_gpu(q, k, v, cp, merge_mode="incremental", full_cu=None, descale
         shards_v.append(zigzag_shard_varlen(v, cu_full, r, cp)[0])
     lens = [b - a for a, b in zip(cu_full[:-1], cu_full[1:])]
     max_local = max(lens) // cp
-    outs = []
+    outs, lses = [], []
     for r in range(cp):
         cfg = RingConfig(cp_size=cp, cp_rank=r, merge_mode=merge_mode)
 
@@ -47,9 +48,12 @@ def simulate_on_gpu(q, k, v, cp, merge_mode="incremental", full_cu=None, descale
             src = (r - step) % cp
             return shards_k[src], shards_v[src]
 
-        outs.append(ring_forward(shards_q[r], kv_at, lambda s: None, cfg, cu=lcu,
-                                 nseq=len(cu_full) - 1, max_seqlen=max_local, descales=descales))
-    return zigzag_unshard_varlen(outs, cu_full, cp)
+        o, l = ring_forward(shards_q[r], kv_at, lambda s: None, cfg, cu=lcu,
+                            nseq=len(cu_full) - 1, max_seqlen=max_local, descales=descales,
+                            return_lse=True)
+        outs.append(o)
+        lses.append(l)
+    return zigzag_unshard_varlen(outs, cu_full, cp), zigzag_unshard_varlen(lses, cu_full, cp)
 
 
 @pytest.mark.parametrize("cp", [1, 2, 3, 4, 8])
@@ -58,10 +62,11 @@ def test_ring_single_sequence(cp, merge_mode):
     g = torch.Generator().manual_seed(cp)
     N, H, Hkv, D = 2 * cp * 160, 4, 2, 128
     q, k, v = (torch.randn(N, h, D, generator=g).bfloat16() for h in (H, Hkv, Hkv))
-    got = simulate_on_gpu(q.cuda(), k.cuda(), v.cuda(), cp, merge_mode)
+    got, got_l = simulate_on_gpu(q.cuda(), k.cuda(), v.cuda(), cp, merge_mode)
     scale = 1.0 / math.sqrt(D)
-    dense, _ = orc.dense_causal(to_np(q), to_np(k), to_np(v), scale)
+    dense, dense_l = orc.dense_causal(to_np(q), to_np(k), to_np(v), scale)
     np.testing.assert_allclose(to_np(got), dense, atol=2e-2, rtol=0)
+    np.testing.assert_allclose(to_np(got_l), dense_l, atol=1e-3, rtol=0)
     assert_device_ok()
 
 
@@ -74,13 +79,15 @@ def test_ring_varlen(cp, merge_mode):
     H, Hkv, D = 4, 1, 128
     N = cu[-1]
     q, k, v = (torch.randn(N, h, D, generator=g).bfloat16() for h in (H, Hkv, Hkv))
-    got = to_np(simulate_on_gpu(q.cuda(), k.cuda(), v.cuda(), cp, merge_mode, full_cu=cu))
+    got, got_l = (to_np(t) for t in simulate_on_gpu(q.cuda(), k.cuda(), v.cuda(), cp, merge_mode,
+                                                       full_cu=cu))
     scale = 1.0 / math.sqrt(D)
     qn, kn, vn = to_np(q), to_np(k), to_np(v)
     for j in range(len(lens)):
         a, b = cu[j], cu[j + 1]
-        dense, _ = orc.dense_causal(qn[a:b], kn[a:b], vn[a:b], scale)
+        dense, dense_l = orc.dense_causal(qn[a:b], kn[a:b], vn[a:b], scale)
         np.testing.assert_allclose(got[a:b], dense, atol=2e-2, rtol=0)
+        np.testing.assert_allclose(got_l[a:b], dense_l, atol=1e-3, rtol=0)
     assert_device_ok()
 
 
@@ -91,12 +98,14 @@ def test_ring_cfg1_against_reference_golden():
     n, H, Hkv, D, cp = c["dims"].tolist()
     torch.manual_seed(0)
     q, k, v = torch.randn(n, H, D), torch.randn(n, Hkv, D), torch.randn(n, Hkv, D)
-    got = to_np(simulate_on_gpu(q.bfloat16().cuda(), k.bfloat16().cuda(), v.bfloat16().cuda(), cp))
+    got, got_l = (to_np(t) for t in simulate_on_gpu(q.bfloat16().cuda(), k.bfloat16().cuda(),
+                                                       v.bfloat16().cuda(), cp))
     rows = c["rows"]
     np.testing.assert_allclose(got[rows], c["ring_out_rows"], atol=3e-2, rtol=0)
     qn, kn, vn = (to_np(t.bfloat16()) for t in (q, k, v))
-    want, _ = orc.simulate_ring(qn, kn, vn, cp, 1.0 / math.sqrt(D))
+    want, want_l = orc.simulate_ring(qn, kn, vn, cp, 1.0 / math.sqrt(D))
     np.testing.assert_allclose(got, want, atol=2e-2, rtol=0)
+    np.testing.assert_allclose(got_l, want_l, atol=1e-3, rtol=0)
     assert_device_ok()
 
 
@@ -120,7 +129,7 @@ def test_ring_fp8_per_source_descales():
     from fa4_ring import RingConfig
     from fa4_ring.ring_attention import ring_forward
     cu = torch.tensor([0, N // cp], dtype=torch.int32, device="cuda")
-    outs = []
+    outs, lses = [], []
     for r in range(cp):
         cfg = RingConfig(cp_size=cp, cp_rank=r)
         desc = Descales(q=qs[r].cuda(), k=[s.cuda() for s in ks], v=[s.cuda() for s in vs])
@@ -129,14 +138,18 @@ def test_ring_fp8_per_source_descales():
             src = (r - step) % cp
             return k8[src].cuda(), v8[src].cuda()
 
-        outs.append(to_np(ring_forward(q8[r].cuda(), kv_at, lambda s: None, cfg, cu=cu, nseq=1,
-                                       max_seqlen=N // cp, descales=desc)))
+        o, l = ring_forward(q8[r].cuda(), kv_at, lambda s: None, cfg, cu=cu, nseq=1,
+                            max_seqlen=N // cp, descales=desc, return_lse=True)
+        outs.append(to_np(o))
+        lses.append(to_np(l))
     got = orc.zigzag_unshard(outs, cp)
+    got_l = orc.zigzag_unshard(lses, cp)
     qf = orc.zigzag_unshard(deq["q"], cp)
     kf = orc.zigzag_unshard(deq["k"], cp)
     vf = orc.zigzag_unshard(deq["v"], cp)
-    want, _ = orc.dense_causal(qf, kf, vf, 1.0 / math.sqrt(D))
+    want, want_l = orc.dense_causal(qf, kf, vf, 1.0 / math.sqrt(D))
     np.testing.assert_allclose(got, want, atol=6e-2, rtol=0)
+    np.testing.assert_allclose(got_l, want_l, atol=1e-3, rtol=0)
     assert_device_ok()
 
 
@@ -185,15 +198,19 @@ def test_ring_bf16_query_e4m3_kv_head_dim_256():
         k8.append(a8); ks.append(a_s); v8.append(b8); vs.append(b_s)
         kd.append(dequant(a8.cpu(), a_s.cpu())); vd.append(dequant(b8.cpu(), b_s.cpu()))
     cu = torch.tensor([0, T], dtype=torch.int32, device="cuda")
-    outs = []
+    outs, lses = [], []
     for r in range(cp):
         rows = torch.from_numpy(orc.zigzag_rows(N, r, cp))
         desc = Descales(k=ks, v=vs)
-        outs.append(to_np(ring_forward(q[rows].cuda(), lambda s, r=r: (k8[(r - s) % cp], v8[(r - s) % cp]),
-                                       lambda s: None, RingConfig(cp_size=cp, cp_rank=r), cu=cu,
-                                       nseq=1, max_seqlen=T, descales=desc)))
+        o, l = ring_forward(q[rows].cuda(), lambda s, r=r: (k8[(r - s) % cp], v8[(r - s) % cp]),
+                            lambda s: None, RingConfig(cp_size=cp, cp_rank=r), cu=cu,
+                            nseq=1, max_seqlen=T, descales=desc, return_lse=True)
+        outs.append(to_np(o))
+        lses.append(to_np(l))
     got = orc.zigzag_unshard(outs, cp)
-    want, _ = orc.dense_causal(to_np(q), orc.zigzag_unshard(kd, cp), orc.zigzag_unshard(vd, cp),
-                               1.0 / math.sqrt(D))
+    got_l = orc.zigzag_unshard(lses, cp)
+    want, want_l = orc.dense_causal(to_np(q), orc.zigzag_unshard(kd, cp), orc.zigzag_unshard(vd, cp),
+                                    1.0 / math.sqrt(D))
     np.testing.assert_allclose(got, want, atol=6e-2, rtol=0)
+    np.testing.assert_allclose(got_l, want_l, atol=1e-3, rtol=0)
     assert_device_ok()

@@ -9,11 +9,10 @@ the oracle's ``ring_rank`` on the same (rounded) inputs (out <= 2e-2, LSE <= 1e-
 stitched output against dense causal attention.  One case passes a counter that already
 holds its target (the in-kernel wait returns at once).  e4m3: every rank quantises its own
 shards (scale = amax/448), the K/V descales are indexed by source rank, and the oracle runs
-on the dequantised shards: out <= 6e-2 on rows that see at least 16 keys, <= 1e-1 on every
-row, LSE <= 1e-2.  The looser bound for rows with a handful of keys is the rounding of P to
-e4m3 itself (3 mantissa bits; the kernel feeds P to the e4m3 MMA as FA4's FP8 path does):
-on the (cp=4, N=1600, Hq=8, Hkv=2) case, rounding P alone, computed exactly on the CPU,
-already errs by 0.0647 at a row that sees 2 keys.  The multi-GPU run of the same
+on the dequantised shards: out <= 6e-2 on every row, LSE <= 1e-3 (the tolerances of the
+FP8 path).  Rows that see only a handful of keys are the hard case for an e4m3 P (3 mantissa
+bits): the kernel feeds the causal diagonal tile's P to the PV MMA as two e4m3 terms
+(P = hi + lo), so those rows are as accurate as the rest.  The multi-GPU run of the same
 kernel behind the copy-engine transport is ``tests/dist_ring_check.py``.
 """
 
@@ -69,7 +68,7 @@ def run_fused(cp, lens, H, Hkv, D, dtype, seed, counter=False, fp8=False):
         k_np = [to_np(t) for t in ks]
         v_np = [to_np(t) for t in vs]
     elem = 1 if fp8 else 2
-    tol_o, tol_l = (6e-2, 1e-2) if fp8 else (OUT_TOL, LSE_TOL)
+    tol_o, tol_l = (6e-2, LSE_TOL) if fp8 else (OUT_TOL, LSE_TOL)
     lcu_list = [int(x) for x in lcu.tolist()]
     outs = []
     for r in range(cp):
@@ -96,14 +95,7 @@ def run_fused(cp, lens, H, Hkv, D, dtype, seed, counter=False, fp8=False):
         torch.cuda.synchronize()
         want_o, want_l = orc.ring_rank(q_np[r], k_np, v_np, r, cp, scale, lcu_list)
         got_o = to_np(out)
-        if fp8:
-            # keys a local row sees = its position in its full sequence + 1
-            seen = np.concatenate([orc.zigzag_rows(n, r, cp) + 1 for n in lens])
-            many = seen >= 16
-            np.testing.assert_allclose(got_o[many], want_o[many], atol=tol_o, rtol=0)
-            np.testing.assert_allclose(got_o, want_o, atol=1e-1, rtol=0)
-        else:
-            np.testing.assert_allclose(got_o, want_o, atol=tol_o, rtol=0)
+        np.testing.assert_allclose(got_o, want_o, atol=tol_o, rtol=0)
         np.testing.assert_allclose(to_np(lse), want_l, atol=tol_l, rtol=0)
         outs.append(to_np(out))
     if fp8:

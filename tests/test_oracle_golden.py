@@ -165,6 +165,26 @@ def test_oracle_cfg1_matches_reference():
     assert abs(float(rl.astype(np.float64).sum()) - float(c["dense_lse_sum"])) < 1e-1
 
 
+def test_row_oracle_matches_reference_rows():
+    """dense_causal_rows (the full-size parity checker) on the sampled rows of BASELINE
+    the reference's ring output and dense LSE at those rows, and the whole-matrix
+    oracle on a GQA case with ragged row positions."""
+    c = _load("cfg1.npz")
+    n, H, Hkv, D, cp = c["dims"].tolist()
+    q, k, v = (t.numpy() for t in _inputs(n, H, Hkv, D, seed=0))
+    rows = c["rows"]
+    ro, rl = orc.dense_causal_rows(q[rows], rows, k, v, 1.0 / math.sqrt(D))
+    np.testing.assert_allclose(ro, c["ring_out_rows"], **TOL)
+    np.testing.assert_allclose(rl, c["dense_lse_rows"], **TOL)
+    rng = np.random.default_rng(3)
+    q2, k2, v2 = (rng.standard_normal((300, h, 64)).astype(np.float32) for h in (6, 2, 2))
+    pos = np.array([0, 1, 2, 17, 128, 129, 250, 299])
+    want_o, want_l = orc.dense_causal(q2, k2, v2, 0.125)
+    got_o, got_l = orc.dense_causal_rows(q2[pos], pos, k2, v2, 0.125, chunk=3)
+    np.testing.assert_allclose(got_o, want_o[pos], atol=1e-5, rtol=1e-5)
+    np.testing.assert_allclose(got_l, want_l[pos], atol=1e-5, rtol=1e-5)
+
+
 def test_planted_mistake_is_caught():
     """A wrong ring schedule (the reference GPU path's off-by-one rotation) fails the pin."""
     a = _load("algo.npz")
