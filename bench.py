@@ -359,10 +359,18 @@ def gpu_main(args, rank, world, local_rank):
 
     parity = sampled_parity(timed_out, C, lens, rank, cp, dev, desc, world)
     del timed_out
+    exposed_8d_local = 0.0
+    local_ms = None
+    if world > 1:
+        fused = nring is not None and n_attn_local == args.steps
+        local_ms = local_schedule_ms(lq, lk, lv, cfg, desc, lcu, len(lens), max_local, fused,
+                                     flush, max(3, min(args.steps, 10)), world)
+        step_ms = ms_local / args.steps
+        exposed_8d_local = max(0.0, (step_ms - local_ms) / step_ms * 100.0)
 
     if args.quick:  # profiling runs: timed loop only
-        vals = torch.tensor([ms_local, attn_ms_local, exposed_local], dtype=torch.float64,
-                            device=dev)
+        vals = torch.tensor([ms_local, attn_ms_local, exposed_local, exposed_8d_local],
+                            dtype=torch.float64, device=dev)
         if world > 1:
             dist.all_reduce(vals, op=dist.ReduceOp.MAX)
         if timeline is not None:
@@ -377,7 +385,8 @@ def gpu_main(args, rank, world, local_rank):
                     "ms_per_step": round(ms_step, 4),
                     "value": round(step_flops / (ms_step * 1e-3) / 1e12, 2),
                     "attn_ms": round(vals[1].item() / args.steps, 4), "gpu_launches": gpu_launches,
-                    "exposed_comm_pct": round(vals[2].item(), 2),
+                    "exposed_comm_pct": round(vals[3].item(), 2),
+                    "exposed_no_attn_pct": round(vals[2].item(), 2),
                     "host_issue_ms_per_step": round(host_s * 1e3 / args.steps, 3),
                     "parity": parity, "device_status": status}
         return None
@@ -456,10 +465,12 @@ def gpu_main(args, rank, world, local_rank):
 
     # ---- reduce over ranks (max)
     vals = torch.tensor([ms_local, attn_ms_local, e2e_ms_local, exposed_local, float(status),
-                         e2e_serial_ms_local], dtype=torch.float64, device=dev)
+                         e2e_serial_ms_local, exposed_8d_local, local_ms or 0.0],
+                        dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
-    ms_total, attn_ms, e2e_ms, exposed, status_max, e2e_serial_ms = vals.tolist()
+    (ms_total, attn_ms, e2e_ms, exposed, status_max, e2e_serial_ms, exposed_8d,
+     local_ms_max) = vals.tolist()
 
     if rank != 0:
         return None
@@ -498,9 +509,15 @@ def gpu_main(args, rank, world, local_rank):
                    "l2": "flushed before every timed step (256 MiB write, untimed)"},
         "per_gpu_tflops": round(value / world, 2),
         "pct_tensor_peak": round(value / world / peak * 100.0, 2),
-        "exposed_comm_pct": round(exposed, 2) if world > 1 else None,
-        "exposed_comm_def": "100 * (step time - summed attention-kernel time) / step time, "
-                            "max over ranks",
+        "exposed_comm_pct": round(exposed_8d, 2) if world > 1 else None,
+        "exposed_comm_def": "100 * (ring step time - the same schedule with the transfers "
+                            "skipped) / ring step time, max over ranks; the no-transfer time "
+                            "runs this rank's forward with every step's K/V already local "
+                            "(all-gathered beforehand, untimed)",
+        "no_transfer_ms_per_step": round(local_ms_max, 4) if world > 1 else None,
+        "exposed_no_attn_pct": round(exposed, 2) if world > 1 else None,
+        "exposed_no_attn_def": "100 * (step time - summed attention-launch time) / step time, "
+                               "max over ranks (blind to hop waits inside the ring kernel)",
         "executor": (f"native (fa4cp_ring_attn_fwd), {nring.transport} transport, "
                      f"{'the ring kernel once per forward (e4m3: a main and a split pass)' if n_attn_local == args.steps else 'per-step kernels'}"
                      if nring is not None else "python step loop"),
@@ -542,6 +559,66 @@ def gpu_main(args, rank, world, local_rank):
     if traffic is not None:
         line["roofline"]["traffic"] = traffic
     return line
+
+
+def local_schedule_ms(lq, lk, lv, cfg, desc, lcu, nseq, max_local, fused, flush, steps, world):
+    """Exposed communication as SURVEY's measurement section defines it: the same schedule
+    with the transfers skipped.  Every rank's K/V shard is all-gathered first (untimed), so
+    each step's K/V is already in this GPU's memory; then this rank's forward is timed exactly
+    as the ring ran it -- the ring kernel through its public C entry point with every receive
+    slot filled and no hop counter (``fa4cp_ring_attn_fused``, arrived = NULL), or the
+    per-step kernels through ``ring_forward`` -- L2 flushed before each step, CUDA events.
+    Returns this rank's ms per forward."""
+    from fa4_ring import _lib
+    from fa4_ring.attn_backend import norm_descale
+    from fa4_ring.ring_attention import ring_forward
+    S, rank = cfg.cp_size, cfg.cp_rank
+    T, Hq, D = lq.shape
+    Hkv = lk.shape[1]
+    gath = []
+    for t in (lk, lv):
+        parts = [torch.empty_like(t.view(torch.uint8)) for _ in range(world)]
+        dist.all_gather(parts, t.contiguous().view(torch.uint8))
+        gath.append([x.view(t.dtype) for x in parts])
+    ks, vs = gath
+    scale = 1.0 / math.sqrt(D)
+    lib = _lib.load()
+    st = _lib.stream_of(lq)
+    if fused:
+        # slot i holds the K/V of rank (rank - i - 1) mod S, as the copy-engine transport leaves it
+        slots_k = torch.stack([ks[(rank - i - 1) % S].view(torch.uint8) for i in range(S - 1)])
+        slots_v = torch.stack([vs[(rank - i - 1) % S].view(torch.uint8) for i in range(S - 1)])
+        out = torch.empty(T, Hq, D, dtype=torch.bfloat16 if lq.dtype == torch.float8_e4m3fn
+                          else lq.dtype, device=lq.device)
+        lse = torch.empty(T, Hq, dtype=torch.float32, device=lq.device)
+        kv8 = lk.dtype == torch.float8_e4m3fn
+        qd = norm_descale(desc.q, Hkv, lq.device) if (desc and desc.q is not None) else None
+        kds = torch.stack([norm_descale(d, Hkv, lq.device) for d in desc.k]) if (kv8 and desc) else None
+        vds = torch.stack([norm_descale(d, Hkv, lq.device) for d in desc.v]) if (kv8 and desc) else None
+
+        def one():
+            _lib.check(lib.fa4cp_ring_attn_fused(
+                lq.data_ptr(), lk.data_ptr(), lv.data_ptr(), slots_k.data_ptr(), slots_v.data_ptr(),
+                slots_k[0].numel(), out.data_ptr(), lse.data_ptr(), lcu.data_ptr(), nseq, max_local,
+                T, Hq, Hkv, D, _lib.dtype_code(lq.dtype), scale, _lib.ptr(qd), _lib.ptr(kds),
+                _lib.ptr(vds), S, rank, None, 0, st), "ring_attn_fused")
+    else:
+        def one():
+            ring_forward(lq, lambda s: (ks[(rank - s) % S], vs[(rank - s) % S]), lambda s: None,
+                         cfg, cu=lcu, nseq=nseq, max_seqlen=max_local, descales=desc)
+    for _ in range(2):
+        one()
+    torch.cuda.synchronize()
+    tot = 0.0
+    for _ in range(steps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        one()
+        e1.record()
+        torch.cuda.synchronize()
+        tot += e0.elapsed_time(e1)
+    return tot / steps
 
 
 def zigzag_positions(n, rank, cp, local_rows):

@@ -21,6 +21,7 @@ attention.  With a CPU process group (gloo) the same schedule runs with blocking
 hops; that path exists to test the rotation logic without a GPU.
 """
 
+import time
 from typing import Dict, Optional, Tuple
 
 import torch
@@ -218,6 +219,71 @@ class GradRing:
         return self.recv
 
 
+# Seconds a native ring call waits on the host for its neighbours to enter the same call
+# before it raises (RingLiveness); None turns the check off.
+RING_LIVENESS_TIMEOUT_S: Optional[float] = 60.0
+
+
+class RingLiveness:
+    """Host-side check, before a ring call queues device waits on its neighbours, that both
+    neighbours are still there.
+
+    The native ring's device-side waits on a neighbour (the copy-engine transport's hop
+    counters, ``cuStreamWaitValue32``; NCCL send/recv on the executor's communicator) have no
+    time limit: a neighbour that left between calls would block this rank's streams until
+    the process ends.  So every call first publishes its call number in the process group's
+    key-value store (``store.add``) and waits, polling with a deadline, until both neighbours
+    have published the same call number; if one has not after ``timeout_s`` seconds, the call
+    raises ``RuntimeError`` naming it, before anything is queued on the GPU.  Costs two or
+    three store round trips per call.  A neighbour that dies while a call runs is not caught
+    here (the ring kernel's own wait for a hop counter is bounded; the stream waits are not).
+    """
+
+    def __init__(self, store, prefix: str, rank: int, size: int, timeout_s: float):
+        self.store, self.prefix, self.rank, self.size = store, prefix, rank, size
+        self.timeout_s = float(timeout_s)
+        self.calls = 0
+        self.peers = sorted({(rank - 1) % size, (rank + 1) % size} - {rank})
+
+    def _key(self, r: int) -> str:
+        return f"{self.prefix}/calls/{r}"
+
+    def enter(self) -> None:
+        self.calls = int(self.store.add(self._key(self.rank), 1))
+        deadline = time.monotonic() + self.timeout_s
+        pause = 0.0
+        for peer in self.peers:
+            while int(self.store.add(self._key(peer), 0)) < self.calls:
+                if time.monotonic() > deadline:
+                    raise RuntimeError(
+                        f"ring rank {self.rank}: neighbour rank {peer} has not entered ring call "
+                        f"{self.calls} within {self.timeout_s:.0f} s (it left or stalled); the "
+                        "call was not queued")
+                time.sleep(pause)
+                pause = min(0.01, pause + 0.0005)
+
+
+_RING_SERIAL: Dict[Tuple, int] = {}
+
+
+def _ring_liveness(group, cp_rank: int, cp_size: int) -> Optional[RingLiveness]:
+    """A RingLiveness on the default store for a ring being created (collectively) on
+    ``group``; None when the check is off or there is no store."""
+    if RING_LIVENESS_TIMEOUT_S is None or cp_size < 2:
+        return None
+    try:
+        from torch.distributed.distributed_c10d import _get_default_store
+        store = _get_default_store()
+    except Exception:  # no default store (a process group without one): no check
+        return None
+    ranks = tuple(dist.get_process_group_ranks(group)) if group is not None else tuple(
+        range(dist.get_world_size()))
+    serial = _RING_SERIAL.get(ranks, 0)  # every rank creates its rings in the same order
+    _RING_SERIAL[ranks] = serial + 1
+    prefix = "fa4cp_ring/" + "_".join(map(str, ranks)) + f"/{serial}"
+    return RingLiveness(store, prefix, cp_rank, cp_size, RING_LIVENESS_TIMEOUT_S)
+
+
 class NativeRing:
     """The library's native ring executor (``fa4cp_ring_*``) for one cp group on one GPU.
 
@@ -264,6 +330,7 @@ class NativeRing:
             _lib.check(self.lib.fa4cp_ring_comm_init(uid, cp_size, cp_rank, ctypes.byref(h)),
                        "ring_comm_init")
         self.handle = h.value
+        self.liveness = _ring_liveness(group, cp_rank, cp_size)
 
     def ensure_capacity(self, kv_bytes: int) -> None:
         """Copy-engine transport: make the receive slots hold ``kv_bytes`` per K (and V).
@@ -300,6 +367,8 @@ class NativeRing:
 
         T, Hq, D = q.shape
         Hkv = k.shape[1]
+        if self.liveness is not None:
+            self.liveness.enter()  # raises if a neighbour left: nothing is queued then
         rc = self.lib.fa4cp_ring_attn_fwd(
             self.handle, q.data_ptr(), k.data_ptr(), v.data_ptr(), _lib.ptr(kv_bufs),
             0 if kv_bufs is None else kv_bufs.numel() * kv_bufs.element_size(), out.data_ptr(),

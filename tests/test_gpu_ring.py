@@ -177,6 +177,19 @@ def test_nccl_ring_multi_gpu():
     assert "RING_OK" in res.stdout
 
 
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs >= 2 GPUs")
+def test_ring_detects_a_departed_neighbour():
+    """A rank leaves between calls (nothing in flight); its neighbours' next ring call raises
+    on the host instead of queuing waits on it (tests/dist_liveness_check.py, NVLS off)."""
+    cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run",
+           "--nnodes=1", "--nproc-per-node=2", "--master-addr=127.0.0.1",
+           "--master-port=29534", os.path.join(ROOT, "tests", "dist_liveness_check.py")]
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    res = subprocess.run(cmd, capture_output=True, text=True, env=env, cwd=ROOT)
+    assert res.returncode == 0, res.stdout[-3000:] + res.stderr[-3000:]
+    assert "LIVENESS_OK rank 0" in res.stdout, res.stdout[-3000:]
+
+
 def test_ring_bf16_query_e4m3_kv_head_dim_256():
     """cfg5 in miniature: bf16 Q, e4m3 K/V quantised per rank (amax/448), D=256, cp=4,
     incremental; vs the oracle on the dequantised K/V (<= 6e-2)."""
