@@ -21,7 +21,6 @@ attention.  With a CPU process group (gloo) the same schedule runs with blocking
 hops; that path exists to test the rotation logic without a GPU.
 """
 
-import time
 from typing import Dict, Optional, Tuple
 
 import torch
@@ -231,12 +230,14 @@ class RingLiveness:
     The native ring's device-side waits on a neighbour (the copy-engine transport's hop
     counters, ``cuStreamWaitValue32``; NCCL send/recv on the executor's communicator) have no
     time limit: a neighbour that left between calls would block this rank's streams until
-    the process ends.  So every call first publishes its call number in the process group's
-    key-value store (``store.add``) and waits, polling with a deadline, until both neighbours
-    have published the same call number; if one has not after ``timeout_s`` seconds, the call
-    raises ``RuntimeError`` naming it, before anything is queued on the GPU.  Costs two or
-    three store round trips per call.  A neighbour that dies while a call runs is not caught
-    here (the ring kernel's own wait for a hop counter is bounded; the stream waits are not).
+    the process ends.  So call ``n`` first sets this rank's key for call ``n`` in the process
+    group's key-value store and waits (server side, ``store.wait``) for both neighbours' keys
+    of call ``n``; if one is missing after ``timeout_s`` seconds, the call raises
+    ``RuntimeError`` naming it, before anything is queued on the GPU.  Three store round trips
+    per call (set, wait, and deleting this rank's key of call ``n - 2``, which both neighbours
+    have read: they entered call ``n - 1``).  A neighbour that dies while a call runs is not
+    caught here (the ring kernel's own wait for a hop counter is bounded; the stream waits are
+    not).
     """
 
     def __init__(self, store, prefix: str, rank: int, size: int, timeout_s: float):
@@ -245,22 +246,26 @@ class RingLiveness:
         self.calls = 0
         self.peers = sorted({(rank - 1) % size, (rank + 1) % size} - {rank})
 
-    def _key(self, r: int) -> str:
-        return f"{self.prefix}/calls/{r}"
+    def _key(self, r: int, n: int) -> str:
+        return f"{self.prefix}/{r}/{n}"
 
     def enter(self) -> None:
-        self.calls = int(self.store.add(self._key(self.rank), 1))
-        deadline = time.monotonic() + self.timeout_s
-        pause = 0.0
-        for peer in self.peers:
-            while int(self.store.add(self._key(peer), 0)) < self.calls:
-                if time.monotonic() > deadline:
-                    raise RuntimeError(
-                        f"ring rank {self.rank}: neighbour rank {peer} has not entered ring call "
-                        f"{self.calls} within {self.timeout_s:.0f} s (it left or stalled); the "
-                        "call was not queued")
-                time.sleep(pause)
-                pause = min(0.01, pause + 0.0005)
+        import datetime
+
+        self.calls += 1
+        n = self.calls
+        self.store.set(self._key(self.rank, n), "1")
+        keys = [self._key(peer, n) for peer in self.peers]
+        try:
+            self.store.wait(keys, datetime.timedelta(seconds=self.timeout_s))
+        except Exception as e:  # the store's timeout error
+            gone = [peer for peer, k in zip(self.peers, keys) if not self.store.check([k])]
+            raise RuntimeError(
+                f"ring rank {self.rank}: neighbour rank {', '.join(map(str, gone or self.peers))} "
+                f"has not entered ring call {n} within {self.timeout_s:.0f} s (it left or "
+                "stalled); the call was not queued") from e
+        if n > 2:
+            self.store.delete_key(self._key(self.rank, n - 2))
 
 
 _RING_SERIAL: Dict[Tuple, int] = {}
