@@ -905,8 +905,11 @@ def main():
                     help="override the single-sequence length (smaller only for profiling)")
     ap.add_argument("--nccl-cta-policy", choices=["default", "zero"], default="default",
                     help="NCCL CTA policy of the ring's process group (zero: no SM CTAs)")
-    ap.add_argument("--transport", choices=["copy_engine", "nccl"], default="copy_engine",
-                    help="K/V transport of the native ring executor (N > 1)")
+    ap.add_argument("--transport", choices=["copy_engine", "copy_engine_chain", "nccl"],
+                    default="copy_engine",
+                    help="K/V transport of the native ring executor (N > 1): direct pushes to "
+                         "every peer (copy_engine), the chained rotation on the copy engines, "
+                         "or NCCL send/recv")
     ap.add_argument("--ring-kernel", choices=["fused", "fused-16bit", "steps"], default="fused",
                     help="copy-engine ring: one ring-kernel launch per forward (fused; "
                          "fused-16bit: not for e4m3) or one attention launch per step")

@@ -52,6 +52,17 @@ int launch_dequant_e4m3(const void* x, const float* descale, void* out, int64_t 
 // the calling host thread (attn_fwd_sm100.cu); 0 = use every SM
 void set_sm_reserve(int n);
 
+// fa4cp_ring_attn_fused with a general arrival-flag layout: slot s-1 is present once
+// arrived[(s-1) * arrived_stride] >= arrived_base + s * arrived_step (attn_fwd_sm100.cu)
+int ring_attn_fused_flags(const void* q, const void* k, const void* v, const void* slots_k,
+                          const void* slots_v, int64_t slot_stride, void* out, float* lse,
+                          const int32_t* cu, int32_t nseq, int32_t max_seqlen, int64_t total,
+                          int32_t num_heads_q, int32_t num_heads_kv, int32_t head_dim,
+                          int32_t dtype, float softmax_scale, const float* q_descale,
+                          const float* k_descales, const float* v_descales, int32_t nranks,
+                          int32_t rank, const uint32_t* arrived, uint32_t arrived_base,
+                          int32_t arrived_stride, int32_t arrived_step, void* stream);
+
 inline int elem_bytes(int dtype) {
   switch (dtype) {
     case FA4CP_DTYPE_F16: return 2;

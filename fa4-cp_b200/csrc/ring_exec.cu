@@ -78,8 +78,10 @@ NcclApi* nccl_api() {
 
 constexpr int kMaxRing = 64;
 constexpr int kDefaultSmReserve = 8;
-// streams of the copy-engine plan: the caller's, the K and V copies, the slot releases
-enum { ST_COMPUTE = 0, ST_COPY_K = 1, ST_COPY_V = 2, ST_RELEASE = 3, ST_COUNT = 4 };
+// streams of the copy-engine plans: the caller's, the K and V copies, the slot releases, and
+// a second K / V copy pair (direct pushes alternate destinations between the two pairs)
+enum { ST_COMPUTE = 0, ST_COPY_K = 1, ST_COPY_V = 2, ST_RELEASE = 3, ST_COPY_K2 = 4,
+       ST_COPY_V2 = 5, ST_COUNT = 6 };
 
 struct RingComm {
   ncclComm_t comm = nullptr;
@@ -95,12 +97,16 @@ struct RingComm {
   int t_used = 0, h_used = 0;
   // copy-engine transport
   bool ce = false;                       // transport: copy engine (else NCCL)
+  bool direct = true;                    // direct pushes (else chained hops); set before alloc
   uint8_t* area = nullptr;               // own receive area (cudaMalloc)
   uint8_t* right = nullptr;              // right neighbour's area (IPC mapping)
   uint8_t* left = nullptr;               // left neighbour's area (== right when nranks == 2)
+  uint8_t* peer[kMaxRing] = {};          // peer[d]: the area of rank rank + d (direct pushes)
   int64_t kv_cap = 0;                    // bytes of one K (or V) part of a slot
+  int64_t nslots = 0;                    // slots per part in the area
   uint64_t hops = 0;                     // hops issued since the area was (re)allocated
-  cudaStream_t cstream[4] = {};          // [1] K copy, [2] V copy, [3] release ([0]: caller's)
+  uint64_t calls = 0;                    // direct-push calls since the area was (re)allocated
+  cudaStream_t cstream[ST_COUNT] = {};   // copy and release streams ([0]: the caller's)
   std::vector<cudaEvent_t> cev;          // plan events
 };
 
@@ -142,8 +148,13 @@ void destroy_timing(RingComm* rc) {
 }
 
 void close_peers(RingComm* rc) {
-  if (rc->right) cudaIpcCloseMemHandle(rc->right);
-  if (rc->left && rc->left != rc->right) cudaIpcCloseMemHandle(rc->left);
+  std::unordered_set<uint8_t*> mapped;  // every mapping once (left == right when nranks == 2)
+  for (int d = 1; d < kMaxRing; ++d)
+    if (rc->peer[d]) mapped.insert(rc->peer[d]);
+  if (rc->right) mapped.insert(rc->right);
+  if (rc->left) mapped.insert(rc->left);
+  for (uint8_t* m : mapped) cudaIpcCloseMemHandle(m);
+  for (int d = 0; d < kMaxRing; ++d) rc->peer[d] = nullptr;
   rc->right = rc->left = nullptr;
   rc->ce = false;
 }
@@ -201,9 +212,21 @@ constexpr int ev_vdone(int s) { return 2 + s; }
 constexpr int ev_push(int s) { return 2 + kMaxRing + s; }
 constexpr int EV_COPY_END = 2 + 2 * kMaxRing;
 constexpr int EV_REL_END = 3 + 2 * kMaxRing;
-constexpr int EV_COUNT = 4 + 2 * kMaxRing;
-constexpr int64_t kFlagOffset[2] = {0, 128};  // ARRIVED, FREED (own 128-byte lines)
+constexpr int EV_COPY_END2 = 4 + 2 * kMaxRing;
+constexpr int EV_COUNT = 5 + 2 * kMaxRing;
 constexpr int64_t kSlotBase = 4096;           // receive slots start here in the area
+// flags (32-bit words of the area's first 4 KiB): chained hops use ARRIVED at byte 0 and FREED
+// at byte 128 (own 128-byte lines); direct pushes one arrival flag per slot (two sets of at
+// most kMaxRing - 1 slots) from byte 256 and FREED[d] from byte 1024
+constexpr int FLAG_SLOT0 = 2;
+constexpr int FLAG_PEER_FREED0 = 2 + 2 * kMaxRing;
+int64_t flag_offset(int64_t id) {
+  if (id == FLAG_ARRIVED) return 0;
+  if (id == FLAG_FREED) return 128;
+  if (id < FLAG_PEER_FREED0) return 256 + 4 * (id - FLAG_SLOT0);
+  return 1024 + 4 * (id - FLAG_PEER_FREED0);
+}
+static_assert(256 + 4 * 2 * kMaxRing <= 1024 && 1024 + 4 * kMaxRing <= kSlotBase, "flag layout");
 
 using RingOp = fa4cp_ring_op;
 
@@ -253,6 +276,73 @@ void build_ce_plan(int S, int rank, uint64_t g0, bool fused, std::vector<RingOp>
   op(ST_COMPUTE, FA4CP_RING_OP_WAIT_EVENT, EV_REL_END);
 }
 
+// ---------------------------------------------------------------------------------------
+// copy-engine transport, direct pushes: the plan of call number n (>= 1)
+//
+// Over NVSwitch every GPU reaches every peer at full bandwidth, so instead of forwarding
+// shards hop by hop (step s then waits for s - 1 transfers in a row), each rank pushes its
+// own K/V straight to every other rank at the start of the call:
+//   RECORD start on the compute stream;
+//   for d = 1 .. S-1 (rank + d attends this rank's K/V at its step d), on copy pair (d-1) % 2:
+//     both streams wait for start and, from call 3 on, for FREED[d] >= n - 2 (rank + d is done
+//     with the same slot set, used by call n - 2); K and V go to slot set*(S-1) + d-1 of
+//     rank + d (set = n % 2); then rank + d's arrival flag of that slot := n;
+//   the attention: per-step launches (step s > 0 after its slot's flag >= n on the compute
+//     stream) or the ring kernel, which waits for each slot's flag itself;
+//   RECORD done; the release stream waits for it and sets FREED[s] := n at rank - s for
+//     every s (the source of the slot this rank read at step s);
+//   the compute stream joins the copy and release streams.
+// A push depends only on the call's start and on releases two calls back, and an attention
+// only on this call's pushes, so no wait can close a cycle even if every stream of every rank
+// ran in host order on one queue.
+// ---------------------------------------------------------------------------------------
+void build_ce_direct_plan(int S, int rank, uint64_t n, bool fused, std::vector<RingOp>& ops) {
+  (void)rank;
+  ops.clear();
+  auto op = [&](int st, int kind, int64_t a = 0, int64_t b = 0, int64_t c = 0) {
+    ops.push_back(RingOp{st, kind, a, b, c});
+  };
+  const int64_t N = int64_t(uint32_t(n));  // flag value of this call
+  if (S == 1) {
+    op(ST_COMPUTE, FA4CP_RING_OP_ATTN, 0, -1);
+    return;
+  }
+  const int64_t set0 = int64_t(n & 1) * (S - 1);  // first slot of this call's set
+  op(ST_COMPUTE, FA4CP_RING_OP_RECORD, EV_START);
+  for (int d = 1; d < S; ++d) {
+    const int kst = (d - 1) % 2 ? ST_COPY_K2 : ST_COPY_K;
+    const int vst = (d - 1) % 2 ? ST_COPY_V2 : ST_COPY_V;
+    const int64_t slot = set0 + d - 1;
+    for (int st : {kst, vst}) {
+      op(st, FA4CP_RING_OP_WAIT_EVENT, EV_START);
+      if (n > 2) op(st, FA4CP_RING_OP_WAIT_FLAG, FLAG_PEER_FREED0 + d, int64_t(uint32_t(n - 2)));
+      op(st, FA4CP_RING_OP_COPY_TO, st == kst ? 0 : 1, d, slot);
+    }
+    op(vst, FA4CP_RING_OP_RECORD, ev_vdone(d));
+    op(kst, FA4CP_RING_OP_WAIT_EVENT, ev_vdone(d));
+    op(kst, FA4CP_RING_OP_WRITE_PEER, d, FLAG_SLOT0 + slot, N);
+    op(kst, FA4CP_RING_OP_RECORD, ev_push(d));
+  }
+  if (fused) {
+    op(ST_COMPUTE, FA4CP_RING_OP_ATTN_FUSED_SLOTS, S, N, set0);
+  } else {
+    for (int s = 0; s < S; ++s) {
+      if (s > 0) op(ST_COMPUTE, FA4CP_RING_OP_WAIT_FLAG, FLAG_SLOT0 + set0 + s - 1, N);
+      op(ST_COMPUTE, FA4CP_RING_OP_ATTN, s, s == 0 ? -1 : set0 + s - 1);
+    }
+  }
+  op(ST_COMPUTE, FA4CP_RING_OP_RECORD, EV_DONE);
+  op(ST_RELEASE, FA4CP_RING_OP_WAIT_EVENT, EV_DONE);
+  for (int s = 1; s < S; ++s)
+    op(ST_RELEASE, FA4CP_RING_OP_WRITE_PEER, S - s, FLAG_PEER_FREED0 + s, N);
+  op(ST_COPY_K, FA4CP_RING_OP_RECORD, EV_COPY_END);
+  if (S > 2) op(ST_COPY_K2, FA4CP_RING_OP_RECORD, EV_COPY_END2);
+  op(ST_RELEASE, FA4CP_RING_OP_RECORD, EV_REL_END);
+  op(ST_COMPUTE, FA4CP_RING_OP_WAIT_EVENT, EV_COPY_END);
+  if (S > 2) op(ST_COMPUTE, FA4CP_RING_OP_WAIT_EVENT, EV_COPY_END2);
+  op(ST_COMPUTE, FA4CP_RING_OP_WAIT_EVENT, EV_REL_END);
+}
+
 using StreamWaitValue32Fn = CUresult (*)(CUstream, CUdeviceptr, cuuint32_t, unsigned int);
 using StreamWriteValue32Fn = CUresult (*)(CUstream, CUdeviceptr, cuuint32_t, unsigned int);
 
@@ -290,6 +380,19 @@ extern "C" int fa4cp_ring_ce_plan(int32_t nranks, int32_t rank, int64_t g0, int3
                   "bad ring size %d / rank %d", nranks, rank);
   std::vector<RingOp> plan;
   build_ce_plan(nranks, rank, uint64_t(g0), fused != 0, plan);
+  FA4CP_CHECK_ARG(ops == nullptr || capacity >= int32_t(plan.size()),
+                  "capacity %d < %d plan entries", capacity, int(plan.size()));
+  if (ops != nullptr) memcpy(ops, plan.data(), plan.size() * sizeof(RingOp));
+  return int32_t(plan.size());
+}
+
+extern "C" int fa4cp_ring_ce_direct_plan(int32_t nranks, int32_t rank, int64_t call,
+                                         int32_t fused, fa4cp_ring_op* ops, int32_t capacity) {
+  FA4CP_CHECK_ARG(call >= 1, "call numbers start at 1");
+  FA4CP_CHECK_ARG(nranks >= 1 && nranks <= kMaxRing && rank >= 0 && rank < nranks,
+                  "bad ring size %d / rank %d", nranks, rank);
+  std::vector<RingOp> plan;
+  build_ce_direct_plan(nranks, rank, uint64_t(call), fused != 0, plan);
   FA4CP_CHECK_ARG(ops == nullptr || capacity >= int32_t(plan.size()),
                   "capacity %d < %d plan entries", capacity, int(plan.size()));
   if (ops != nullptr) memcpy(ops, plan.data(), plan.size() * sizeof(RingOp));
@@ -381,11 +484,14 @@ extern "C" int fa4cp_ring_ipc_alloc(int64_t handle, int64_t kv_capacity, uint8_t
   }
   const int64_t cap = (kv_capacity + 255) / 256 * 256;
   void* p = nullptr;
-  const int64_t nslots = rc->nranks > 1 ? rc->nranks - 1 : 1;
+  // per part (K, V): one slot per hop, times two alternating sets for direct pushes
+  const int64_t nslots = (rc->nranks > 1 ? rc->nranks - 1 : 1) * (rc->direct ? 2 : 1);
   FA4CP_CHECK_CUDA(cudaMalloc(&p, size_t(kSlotBase + 2 * nslots * cap)));
   rc->area = static_cast<uint8_t*>(p);
   rc->kv_cap = cap;
+  rc->nslots = nslots;
   rc->hops = 0;
+  rc->calls = 0;
   FA4CP_CHECK_CUDA(cudaMemset(rc->area, 0, size_t(kSlotBase)));
   FA4CP_CHECK_CUDA(cudaDeviceSynchronize());
   cudaIpcMemHandle_t h;
@@ -422,7 +528,47 @@ extern "C" int fa4cp_ring_ipc_open(int64_t handle, const uint8_t* left_ipc,
     }
     rc->left = static_cast<uint8_t*>(pl);
   }
+  rc->peer[1] = rc->right;
+  rc->peer[rc->nranks - 1] = rc->left;
   rc->ce = true;
+  return FA4CP_OK;
+}
+
+extern "C" int fa4cp_ring_ipc_open_all(int64_t handle, const uint8_t* ipc_handles) {
+  FA4CP_CHECK_ARG(handle != 0 && ipc_handles != nullptr, "null argument");
+  RingComm* rc = ring_of(handle);
+  FA4CP_CHECK_ARG(rc != nullptr, "unknown ring handle");
+  FA4CP_CHECK_ARG(rc->nranks > 1, "a ring of one rank has no peers");
+  FA4CP_CHECK_ARG(rc->area != nullptr, "fa4cp_ring_ipc_alloc must come first");
+  FA4CP_CHECK_ARG(stream_mem_ops() != nullptr,
+                  "cuStreamWaitValue32/cuStreamWriteValue32 are not available");
+  close_peers(rc);
+  for (int d = 1; d < rc->nranks; ++d) {
+    cudaIpcMemHandle_t h;
+    memcpy(&h, ipc_handles + 64 * ((rc->rank + d) % rc->nranks), sizeof(h));
+    void* ptr = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      close_peers(rc);
+      set_last_error("cudaIpcOpenMemHandle(rank %d) failed: %s", (rc->rank + d) % rc->nranks,
+                     cudaGetErrorString(e));
+      return FA4CP_ERR_CUDA;
+    }
+    rc->peer[d] = static_cast<uint8_t*>(ptr);
+  }
+  rc->right = rc->peer[1];
+  rc->left = rc->peer[rc->nranks - 1];
+  rc->ce = true;
+  return FA4CP_OK;
+}
+
+extern "C" int fa4cp_ring_set_direct(int64_t handle, int32_t on) {
+  FA4CP_CHECK_ARG(handle != 0, "null ring handle");
+  FA4CP_CHECK_ARG(on == 0 || on == 1, "direct must be 0 or 1");
+  RingComm* rc = ring_of(handle);
+  FA4CP_CHECK_ARG(rc != nullptr, "unknown ring handle");
+  FA4CP_CHECK_ARG(rc->area == nullptr, "set the push mode before fa4cp_ring_ipc_alloc");
+  rc->direct = on != 0;
   return FA4CP_OK;
 }
 
@@ -522,8 +668,8 @@ extern "C" int fa4cp_ring_timing_read(int64_t handle, double* total_ms, int32_t*
 
 namespace {
 
-// Issues the copy-engine plan of one call (build_ce_plan) on the caller's stream `st` and
-// the ring's copy / release streams.
+// Issues the copy-engine plan of one call (build_ce_plan, or build_ce_direct_plan for direct
+// pushes) on the caller's stream `st` and the ring's copy / release streams.
 template <class AttnStep, class AttnFused>
 int run_ce(RingComm* rc, AttnStep& attn_step, AttnFused* attn_fused, const void* k,
            const void* v, int64_t kv_bytes, cudaStream_t st) {
@@ -532,16 +678,27 @@ int run_ce(RingComm* rc, AttnStep& attn_step, AttnFused* attn_fused, const void*
                   static_cast<long long>(kv_bytes), static_cast<long long>(rc->kv_cap));
   StreamMemOps* mem = stream_mem_ops();
   FA4CP_CHECK_ARG(mem != nullptr, "stream memory operations are not available");
+  const bool direct = rc->direct;
+  FA4CP_CHECK_ARG(rc->nslots == (rc->nranks - 1) * (direct ? 2 : 1),
+                  "the receive area was allocated for the other push mode");
+  for (int d = 1; direct && d < rc->nranks; ++d)
+    FA4CP_CHECK_ARG(rc->peer[d] != nullptr, "direct pushes need every peer mapped "
+                    "(fa4cp_ring_ipc_open_all)");
   std::vector<RingOp> plan;
-  build_ce_plan(rc->nranks, rc->rank, rc->hops, attn_fused != nullptr, plan);
-  cudaStream_t streams[ST_COUNT] = {st, rc->cstream[1], rc->cstream[2], rc->cstream[3]};
-  const int64_t nslots = rc->nranks - 1;
+  const uint64_t call = rc->calls + 1;
+  if (direct)
+    build_ce_direct_plan(rc->nranks, rc->rank, call, attn_fused != nullptr, plan);
+  else
+    build_ce_plan(rc->nranks, rc->rank, rc->hops, attn_fused != nullptr, plan);
+  cudaStream_t streams[ST_COUNT];
+  streams[ST_COMPUTE] = st;
+  for (int i = 1; i < ST_COUNT; ++i) streams[i] = rc->cstream[i];
   // K slots 0 .. nslots-1, then V slots
   auto slot = [&](uint8_t* area, int64_t idx, int64_t part) {
-    return area + kSlotBase + (part * nslots + idx) * rc->kv_cap;
+    return area + kSlotBase + (part * rc->nslots + idx) * rc->kv_cap;
   };
-  auto flag = [&](uint8_t* area, int64_t which) {
-    return reinterpret_cast<CUdeviceptr>(area + kFlagOffset[which]);
+  auto flag = [&](uint8_t* area, int64_t id) {
+    return reinterpret_cast<CUdeviceptr>(area + flag_offset(id));
   };
   for (const RingOp& o : plan) {
     cudaStream_t cs = streams[o.stream];
@@ -567,12 +724,25 @@ int run_ce(RingComm* rc, AttnStep& attn_step, AttnFused* attn_fused, const void*
         FA4CP_CHECK_ARG(e == CUDA_SUCCESS, "cuStreamWriteValue32 failed (CUresult %d)", int(e));
         break;
       }
+      case FA4CP_RING_OP_WRITE_PEER: {
+        CUresult e = mem->write(cs, flag(rc->peer[o.a], o.b), cuuint32_t(o.c),
+                                CU_STREAM_WRITE_VALUE_DEFAULT);
+        FA4CP_CHECK_ARG(e == CUDA_SUCCESS, "cuStreamWriteValue32 failed (CUresult %d)", int(e));
+        break;
+      }
       case FA4CP_RING_OP_COPY: {
         const void* src = o.b < 0 ? (o.a == 0 ? k : v) : slot(rc->area, o.b, o.a);
         if (o.a == 0 && rc->h_used < int(rc->hev.size() / 2))
           FA4CP_CHECK_CUDA(cudaEventRecord(rc->hev[2 * rc->h_used], cs));
         FA4CP_CHECK_CUDA(cudaMemcpyAsync(slot(rc->right, o.c, o.a), src, size_t(kv_bytes),
                                          cudaMemcpyDeviceToDevice, cs));
+        break;
+      }
+      case FA4CP_RING_OP_COPY_TO: {
+        if (o.a == 0 && rc->h_used < int(rc->hev.size() / 2))
+          FA4CP_CHECK_CUDA(cudaEventRecord(rc->hev[2 * rc->h_used], cs));
+        FA4CP_CHECK_CUDA(cudaMemcpyAsync(slot(rc->peer[o.b], o.c, o.a), o.a == 0 ? k : v,
+                                         size_t(kv_bytes), cudaMemcpyDeviceToDevice, cs));
         break;
       }
       case FA4CP_RING_OP_ATTN: {
@@ -584,8 +754,15 @@ int run_ce(RingComm* rc, AttnStep& attn_step, AttnFused* attn_fused, const void*
       }
       case FA4CP_RING_OP_ATTN_FUSED: {
         int r = (*attn_fused)(slot(rc->area, 0, 0), slot(rc->area, 0, 1), rc->kv_cap,
-                              reinterpret_cast<const uint32_t*>(rc->area + kFlagOffset[FLAG_ARRIVED]),
-                              uint32_t(o.b));
+                              reinterpret_cast<const uint32_t*>(rc->area + flag_offset(FLAG_ARRIVED)),
+                              uint32_t(o.b), 0, 1);
+        if (r != FA4CP_OK) return r;
+        break;
+      }
+      case FA4CP_RING_OP_ATTN_FUSED_SLOTS: {
+        int r = (*attn_fused)(slot(rc->area, o.c, 0), slot(rc->area, o.c, 1), rc->kv_cap,
+                              reinterpret_cast<const uint32_t*>(rc->area + flag_offset(FLAG_SLOT0 + o.c)),
+                              uint32_t(o.b), 1, 0);
         if (r != FA4CP_OK) return r;
         break;
       }
@@ -594,7 +771,10 @@ int run_ce(RingComm* rc, AttnStep& attn_step, AttnFused* attn_fused, const void*
         return FA4CP_ERR_INVALID;
     }
   }
-  rc->hops += uint64_t(rc->nranks - 1);
+  if (direct)
+    rc->calls = call;
+  else
+    rc->hops += uint64_t(rc->nranks - 1);
   return FA4CP_OK;
 }
 
@@ -653,13 +833,13 @@ extern "C" int fa4cp_ring_attn_fwd(int64_t handle, const void* q, const void* k,
 
   // the persistent ring kernel: every step in one launch (f16 / bf16 D 64 or 128, e4m3 D 128)
   auto attn_fused = [&](const void* sk, const void* sv, int64_t stride, const uint32_t* arrived,
-                        uint32_t base) -> int {
+                        uint32_t base, int32_t flag_stride, int32_t flag_step) -> int {
     const bool timed = rc->t_used < int(rc->tev.size() / 2);
     if (timed) FA4CP_CHECK_CUDA(cudaEventRecord(rc->tev[2 * rc->t_used], st));
-    int r = fa4cp_ring_attn_fused(q, k, v, sk, sv, stride, out, lse, cu, nseq, max_seqlen, total,
+    int r = ring_attn_fused_flags(q, k, v, sk, sv, stride, out, lse, cu, nseq, max_seqlen, total,
                                   num_heads_q, num_heads_kv, head_dim, q_dtype, softmax_scale,
                                   q_descale, k_descales, v_descales, S, rank, arrived, base,
-                                  stream);
+                                  flag_stride, flag_step, stream);
     if (r != FA4CP_OK) return r;
     if (timed) FA4CP_CHECK_CUDA(cudaEventRecord(rc->tev[2 * rc->t_used++ + 1], st));
     return FA4CP_OK;
@@ -669,7 +849,8 @@ extern "C" int fa4cp_ring_attn_fwd(int64_t handle, const void* q, const void* k,
       ((rc->fused >= 1 && (q_dtype == FA4CP_DTYPE_BF16 || q_dtype == FA4CP_DTYPE_F16) &&
         (head_dim == 64 || head_dim == 128)) ||
        (rc->fused >= 2 && q_dtype == FA4CP_DTYPE_E4M3 && head_dim == 128));
-  if (S == 1) return fusable ? attn_fused(nullptr, nullptr, 0, nullptr, 0) : attn_step(0, k, v);
+  if (S == 1)
+    return fusable ? attn_fused(nullptr, nullptr, 0, nullptr, 0, 0, 1) : attn_step(0, k, v);
   if (rc->ce)
     return run_ce(rc, attn_step, fusable ? &attn_fused : nullptr, k, v, kv_bytes, st);
 

@@ -17,16 +17,21 @@
 // the softmax warps rescale O by old / new (together with any lazy max rescale), and the
 // epilogue multiplies by the last one.  Both query tiles of a CTA walk the same number of K/V
 // tiles: at the end of step 0 the lower tile walks one tile past its diagonal, which the
-// causal mask zeroes.  Before the producer's first load of slot s-1 it waits (bounded) for
-// the rank's ARRIVED hop counter to reach arrived_base + s.
+// causal mask zeroes.  Before the producer's first load of slot s-1 it waits (bounded) until
+// that slot's arrival flag says it is present (RingFusedParams::arrived).
 #pragma once
 
 struct RingFusedParams {
   const int32_t* cu;          // local cu [nseq + 1] (every length even)
   void* out;                  // [total, Hq, D], q dtype
   float* lse;                 // [total, Hq]
-  const uint32_t* arrived;    // this rank's ARRIVED counter, or nullptr (all slots present)
-  uint32_t arrived_base;      // slot s-1 is present once *arrived >= arrived_base + s
+  // arrival of the receive slots, or nullptr (all slots present): slot s-1 is present once
+  // arrived[(s-1) * arrived_stride] >= arrived_base + s * arrived_step -- one hop counter for
+  // the chained rotation (stride 0, step 1), or one flag per slot holding the call number for
+  // the direct pushes (stride 1, step 0)
+  const uint32_t* arrived;
+  uint32_t arrived_base;
+  int arrived_stride, arrived_step;
   int nseq, Hq, Hkv, group, S, rank;
   int n_pairs;                // query-tile pairs per half, max over sequences
   int n_tiles;                // tiles of the schedule (ring_grid); the grid walks them
@@ -284,8 +289,9 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
         const int row = g.a + (j - cur.first) * BN;
         if (cur.s > waited) {
           if (p.arrived != nullptr &&
-              !wait_arrived(p.arrived, p.arrived_base + uint32_t(cur.s), p.arrive_wait_ns, abort,
-                            status))
+              !wait_arrived(p.arrived + (cur.s - 1) * p.arrived_stride,
+                            p.arrived_base + uint32_t(cur.s * p.arrived_step), p.arrive_wait_ns,
+                            abort, status))
             break;
           waited = cur.s;
         }
@@ -701,8 +707,9 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
           const int row = x.g.a + (j - cur.first) * BN;
           if (cur.s > waited) {
             if (p.arrived != nullptr &&
-                !wait_arrived(p.arrived, p.arrived_base + uint32_t(cur.s), p.arrive_wait_ns, abort,
-                              status)) { ok = false; break; }
+                !wait_arrived(p.arrived + (cur.s - 1) * p.arrived_stride,
+                              p.arrived_base + uint32_t(cur.s * p.arrived_step), p.arrive_wait_ns,
+                              abort, status)) { ok = false; break; }
             waited = cur.s;
           }
           if (kv_it >= ST && !mbar_wait(k_empty(s), ph ^ 1, abort, kErrKEmpty, status)) { ok = false; break; }

@@ -71,6 +71,9 @@ _SIGNATURES = {
     "fa4cp_ring_ipc_open": [_i64, _vp, _vp],
     "fa4cp_ring_ipc_close": [_i64],
     "fa4cp_ring_ce_plan": [_i32, _i32, _i64, _i32, _vp, _i32],
+    "fa4cp_ring_ce_direct_plan": [_i32, _i32, _i64, _i32, _vp, _i32],
+    "fa4cp_ring_set_direct": [_i64, _i32],
+    "fa4cp_ring_ipc_open_all": [_i64, _vp],
     "fa4cp_ring_attn_fused": [_vp, _vp, _vp, _vp, _vp, _i64, _vp, _vp, _vp, _i32, _i32, _i64,
                               _i32, _i32, _i32, _i32, _f32, _vp, _vp, _vp, _i32, _i32, _vp,
                               ctypes.c_uint32, _vp],

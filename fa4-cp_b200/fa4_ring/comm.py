@@ -296,17 +296,22 @@ class NativeRing:
     attention step) from C++, so the host cost per step is a few CUDA API calls instead of
     a Python loop over ``torch.distributed`` P2P ops.  Transports:
 
-    * ``"copy_engine"`` (default): each hop is a ``cudaMemcpyAsync`` straight into the right
-      neighbour's receive slot over NVLink (CUDA IPC mappings exchanged over ``group``), with
-      arrival / release hop counters written into the peers' memory and waited on by the
-      streams (``cuStreamWriteValue32`` / ``cuStreamWaitValue32``): the rotation uses no SM;
+    * ``"copy_engine"`` (default): at the start of a call every rank pushes its own K/V with
+      ``cudaMemcpyAsync`` straight into every peer's receive slot over NVSwitch (CUDA IPC
+      mappings exchanged over ``group``), in step order, and sets that slot's arrival flag in
+      the peer's memory (``cuStreamWriteValue32``); the attention waits for each slot's flag
+      (the ring kernel in-kernel, per-step launches with ``cuStreamWaitValue32``).  Slots come
+      in two sets used by alternate calls.  The transfer uses no SM;
+    * ``"copy_engine_chain"``: the reference's chain-forward rotation on the copy engines --
+      hop ``s`` forwards the K/V attended at step ``s - 1`` into the right neighbour's slot,
+      with one arrival and one release hop counter per rank;
     * ``"nccl"``: NCCL send/recv on the executor's own communicator (created collectively
       from a unique id that cp rank 0 broadcasts over ``group``).
 
     Call :func:`close_native_rings` on every rank before ``destroy_process_group``.
     """
 
-    TRANSPORTS = ("copy_engine", "nccl")
+    TRANSPORTS = ("copy_engine", "copy_engine_chain", "nccl")
 
     def __init__(self, cp_rank: int, cp_size: int, device: torch.device,
                  group: Optional["dist.ProcessGroup"] = None, transport: str = "copy_engine"):
@@ -335,6 +340,11 @@ class NativeRing:
             _lib.check(self.lib.fa4cp_ring_comm_init(uid, cp_size, cp_rank, ctypes.byref(h)),
                        "ring_comm_init")
         self.handle = h.value
+        self.copy_engine = transport.startswith("copy_engine")
+        if self.copy_engine:
+            _lib.check(self.lib.fa4cp_ring_set_direct(self.handle,
+                                                      int(transport == "copy_engine")),
+                       "ring_set_direct")
         self.liveness = _ring_liveness(group, cp_rank, cp_size)
 
     def ensure_capacity(self, kv_bytes: int) -> None:
@@ -344,7 +354,7 @@ class NativeRing:
 
         from . import _lib
 
-        if self.transport != "copy_engine" or self.size < 2 or kv_bytes <= self.kv_capacity:
+        if not self.copy_engine or self.size < 2 or kv_bytes <= self.kv_capacity:
             return
         with torch.cuda.device(self.device):
             torch.cuda.synchronize()
@@ -357,9 +367,15 @@ class NativeRing:
             handles = [None] * self.size
             dist.all_gather_object(handles, (bytes(mine), int(kv_bytes)), group=self.group)
             assert all(hb[1] == kv_bytes for hb in handles), "ranks disagree on the K/V size"
-            left = (ctypes.c_uint8 * 64)(*handles[(self.rank - 1) % self.size][0])
-            right = (ctypes.c_uint8 * 64)(*handles[(self.rank + 1) % self.size][0])
-            _lib.check(self.lib.fa4cp_ring_ipc_open(self.handle, left, right), "ring_ipc_open")
+            if self.transport == "copy_engine":  # direct pushes: every peer's area
+                allh = (ctypes.c_uint8 * (64 * self.size))(*b"".join(hb[0] for hb in handles))
+                _lib.check(self.lib.fa4cp_ring_ipc_open_all(self.handle, allh),
+                           "ring_ipc_open_all")
+            else:
+                left = (ctypes.c_uint8 * 64)(*handles[(self.rank - 1) % self.size][0])
+                right = (ctypes.c_uint8 * 64)(*handles[(self.rank + 1) % self.size][0])
+                _lib.check(self.lib.fa4cp_ring_ipc_open(self.handle, left, right),
+                           "ring_ipc_open")
             dist.barrier(group=self.group)  # every area is mapped before the first push
         self.kv_capacity = int(kv_bytes)
 
@@ -470,7 +486,7 @@ def close_native_rings() -> None:
     rings = [ring for _, ring in _NATIVE_RINGS.values()]
     for ring in rings:
         ring.unmap_peers()
-    if any(r.transport == "copy_engine" and r.size > 1 for r in rings) and dist.is_initialized():
+    if any(r.copy_engine and r.size > 1 for r in rings) and dist.is_initialized():
         dist.barrier()
     for ring in rings:
         ring.close()

@@ -175,8 +175,10 @@ class _RingFlashAttnFn(torch.autograd.Function):
 # Run incremental-mode rings over an NCCL group through the native executor
 # (fa4cp_ring_attn_fwd); False keeps the Python step loop over KVRing.
 NATIVE_EXECUTOR = True
-# K/V transport of the native executor: "copy_engine" (NVLink copies + stream counters, no
-# SM used) or "nccl" (send/recv on the executor's own communicator)
+# K/V transport of the native executor: "copy_engine" (each rank pushes its K/V straight into
+# every peer's receive slot over NVSwitch, per-slot arrival flags, no SM used),
+# "copy_engine_chain" (the chain-forward rotation on the copy engines, hop counters) or "nccl"
+# (send/recv on the executor's own communicator)
 RING_TRANSPORT = "copy_engine"
 # copy engine: run the whole forward as one launch of the ring kernel -- True: for f16 / bf16
 # with D 64 or 128 and e4m3 with D 128; "16bit": f16 / bf16 only; False: one attention launch
@@ -226,7 +228,7 @@ def _native_forward(q, k, v, cfg: RingConfig, group, *, cu, nseq, max_seqlen,
     ring.forward(
         q, k, v, out, lse, cu, nseq=nseq, max_seqlen=max_seqlen, softmax_scale=scale,
         q_descale=qd, k_descales=kds, v_descales=vds, kv_bufs=bufs, workspace=ws)
-    fused = (ring.transport == "copy_engine" and bool(RING_FUSED) and q.dtype == k.dtype
+    fused = (ring.copy_engine and bool(RING_FUSED) and q.dtype == k.dtype
              and ((q.dtype in (torch.float16, torch.bfloat16) and D in (64, 128))
                   or (RING_FUSED is True and q.dtype == torch.float8_e4m3fn and D == 128)))
     # the e4m3 ring kernel runs as a main pass and a split pass (rows that see few keys)

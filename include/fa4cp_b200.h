@@ -334,7 +334,7 @@ FA4CP_API int fa4cp_local_cu(const int32_t* full_cu, int32_t nseq, int32_t cp_si
  *   persistent ring kernel (fused 1); returns the count (ops may be NULL to ask for it).
  */
 typedef struct {
-  int32_t stream; /* 0 caller's (compute), 1 K copy, 2 V copy, 3 release */
+  int32_t stream; /* 0 caller's (compute), 1 K copy, 2 V copy, 3 release, 4 K copy 2, 5 V copy 2 */
   int32_t kind;   /* FA4CP_RING_OP_* */
   int64_t a, b, c;
 } fa4cp_ring_op;
@@ -348,12 +348,42 @@ typedef struct {
                                       slot b) */
 #define FA4CP_RING_OP_ATTN_FUSED 6 /* persistent ring kernel over a steps; before reading
                                       slot s-1 it waits for own ARRIVED >= b + s */
+/* direct pushes (fa4cp_ring_set_direct): flags are 32-bit words of the receive area's header,
+ * flag 2 + i = the arrival flag of slot i, flag 130 + d = FREED[d] (the release, by rank
+ * rank + d, of the slot holding this rank's K/V); WAIT_FLAG a is such a flag index */
+#define FA4CP_RING_OP_COPY_TO 7    /* part a (0 K, 1 V) of the caller's K/V -> slot c of rank
+                                      rank + b */
+#define FA4CP_RING_OP_WRITE_PEER 8 /* write flag b of rank rank + a := c */
+#define FA4CP_RING_OP_ATTN_FUSED_SLOTS 9 /* persistent ring kernel over a steps on own slots
+                                      c .. c+a-2; before reading slot c+s-1 it waits for that
+                                      slot's arrival flag >= b */
 FA4CP_API int fa4cp_ring_ipc_alloc(int64_t handle, int64_t kv_capacity, uint8_t* ipc_out);
 FA4CP_API int fa4cp_ring_ipc_open(int64_t handle, const uint8_t* left_ipc,
                                   const uint8_t* right_ipc);
 FA4CP_API int fa4cp_ring_ipc_close(int64_t handle);
 FA4CP_API int fa4cp_ring_ce_plan(int32_t nranks, int32_t rank, int64_t g0, int32_t fused,
                                  fa4cp_ring_op* ops, int32_t capacity);
+
+/*
+ * Direct pushes (the copy-engine transport's default over NVSwitch; no counterpart in the
+ * reference, whose rotation is a chain of P2P hops, fa4_ring/ring_attention.py:121-136):
+ * at the start of call n every rank copies its own K/V straight into slot d-1 of rank
+ * rank + d (d = 1 .. nranks-1, step order, two pairs of copy streams), then sets that slot's
+ * arrival flag to n; the attention of step s waits for its slot's flag (the ring kernel does
+ * so itself).  Slots come in two sets used by alternate calls, so a push of call n waits only
+ * for the destination's release of call n-2: no call waits for the end of the previous one.
+ * After its attention a rank sets FREED[s] := n at rank rank - s for every s.
+ * fa4cp_ring_set_direct: on (1) or off (0, the chained hops of fa4cp_ring_ce_plan); call before
+ *   fa4cp_ring_ipc_alloc (the area holds two slot sets when on).
+ * fa4cp_ring_ipc_open_all: maps every peer's area (HOST: nranks x 64-byte handles, this rank's
+ *   own included, indexed by rank); needed by direct pushes, enough for chained hops too.
+ * fa4cp_ring_ce_direct_plan: the ordered operations of call number `call` (>= 1) with direct
+ *   pushes (host only, no GPU needed); returns the count (ops may be NULL to ask for it).
+ */
+FA4CP_API int fa4cp_ring_set_direct(int64_t handle, int32_t on);
+FA4CP_API int fa4cp_ring_ipc_open_all(int64_t handle, const uint8_t* ipc_handles);
+FA4CP_API int fa4cp_ring_ce_direct_plan(int32_t nranks, int32_t rank, int64_t call, int32_t fused,
+                                        fa4cp_ring_op* ops, int32_t capacity);
 
 /*
  * Persistent ring kernel: the whole zig-zag ring forward of one rank in ONE launch.  Each

@@ -3,8 +3,9 @@
 oracle's dense causal attention.
 
 Cases: bf16 single and packed sequences in ``incremental`` mode through the native C++
-executor (``fa4cp_ring_attn_fwd``) with both transports (copy engine -- the persistent
-ring kernel, and one launch per step -- and NCCL) and through
+executor (``fa4cp_ring_attn_fwd``) with every transport (copy engine with direct pushes -- the
+persistent ring kernel three calls in a row, so both slot sets are reused, and one launch per
+step -- the chained copy-engine rotation, and NCCL) and through
 the Python step loop over ``KVRing``, and in ``batched`` mode; FP8 e4m3 Q/K/V and bf16 Q
 with e4m3 K/V (quantised per rank, descales all-gathered by source rank) through the
 native executor, checked against the dense attention of the dequantised tensors.  The
@@ -57,7 +58,9 @@ def main():
         H, Hkv, D = 8, 2, 128
         scale = 1.0 / math.sqrt(D)
         runs = [("bf16", "incremental", "copy_engine"), ("bf16", "incremental", "copy_engine"),
-                ("bf16", "incremental", "copy_engine_steps"),
+                ("bf16", "incremental", "copy_engine"), ("bf16", "incremental", "copy_engine_steps"),
+                ("bf16", "incremental", "copy_engine_chain"), ("bf16", "incremental", "copy_engine_chain"),
+                ("e4m3", "incremental", "copy_engine_chain"),
                 ("bf16", "incremental", "nccl"), ("bf16", "incremental", "python"),
                 ("bf16", "batched", "python"), ("e4m3", "incremental", "copy_engine"),
                 ("e4m3", "incremental", "copy_engine_steps"),
@@ -80,7 +83,7 @@ def main():
                 ring_attention.NATIVE_EXECUTOR = executor != "python"
                 ring_attention.RING_FUSED = executor != "copy_engine_steps"
                 if executor != "python":
-                    ring_attention.RING_TRANSPORT = ("copy_engine" if executor.startswith("copy")
+                    ring_attention.RING_TRANSPORT = ("copy_engine" if executor == "copy_engine_steps"
                                                      else executor)
                 cfg = RingConfig(cp_size=world, cp_rank=rank, merge_mode=mode)
                 tq, tk, tv, desc = lq, lk, lv, None
