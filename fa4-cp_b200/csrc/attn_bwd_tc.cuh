@@ -269,13 +269,17 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint8_t* ds_s = smem + OFF_DS;
     const int shift = geo.kl - geo.ql;
     bool aborted = false;
-    for (int t = 0; t < n_tiles && !aborted; ++t) {
+    // Every softmax warp runs every trip of this loop and reaches every named_sync(1, 128)
+    // (which needs all four warps) even after a bounded wait of its own gave up: a give-up
+    // only skips the waits and the work of the later trips.  Leaving the loop early would
+    // strand the other warps at the named barrier.
+    for (int t = 0; t < n_tiles; ++t) {
       const int b = t & 1;
       const int q0 = tile_q0(t), hq = tile_head(t);
       float* lse_t = ld_s + b * 2 * BMQ;
       float* del_t = lse_t + BMQ;
       // this tile's LSE (natural log -> log2, +inf where no key / past the end) and Delta
-      {
+      if (!aborted) {
         const int i = r & (BMQ - 1);
         const bool ok_row = q0 + i < geo.ql;
         const int64_t idx = (int64_t(geo.qs) + q0 + i) * p.Hq + hq;
@@ -287,8 +291,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
       named_sync(1, 128);
+      if (aborted) continue;
       bool ok = mbar_wait(s_full, t & 1, abort, kErrBase + 8, status);
-      if (!__all_sync(0xffffffffu, ok)) { aborted = true; break; }
+      if (!__all_sync(0xffffffffu, ok)) { aborted = true; continue; }
       tc_fence_after();
       uint32_t sv[2][32], dv[2][32];
       tmem_ld32(t_lane + TM_ST, sv[0]);
@@ -318,7 +323,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       // XOR-swizzled by r % 8, as a 128-byte-swizzled TMA copy would place them)
       if (t >= 2) {
         ok = mbar_wait(ds_free(b), ((t >> 1) - 1) & 1, abort, kErrBase + 9, status);
-        if (!__all_sync(0xffffffffu, ok)) { aborted = true; break; }
+        if (!__all_sync(0xffffffffu, ok)) { aborted = true; continue; }
       }
       uint8_t* row = ds_s + b * DS_BYTES + r * 128;
 #pragma unroll

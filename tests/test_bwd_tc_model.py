@@ -229,3 +229,40 @@ def test_staged_kernel_compiles_for_sm100a(tmp_path):
                           "-O3", "-std=c++17", "--expt-relaxed-constexpr", "-c", HEADER, "-o",
                           str(tmp_path / "tc.o")], capture_output=True, text=True)
     assert res.returncode == 0, res.stderr[-2000:]
+
+
+def test_softmax_warps_reach_every_named_barrier_after_a_give_up():
+    """The staged kernel's four softmax warps share named barrier 1 (128 threads) once per
+    query tile.  If one warp's bounded wait expires while the others' succeed, the warp that
+    gave up must still reach every later named_sync, or the others wait there forever.  The
+    loop is modelled trip by trip (named_sync, then the waits, which expire for the chosen warp
+    at the chosen trip, or for every warp once the CTA's abort flag is up); every warp must
+    arrive at the barrier exactly n_tiles times for every choice.  A source guard keeps the
+    loop free of `break`."""
+    import itertools
+    import re
+
+    src = open(os.path.join(ROOT, "fa4-cp_b200", "csrc", "attn_bwd_tc.cuh")).read()
+    loop = src[src.index("Every softmax warp runs every trip"):src.index("dK / dV of this key row")]
+    assert "named_sync(1, 128)" in loop and not re.search(r"\bbreak\b", loop)
+
+    n_tiles, warps = 5, 4
+    for bad_warp, bad_trip, which in itertools.product(range(warps), range(n_tiles), (0, 1)):
+        arrivals = [0] * warps
+        aborted = [False] * warps
+        cta_abort = False
+        for t in range(n_tiles):
+            for w in range(warps):
+                arrivals[w] += 1  # named_sync(1, 128)
+                if aborted[w]:
+                    continue
+                # s_full wait, then (t >= 2) the ds_free wait; a wait gives up when its own
+                # limit expires or when another warp already raised the CTA's abort flag
+                for k, needed in ((0, True), (1, t >= 2)):
+                    if not needed or aborted[w]:
+                        continue
+                    expired = (w == bad_warp and t == bad_trip and k == which) or cta_abort
+                    if expired:
+                        aborted[w] = True
+                        cta_abort = True
+        assert arrivals == [n_tiles] * warps, (bad_warp, bad_trip, which, arrivals)
