@@ -555,9 +555,10 @@ def gpu_main(args, rank, world, local_rank):
                       f"tokens; {flops_cpu:.3e} FLOP in {secs_cpu:.1f} s"}
     if world == 1:
         line["hbm_kernels"] = hbm_kernels(dev)
-    traffic = _traffic_from_profile(args.config, world)
+    traffic, traffic_src = _traffic_from_profile(args.config, world)
     if traffic is not None:
         line["roofline"]["traffic"] = traffic
+        line["roofline"]["traffic_source"] = traffic_src
     return line
 
 
@@ -797,15 +798,22 @@ def _bwd_cpu_baseline():
 
 
 def _traffic_from_profile(config, world):
-    """DRAM bytes per attention launch recorded from an ncu capture of this workload
-    (profiles/attn_fwd_traffic.json), or None when none was captured."""
+    """(DRAM bytes per attention launch, provenance) recorded from an ncu capture of this
+    workload (profiles/attn_fwd_traffic.json: ncu cannot run inside the timed bench), or
+    (None, None) when none was captured.  The provenance names the commit of the capture, so
+    a figure older than the kernel shows as such."""
     path = os.path.join(ROOT, "profiles", "attn_fwd_traffic.json")
     try:
         with open(path) as f:
             t = json.load(f)
-        return t.get(f"{config}_cp{world}")
     except (OSError, ValueError):
-        return None
+        return None, None
+    v = t.get(f"{config}_cp{world}")
+    if v is None:
+        return None, None
+    return v, (f"ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch of this "
+               f"workload, captured at commit {t.get('captured_at_commit', '?')} "
+               f"(profiles/attn_fwd_traffic.json)")
 
 
 # --------------------------------------------------------------------------- HBM-bound kernels

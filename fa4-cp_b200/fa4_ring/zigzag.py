@@ -8,7 +8,10 @@ one and the local shards stay packed in sequence order.
 Every function here moves data with the gather/scatter kernels of the CUDA library
 (``fa4cp_zigzag_shard``, ``fa4cp_zigzag_unshard``, ``fa4cp_half_index``,
 ``fa4cp_local_cu``); inputs must be CUDA tensors.  The only host work is validating
-sequence lengths, as the reference does with its ``assert``s.
+sequence lengths, as the reference does with its ``assert``s -- for boundaries given on the
+host.  Boundaries given as a CUDA tensor are trusted and never copied to the host (the
+reference's ``.tolist()`` at ``fa4_ring/zigzag.py:71`` is a device->host sync): the packed
+length comes from the tensors' shapes, or from ``total=`` for :func:`get_half_index`.
 """
 
 import math
@@ -70,6 +73,10 @@ def _cu_list(cu) -> List[int]:
     return [int(c) for c in (cu.tolist() if torch.is_tensor(cu) else cu)]
 
 
+def _on_device(cu) -> bool:
+    return torch.is_tensor(cu) and cu.is_cuda
+
+
 def _cu_device(cu, device) -> torch.Tensor:
     if torch.is_tensor(cu) and cu.is_cuda and cu.dtype == torch.int32 and cu.is_contiguous():
         return cu
@@ -86,14 +93,21 @@ def zigzag_shard_varlen(x: torch.Tensor, full_cu_seqlens: Union[torch.Tensor, Se
     ``(local_packed, local_cu_seqlens)`` with ``local_cu_seqlens`` int32 on ``x.device``.
     """
     _lib.require_cuda(x)
-    cu = _cu_list(full_cu_seqlens)
-    assert len(cu) >= 1 and cu[0] == 0, "cu_seqlens must start at 0"
-    for j in range(len(cu) - 1):
-        n = cu[j + 1] - cu[j]
-        assert n >= 0, "cu_seqlens must be non-decreasing"
-        assert n % (2 * cp_size) == 0, f"seqlen {n} must be divisible by 2*cp_size={2 * cp_size}"
-    assert cu[-1] <= x.shape[0], "cu_seqlens exceed the packed tensor"
-    nseq = len(cu) - 1
+    if _on_device(full_cu_seqlens):
+        # trusted (no host copy): the sequences must cover x exactly
+        nseq = full_cu_seqlens.numel() - 1
+        total = x.shape[0]
+        assert total % (2 * cp_size) == 0, "the packed length must be divisible by 2*cp_size"
+    else:
+        cu = _cu_list(full_cu_seqlens)
+        assert len(cu) >= 1 and cu[0] == 0, "cu_seqlens must start at 0"
+        for j in range(len(cu) - 1):
+            n = cu[j + 1] - cu[j]
+            assert n >= 0, "cu_seqlens must be non-decreasing"
+            assert n % (2 * cp_size) == 0, f"seqlen {n} must be divisible by 2*cp_size={2 * cp_size}"
+        assert cu[-1] <= x.shape[0], "cu_seqlens exceed the packed tensor"
+        nseq = len(cu) - 1
+        total = cu[-1]
     x = x.contiguous()
     cu_dev = _cu_device(full_cu_seqlens, x.device)
     local_cu = torch.empty(nseq + 1, dtype=torch.int32, device=x.device)
@@ -101,7 +115,6 @@ def zigzag_shard_varlen(x: torch.Tensor, full_cu_seqlens: Union[torch.Tensor, Se
     lib = _lib.load()
     _lib.check(lib.fa4cp_local_cu(cu_dev.data_ptr(), nseq, cp_size, local_cu.data_ptr(), stream),
                "local_cu")
-    total = cu[-1]
     out = torch.empty((total // cp_size,) + tuple(x.shape[1:]), dtype=x.dtype, device=x.device)
     if nseq > 0 and out.numel() > 0:
         _lib.check(lib.fa4cp_zigzag_shard(
@@ -114,35 +127,47 @@ def zigzag_unshard_varlen(local_shards: List[torch.Tensor], full_cu_seqlens, cp_
     """Stitch per-rank packed varlen shards back into the full packed ``[sum N_j, ...]``."""
     _lib.require_cuda(*local_shards)
     assert len(local_shards) == cp_size
-    cu = _cu_list(full_cu_seqlens)
-    for j in range(len(cu) - 1):
-        assert (cu[j + 1] - cu[j]) % (2 * cp_size) == 0
     shards = [s.contiguous() for s in local_shards]
     t0 = shards[0]
-    total = cu[-1]
-    assert t0.shape[0] * cp_size == total
+    total = t0.shape[0] * cp_size
+    if _on_device(full_cu_seqlens):
+        nseq = full_cu_seqlens.numel() - 1  # trusted (no host copy)
+    else:
+        cu = _cu_list(full_cu_seqlens)
+        for j in range(len(cu) - 1):
+            assert (cu[j + 1] - cu[j]) % (2 * cp_size) == 0
+        assert cu[-1] == total, "the shards do not hold the sequences"
+        nseq = len(cu) - 1
     out = torch.empty((total,) + tuple(t0.shape[1:]), dtype=t0.dtype, device=t0.device)
     cu_dev = _cu_device(full_cu_seqlens, t0.device)
     if out.numel() > 0:
         _lib.check(_lib.load().fa4cp_zigzag_unshard(
-            _lib.ptr_array(shards), out.data_ptr(), cu_dev.data_ptr(), len(cu) - 1, total, cp_size,
+            _lib.ptr_array(shards), out.data_ptr(), cu_dev.data_ptr(), nseq, total, cp_size,
             _row_bytes(t0), _lib.stream_of(t0)), "zigzag_unshard_varlen")
     return out
 
 
-def get_half_index(cu_seqlens: torch.Tensor, *, front: bool) -> torch.Tensor:
+def get_half_index(cu_seqlens: torch.Tensor, *, front: bool, total: int = None) -> torch.Tensor:
     """int64 indices of the front (early) or back (late) half of every packed local
-    sequence (fa4_ring/zigzag.py:65-79), computed by a kernel on ``cu_seqlens.device``."""
+    sequence (fa4_ring/zigzag.py:65-79), computed by a kernel on ``cu_seqlens.device``.
+
+    ``total`` (keyword, not in the reference): the packed length ``cu_seqlens[-1]``, when the
+    caller knows it.  Given, the call reads nothing back from the device (the boundaries are
+    trusted); omitted, ``cu_seqlens`` is copied to the host to size the output and check that
+    every length is even, as the reference does."""
     _lib.require_cuda(cu_seqlens)
-    cu = _cu_list(cu_seqlens)
-    for i in range(len(cu) - 1):
-        assert (cu[i + 1] - cu[i]) % 2 == 0, "each local sequence length must be even (zig-zag)"
-    total = cu[-1] if cu else 0
+    if total is None:
+        cu = _cu_list(cu_seqlens)
+        for i in range(len(cu) - 1):
+            assert (cu[i + 1] - cu[i]) % 2 == 0, "each local sequence length must be even (zig-zag)"
+        total = cu[-1] if cu else 0
+    nseq = cu_seqlens.numel() - 1
+    assert total % 2 == 0, "the packed local length must be even (zig-zag)"
     out = torch.empty(total // 2, dtype=torch.long, device=cu_seqlens.device)
-    if len(cu) >= 2 and total > 0:
+    if nseq >= 1 and total > 0:
         cu_dev = _cu_device(cu_seqlens, cu_seqlens.device)
         _lib.check(_lib.load().fa4cp_half_index(
-            cu_dev.data_ptr(), len(cu) - 1, total, 1 if front else 0, out.data_ptr(),
+            cu_dev.data_ptr(), nseq, total, 1 if front else 0, out.data_ptr(),
             _lib.stream_of(cu_dev)), "half_index")
     return out
 
@@ -150,4 +175,5 @@ def get_half_index(cu_seqlens: torch.Tensor, *, front: bool) -> torch.Tensor:
 def half_indices(local_len: int, device) -> tuple:
     """(first_half_idx, second_half_idx) into a single local ``[2h]`` sequence."""
     cu = torch.tensor([0, local_len], dtype=torch.int32, device=device)
-    return get_half_index(cu, front=True), get_half_index(cu, front=False)
+    return (get_half_index(cu, front=True, total=local_len),
+            get_half_index(cu, front=False, total=local_len))

@@ -61,8 +61,13 @@ def test_golden_varlen_rows_and_half_index():
                               z[f"varlen_{name}_cp{cp}_r{r}_front"])
         assert np.array_equal(get_half_index(lcu, front=False).cpu().numpy(),
                               z[f"varlen_{name}_cp{cp}_r{r}_back"])
+        # with the packed length given, nothing is read back from the device
+        for front, tag in ((True, "front"), (False, "back")):
+            got = get_half_index(lcu, front=front, total=total // cp)
+            assert np.array_equal(got.cpu().numpy(), z[f"varlen_{name}_cp{cp}_r{r}_{tag}"])
         shards = [zigzag_shard_varlen(x, full_cu.tolist(), rr, cp)[0] for rr in range(cp)]
         assert torch.equal(zigzag_unshard_varlen(shards, full_cu.tolist(), cp), x)
+        assert torch.equal(zigzag_unshard_varlen(shards, torch.from_numpy(full_cu).cuda(), cp), x)
         checked += 1
     assert checked >= 10
     assert_device_ok()
