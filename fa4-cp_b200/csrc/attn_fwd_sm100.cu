@@ -1560,7 +1560,24 @@ extern "C" int fa4cp_ring_attn_fused(const void* q, const void* k, const void* v
   return ring_attn_fused_flags(q, k, v, slots_k, slots_v, slot_stride, out, lse, cu, nseq,
                                max_seqlen, total, num_heads_q, num_heads_kv, head_dim, dtype,
                                softmax_scale, q_descale, k_descales, v_descales, nranks, rank,
-                               arrived, arrived_base, 0, 1, stream);
+                               arrived, arrived_base, 0, 1, 0, 0, stream);
+}
+
+extern "C" int fa4cp_ring_attn_fused_remote(const void* q, const void* k, const void* v,
+                                            const void* slots_k, const void* slots_v,
+                                            int64_t slot_stride, void* out, float* lse,
+                                            const int32_t* cu, int32_t nseq, int32_t max_seqlen,
+                                            int64_t total, int32_t num_heads_q,
+                                            int32_t num_heads_kv, int32_t head_dim, int32_t dtype,
+                                            float softmax_scale, int32_t nranks, int32_t rank,
+                                            const uint32_t* arrived, uint32_t arrived_base,
+                                            void* stream) {
+  FA4CP_CHECK_ARG(dtype == FA4CP_DTYPE_BF16 || dtype == FA4CP_DTYPE_F16,
+                  "the remote-only ring walk takes f16 / bf16");
+  return ring_attn_fused_flags(q, k, v, slots_k, slots_v, slot_stride, out, lse, cu, nseq,
+                               max_seqlen, total, num_heads_q, num_heads_kv, head_dim, dtype,
+                               softmax_scale, nullptr, nullptr, nullptr, nranks, rank, arrived,
+                               arrived_base, 0, 1, 1, 1, stream);
 }
 
 int fa4cp::ring_attn_fused_flags(const void* q, const void* k, const void* v,
@@ -1571,8 +1588,13 @@ int fa4cp::ring_attn_fused_flags(const void* q, const void* k, const void* v,
                                  float softmax_scale, const float* q_descale,
                                  const float* k_descales, const float* v_descales, int32_t nranks,
                                  int32_t rank, const uint32_t* arrived, uint32_t arrived_base,
-                                 int32_t arrived_stride, int32_t arrived_step, void* stream) {
+                                 int32_t arrived_stride, int32_t arrived_step, int32_t first_step,
+                                 int32_t accumulate, void* stream) {
   FA4CP_CHECK_ARG(arrived_stride >= 0 && arrived_step >= 0, "bad arrival flag layout");
+  FA4CP_CHECK_ARG((first_step == 0 || first_step == 1) && (accumulate == 0 || accumulate == 1),
+                  "bad first_step / accumulate");
+  FA4CP_CHECK_ARG(first_step == 0 || dtype != FA4CP_DTYPE_E4M3,
+                  "the remote-only walk is for f16 / bf16");
   FA4CP_CHECK_ARG(nseq >= 1 && cu != nullptr, "cu_seqlens must describe >= 1 sequence");
   FA4CP_CHECK_ARG(nranks >= 1 && nranks <= 64 && rank >= 0 && rank < nranks,
                   "bad ring size %d / rank %d", nranks, rank);
@@ -1604,6 +1626,8 @@ int fa4cp::ring_attn_fused_flags(const void* q, const void* k, const void* v,
   p.arrived_base = arrived_base;
   p.arrived_stride = arrived_stride;
   p.arrived_step = arrived_step;
+  p.first_step = first_step;
+  p.accumulate = accumulate;
   p.nseq = nseq;
   p.Hq = num_heads_q;
   p.Hkv = num_heads_kv;

@@ -61,7 +61,8 @@ int ring_attn_fused_flags(const void* q, const void* k, const void* v, const voi
                           int32_t dtype, float softmax_scale, const float* q_descale,
                           const float* k_descales, const float* v_descales, int32_t nranks,
                           int32_t rank, const uint32_t* arrived, uint32_t arrived_base,
-                          int32_t arrived_stride, int32_t arrived_step, void* stream);
+                          int32_t arrived_stride, int32_t arrived_step, int32_t first_step,
+                          int32_t accumulate, void* stream);
 
 inline int elem_bytes(int dtype) {
   switch (dtype) {

@@ -832,14 +832,27 @@ extern "C" int fa4cp_ring_attn_fwd(int64_t handle, const void* q, const void* k,
   };
 
   // the persistent ring kernel: every step in one launch (f16 / bf16 D 64 or 128, e4m3 D 128)
+  // With direct pushes and f16 / bf16 operands the forward is two launches: step 0 (the local
+  // K/V, causal) on its own, then the ring kernel over the remote steps, merged into it.  Step
+  // 0 is 1/S of the rank's work and needs no transfer, so the remote walk starts only once the
+  // first pushes have landed: with one launch, the first wave of CTAs reaches the remote steps
+  // after its own short step-0 tiles and waits for slots still in flight.
   auto attn_fused = [&](const void* sk, const void* sv, int64_t stride, const uint32_t* arrived,
                         uint32_t base, int32_t flag_stride, int32_t flag_step) -> int {
     const bool timed = rc->t_used < int(rc->tev.size() / 2);
     if (timed) FA4CP_CHECK_CUDA(cudaEventRecord(rc->tev[2 * rc->t_used], st));
-    int r = ring_attn_fused_flags(q, k, v, sk, sv, stride, out, lse, cu, nseq, max_seqlen, total,
-                                  num_heads_q, num_heads_kv, head_dim, q_dtype, softmax_scale,
-                                  q_descale, k_descales, v_descales, S, rank, arrived, base,
-                                  flag_stride, flag_step, stream);
+    const bool two_pass = S > 1 && flag_stride == 1 && q_dtype != FA4CP_DTYPE_E4M3;
+    int r = FA4CP_OK;
+    if (two_pass)
+      r = fa4cp_attn_fwd(q, k, v, out, lse, cu, cu, nseq, max_seqlen, total, total, num_heads_q,
+                         num_heads_kv, head_dim, q_dtype, out_dtype, FA4CP_PATTERN_VARLEN, 1,
+                         softmax_scale, nullptr, nullptr, nullptr, 0, stream);
+    if (r == FA4CP_OK)
+      r = ring_attn_fused_flags(q, k, v, sk, sv, stride, out, lse, cu, nseq, max_seqlen, total,
+                                num_heads_q, num_heads_kv, head_dim, q_dtype, softmax_scale,
+                                q_descale, k_descales, v_descales, S, rank, arrived, base,
+                                flag_stride, flag_step, two_pass ? 1 : 0, two_pass ? 1 : 0,
+                                stream);
     if (r != FA4CP_OK) return r;
     if (timed) FA4CP_CHECK_CUDA(cudaEventRecord(rc->tev[2 * rc->t_used++ + 1], st));
     return FA4CP_OK;

@@ -32,6 +32,9 @@ struct RingFusedParams {
   const uint32_t* arrived;
   uint32_t arrived_base;
   int arrived_stride, arrived_step;
+  // one-tile kernel only: first_step 1 walks the remote steps alone (step 0 ran in a launch of
+  // its own, which wrote out / lse); accumulate 1 merges the result into out / lse
+  int first_step, accumulate;
   int nseq, Hq, Hkv, group, S, rank;
   int n_pairs;                // query-tile pairs per half, max over sequences
   int n_tiles;                // tiles of the schedule (ring_grid); the grid walks them
@@ -213,7 +216,10 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
   const RingSegs g = x.g;
   const int q_start = x.q_start, q0 = x.q0;
   const int rows_t[2] = {x.rows_t[0], x.rows_t[1]};
-  const int n_t[2] = {x.n_t[0], x.n_t[1]};
+  // remote-only walk (first_step 1): the tiles of step 0 are skipped; j counts the walked tiles
+  // (pipeline stages and phases), j + j0 is the tile in the CTA's K/V sequence
+  const int j0 = p.first_step ? g.n0 : 0;
+  const int n_t[2] = {x.n_t[0] > j0 ? x.n_t[0] - j0 : 0, x.n_t[1] > j0 ? x.n_t[1] - j0 : 0};
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TR::OFF_BAR);
   const uint32_t bar0 = smem_u32(bars);
@@ -284,9 +290,9 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
       cur.start(g, BN);
       int waited = 0;  // highest step whose slot is known present
       for (int j = 0; j < nmax; ++j) {
-        cur.seek(g, j, BN);
+        cur.seek(g, j + j0, BN);
         const int s = j % ST, ph = (j / ST) & 1;
-        const int row = g.a + (j - cur.first) * BN;
+        const int row = g.a + (j + j0 - cur.first) * BN;
         if (cur.s > waited) {
           if (p.arrived != nullptr &&
               !wait_arrived(p.arrived + (cur.s - 1) * p.arrived_stride,
@@ -440,7 +446,7 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
       cur.start(g, BN);
 
       for (int j = 0; j < nn; ++j) {
-        cur.seek(g, j, BN);
+        cur.seek(g, j + j0, BN);
         float fo = 1.0f;  // O factor when the V descale changes with the step
         if (cur.s != step) {
           step = cur.s;
@@ -459,7 +465,7 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
 #pragma unroll
         for (int c = 0; c < BN / 32; ++c) reg_fence32(sr[c]);
 
-        const int kbase = (j - cur.first) * BN;
+        const int kbase = (j + j0 - cur.first) * BN;
         const int seg_len = g.len(cur.s);
         const bool causal = cur.s == 0;
         const bool need_mask = (kbase + BN > seg_len) || (causal && kbase + BN - 1 > first + g.diag);
@@ -551,7 +557,26 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
         const bool valid = r < rows_t[t];
         const int64_t grow = int64_t(q_start) + first + r;
         const bool any_key = (m != kNegInf) && (l > 0.f);
-        const float inv_l = any_key ? vscale / l : 0.f;  // O is in units of the last V descale
+        const float lse_new = any_key ? (m + lg2_approx(l)) * kLn2 : kNegInf;
+        float* lse_ptr = p.lse + grow * p.Hq + w.head;
+        // out = acc * ca + O_raw * cb (O is in units of the last V descale)
+        float ca = 0.f, cb = any_key ? vscale / l : 0.f, lse_out = lse_new;
+        bool write = valid, read_acc = false;
+        if (valid && p.accumulate) {  // merge into the partial already in (out, lse)
+          const float acc_lse = *lse_ptr;
+          if (lse_new == kNegInf) {
+            write = false;
+          } else if (acc_lse != kNegInf) {
+            const float mm = fmaxf(acc_lse, lse_new);
+            const float wa = ex2_approx((acc_lse - mm) * kLog2e);
+            const float wb = ex2_approx((lse_new - mm) * kLog2e);
+            const float inv = 1.0f / (wa + wb);
+            ca = wa * inv;
+            cb *= wb * inv;
+            lse_out = mm + lg2_approx(wa + wb) * kLn2;
+            read_acc = true;
+          }
+        }
         uint8_t* orow = static_cast<uint8_t*>(p.out) + (grow * p.Hq + w.head) * int64_t(D) * 2;
 #pragma unroll 1
         for (int c = 0; c < D / 32; ++c) {
@@ -559,23 +584,43 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
           tmem_ld32(t_lane + uint32_t(TR::tm_o(t) + c * 32), o);
           tmem_wait_ld();
           reg_fence32(o);
-          if (valid) {
+          if (write) {
             uint4* dst = reinterpret_cast<uint4*>(orow + c * 64);
+            float f[32];
+#pragma unroll
+            for (int e = 0; e < 32; ++e) f[e] = __uint_as_float(o[e]) * cb;
+            if (read_acc) {
+#pragma unroll
+              for (int v4 = 0; v4 < 4; ++v4) {
+                const uint4 a = dst[v4];
+                const uint32_t wa4[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                  float lo, hi;
+                  if (p.out_bf16) {
+                    lo = __uint_as_float(wa4[i] << 16);
+                    hi = __uint_as_float(wa4[i] & 0xFFFF0000u);
+                  } else {
+                    const float2 tt = __half22float2(*reinterpret_cast<const __half2*>(&wa4[i]));
+                    lo = tt.x; hi = tt.y;
+                  }
+                  f[v4 * 8 + 2 * i] = fmaf(lo, ca, f[v4 * 8 + 2 * i]);
+                  f[v4 * 8 + 2 * i + 1] = fmaf(hi, ca, f[v4 * 8 + 2 * i + 1]);
+                }
+              }
+            }
 #pragma unroll
             for (int v4 = 0; v4 < 4; ++v4) {
               uint32_t wd[4];
 #pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                const float f0 = __uint_as_float(o[v4 * 8 + 2 * i]) * inv_l;
-                const float f1 = __uint_as_float(o[v4 * 8 + 2 * i + 1]) * inv_l;
-                wd[i] = p.out_bf16 ? pack_bf16x2(f0, f1) : pack_f16x2(f0, f1);
-              }
+              for (int i = 0; i < 4; ++i)
+                wd[i] = p.out_bf16 ? pack_bf16x2(f[v4 * 8 + 2 * i], f[v4 * 8 + 2 * i + 1])
+                                   : pack_f16x2(f[v4 * 8 + 2 * i], f[v4 * 8 + 2 * i + 1]);
               dst[v4] = make_uint4(wd[0], wd[1], wd[2], wd[3]);
             }
           }
         }
-        if (valid)
-          p.lse[grow * p.Hq + w.head] = any_key ? (m + lg2_approx(l)) * kLn2 : kNegInf;
+        if (write) *lse_ptr = lse_out;
       }
     }
   }

@@ -419,6 +419,22 @@ FA4CP_API int fa4cp_ring_attn_fused(const void* q, const void* k, const void* v,
                                     const float* v_descales, int32_t nranks, int32_t rank,
                                     const uint32_t* arrived, uint32_t arrived_base,
                                     void* stream);
+/*
+ * fa4cp_ring_attn_fused_remote: the same ring kernel over the remote steps 1 .. nranks-1 only,
+ * merged into the (out, lse) already there -- the partial of step 0, the local K/V, causal, as
+ * fa4cp_attn_fwd (VARLEN, causal) writes it.  f16 / bf16 only.  The executor's direct pushes run
+ * a forward this way (no counterpart in the reference, whose merge is a separate pass,
+ * fa4_ring/merge.py:45-64): the remote walk then starts once the first pushes have landed.
+ */
+FA4CP_API int fa4cp_ring_attn_fused_remote(const void* q, const void* k, const void* v,
+                                           const void* slots_k, const void* slots_v,
+                                           int64_t slot_stride, void* out, float* lse,
+                                           const int32_t* cu, int32_t nseq, int32_t max_seqlen,
+                                           int64_t total, int32_t num_heads_q,
+                                           int32_t num_heads_kv, int32_t head_dim, int32_t dtype,
+                                           float softmax_scale, int32_t nranks, int32_t rank,
+                                           const uint32_t* arrived, uint32_t arrived_base,
+                                           void* stream);
 
 FA4CP_API int fa4cp_ring_unique_id(uint8_t* id_out);
 FA4CP_API int fa4cp_ring_comm_init(const uint8_t* id, int32_t nranks, int32_t rank,

@@ -31,7 +31,7 @@ pytestmark = pytest.mark.gpu
 OUT_TOL, LSE_TOL = 2e-2, 1e-3
 
 
-def run_fused(cp, lens, H, Hkv, D, dtype, seed, counter=False, fp8=False):
+def run_fused(cp, lens, H, Hkv, D, dtype, seed, counter=False, fp8=False, two_pass=False):
     from fa4_ring import _lib
     from fa4_ring.zigzag import zigzag_shard_varlen
     lib = _lib.load()
@@ -85,12 +85,26 @@ def run_fused(cp, lens, H, Hkv, D, dtype, seed, counter=False, fp8=False):
         if counter:
             base = 1000
             ctr = torch.tensor([base + cp - 1], dtype=torch.int32, device="cuda")
-        rc = lib.fa4cp_ring_attn_fused(
-            qs[r].data_ptr(), ks[r].data_ptr(), vs[r].data_ptr(), slots_k.data_ptr(),
-            slots_v.data_ptr(), T * Hkv * D * elem, out.data_ptr(), lse.data_ptr(), lcu.data_ptr(),
-            len(lens), max_local, T, H, Hkv, D, _lib.dtype_code(dtype), scale,
-            _lib.ptr(qds[r]) if fp8 else None, _lib.ptr(kd), _lib.ptr(vd), cp, r,
-            None if ctr is None else ctypes.c_void_p(ctr.data_ptr()), base, stream)
+        if two_pass:
+            # step 0 (local K/V, causal) on its own, then the remote steps merged into it
+            rc = lib.fa4cp_attn_fwd(
+                qs[r].data_ptr(), ks[r].data_ptr(), vs[r].data_ptr(), out.data_ptr(),
+                lse.data_ptr(), lcu.data_ptr(), lcu.data_ptr(), len(lens), max_local, T, T, H, Hkv,
+                D, _lib.dtype_code(dtype), _lib.dtype_code(out_dt), _lib.PATTERN_VARLEN, 1, scale,
+                None, None, None, 0, stream)
+            assert rc == 0, _lib.last_error()
+            rc = lib.fa4cp_ring_attn_fused_remote(
+                qs[r].data_ptr(), ks[r].data_ptr(), vs[r].data_ptr(), slots_k.data_ptr(),
+                slots_v.data_ptr(), T * Hkv * D * elem, out.data_ptr(), lse.data_ptr(),
+                lcu.data_ptr(), len(lens), max_local, T, H, Hkv, D, _lib.dtype_code(dtype), scale,
+                cp, r, None if ctr is None else ctypes.c_void_p(ctr.data_ptr()), base, stream)
+        else:
+            rc = lib.fa4cp_ring_attn_fused(
+                qs[r].data_ptr(), ks[r].data_ptr(), vs[r].data_ptr(), slots_k.data_ptr(),
+                slots_v.data_ptr(), T * Hkv * D * elem, out.data_ptr(), lse.data_ptr(),
+                lcu.data_ptr(), len(lens), max_local, T, H, Hkv, D, _lib.dtype_code(dtype), scale,
+                _lib.ptr(qds[r]) if fp8 else None, _lib.ptr(kd), _lib.ptr(vd), cp, r,
+                None if ctr is None else ctypes.c_void_p(ctr.data_ptr()), base, stream)
         assert rc == 0, _lib.last_error()
         torch.cuda.synchronize()
         want_o, want_l = orc.ring_rank(q_np[r], k_np, v_np, r, cp, scale, lcu_list)
@@ -131,6 +145,19 @@ def test_ring_fused_matches_oracle(cp, lens, H, Hkv, D, dtype):
 ])
 def test_ring_fused_fp8_per_source_descales(cp, lens, H, Hkv):
     run_fused(cp, lens, H, Hkv, 128, torch.bfloat16, seed=100 + cp, fp8=True)
+
+
+@pytest.mark.parametrize("cp,lens,H,Hkv,D,dtype", [
+    (1, [512], 4, 2, 128, torch.bfloat16),                 # no remote step: step 0 alone
+    (2, [2 * 2 * 160], 4, 2, 128, torch.bfloat16),
+    (8, [2 * 8 * 256], 4, 1, 128, torch.bfloat16),
+    (3, [2 * 3 * 100], 4, 4, 64, torch.float16),
+    (4, [2 * 4 * n for n in (40, 3, 97, 64)], 4, 1, 128, torch.bfloat16),  # rows with no remote key
+])
+def test_ring_remote_walk_merged_into_step0(cp, lens, H, Hkv, D, dtype):
+    """The direct-push forward of f16 / bf16: step 0 by fa4cp_attn_fwd, then the ring kernel
+    over the remote steps only (fa4cp_ring_attn_fused_remote), merged in its epilogue."""
+    run_fused(cp, lens, H, Hkv, D, dtype, seed=40 + cp, two_pass=True)
 
 
 def test_ring_fused_counter_already_reached():
