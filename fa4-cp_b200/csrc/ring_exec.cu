@@ -291,7 +291,8 @@ void build_ce_plan(int S, int rank, uint64_t g0, bool fused, std::vector<RingOp>
 //     stream) or the ring kernel, which waits for each slot's flag itself;
 //   RECORD done; the release stream waits for it and sets FREED[s] := n at rank - s for
 //     every s (the source of the slot this rank read at step s);
-//   the compute stream joins the copy and release streams.
+//   the compute stream joins the copy streams (they read the caller's K/V); the releases run
+//     on in the background.
 // A push depends only on the call's start and on releases two calls back, and an attention
 // only on this call's pushes, so no wait can close a cycle even if every stream of every rank
 // ran in host order on one queue.
@@ -335,12 +336,13 @@ void build_ce_direct_plan(int S, int rank, uint64_t n, bool fused, std::vector<R
   op(ST_RELEASE, FA4CP_RING_OP_WAIT_EVENT, EV_DONE);
   for (int s = 1; s < S; ++s)
     op(ST_RELEASE, FA4CP_RING_OP_WRITE_PEER, S - s, FLAG_PEER_FREED0 + s, N);
+  // the caller's stream joins the copy streams, which read its K/V; the releases only write
+  // flags in the peers' memory and run on in the background (the next call's release follows
+  // them on the same stream, and a push waits for its destination's release itself)
   op(ST_COPY_K, FA4CP_RING_OP_RECORD, EV_COPY_END);
   if (S > 2) op(ST_COPY_K2, FA4CP_RING_OP_RECORD, EV_COPY_END2);
-  op(ST_RELEASE, FA4CP_RING_OP_RECORD, EV_REL_END);
   op(ST_COMPUTE, FA4CP_RING_OP_WAIT_EVENT, EV_COPY_END);
   if (S > 2) op(ST_COMPUTE, FA4CP_RING_OP_WAIT_EVENT, EV_COPY_END2);
-  op(ST_COMPUTE, FA4CP_RING_OP_WAIT_EVENT, EV_REL_END);
 }
 
 using StreamWaitValue32Fn = CUresult (*)(CUstream, CUdeviceptr, cuuint32_t, unsigned int);
