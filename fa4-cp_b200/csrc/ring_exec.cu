@@ -834,16 +834,18 @@ extern "C" int fa4cp_ring_attn_fwd(int64_t handle, const void* q, const void* k,
   };
 
   // the persistent ring kernel: every step in one launch (f16 / bf16 D 64 or 128, e4m3 D 128)
-  // With direct pushes and f16 / bf16 operands the forward is two launches: step 0 (the local
-  // K/V, causal) on its own, then the ring kernel over the remote steps, merged into it.  Step
-  // 0 is 1/S of the rank's work and needs no transfer, so the remote walk starts only once the
-  // first pushes have landed: with one launch, the first wave of CTAs reaches the remote steps
-  // after its own short step-0 tiles and waits for slots still in flight.
+  // With direct pushes, f16 / bf16 operands and S >= 8 the forward is two launches: step 0
+  // (the local K/V, causal) on its own, then the ring kernel over the remote steps, merged into
+  // it.  Step 0 is 1/S of the rank's work and needs no transfer, so the remote walk starts only
+  // once the first pushes have landed: with one launch, the first wave of CTAs reaches the
+  // remote steps after its own short step-0 tiles and waits for slots still in flight.  With
+  // fewer ranks step 0 is a large share of the work and the second launch's tail and merge
+  // cost more than they hide (cfg2 at cp=2: 2064 against 2240-2316 TF/s in one launch).
   auto attn_fused = [&](const void* sk, const void* sv, int64_t stride, const uint32_t* arrived,
                         uint32_t base, int32_t flag_stride, int32_t flag_step) -> int {
     const bool timed = rc->t_used < int(rc->tev.size() / 2);
     if (timed) FA4CP_CHECK_CUDA(cudaEventRecord(rc->tev[2 * rc->t_used], st));
-    const bool two_pass = S > 1 && flag_stride == 1 && q_dtype != FA4CP_DTYPE_E4M3;
+    const bool two_pass = S >= 8 && flag_stride == 1 && q_dtype != FA4CP_DTYPE_E4M3;
     int r = FA4CP_OK;
     if (two_pass)
       r = fa4cp_attn_fwd(q, k, v, out, lse, cu, cu, nseq, max_seqlen, total, total, num_heads_q,

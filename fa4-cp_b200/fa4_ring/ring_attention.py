@@ -232,8 +232,8 @@ def _native_forward(q, k, v, cfg: RingConfig, group, *, cu, nseq, max_seqlen,
              and ((q.dtype in (torch.float16, torch.bfloat16) and D in (64, 128))
                   or (RING_FUSED is True and q.dtype == torch.float8_e4m3fn and D == 128)))
     # the ring kernel: e4m3 runs a main pass and a split pass (rows that see few keys); with
-    # direct pushes f16 / bf16 run step 0 in a launch of its own before the remote walk
-    two_pass = q.dtype == torch.float8_e4m3fn or ring.transport == "copy_engine"
+    # direct pushes and S >= 8 f16 / bf16 run step 0 in a launch of its own before the remote walk
+    two_pass = q.dtype == torch.float8_e4m3fn or (ring.transport == "copy_engine" and S >= 8)
     _lib.count_launches((2 if two_pass else 1) if fused else S * (3 if ws is not None else 1))
     return out, lse
 
