@@ -871,6 +871,57 @@ def hbm_kernels(dev, iters=10):
             "shape": f"T={T}, Hq={H}, D={D}, bf16 out, fp32 LSE; zig-zag over 131072 rows"}
 
 
+# --------------------------------------------------------------------------- library comparison
+def library_compare(dev, lens=(32768, 8192), iters=10):
+    """This repo's attention kernel beside a library tcgen05 kernel on the same inputs:
+    flashinfer's CUTLASS SM100 FMHA (``flashinfer.prefill.fmha_varlen``; the reference's GPU
+    kernel, FA4's ``flash_attn.cute``, is not installed in this image).  Causal bf16, Hq=32,
+    Hkv=8, D=128 (cfg2's heads), one sequence of each length; best of ``iters`` with the L2
+    flushed before each launch, CUDA events.  flashinfer builds the module on first use
+    (minutes; FLASHINFER_WORKSPACE_BASE selects its cache).  Comparison only: nothing here is
+    on the product path."""
+    try:
+        from flashinfer.prefill import fmha_varlen
+    except Exception as e:  # the library is missing or cannot load: say so
+        return {"unavailable": f"flashinfer fmha_varlen: {type(e).__name__}: {e}"}
+    from fa4_ring.attn_backend import b200_attn
+    Hq, Hkv, D = 32, 8, 128
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    res = {}
+    for N in lens:
+        g = torch.Generator(device=dev).manual_seed(0)
+        q = torch.randn(N, Hq, D, device=dev, generator=g, dtype=torch.bfloat16)
+        k = torch.randn(N, Hkv, D, device=dev, generator=g, dtype=torch.bfloat16)
+        v = torch.randn(N, Hkv, D, device=dev, generator=g, dtype=torch.bfloat16)
+        cu = torch.tensor([0, N], dtype=torch.int32, device=dev)
+        sc = 1.0 / math.sqrt(D)
+        fns = {"flashinfer_cutlass_sm100_fmha": lambda: fmha_varlen(q, k, v, cu, cu, causal=True,
+                                                                    sm_scale=sc, max_qo_len=N),
+               "fa4cp_attn_fwd_2q_kernel": lambda: b200_attn(q, k, v, causal=True,
+                                                             softmax_scale=sc)[0]}
+        outs, row = {}, {}
+        for name, fn in fns.items():
+            for _ in range(3):
+                o = fn()
+            torch.cuda.synchronize()
+            best = float("inf")
+            for _ in range(iters):
+                flush.zero_()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                o = fn()
+                e1.record()
+                torch.cuda.synchronize()
+                best = min(best, e0.elapsed_time(e1))
+            outs[name] = o[0] if isinstance(o, tuple) else o
+            row[name] = {"ms": round(best, 4),
+                         "tflops": round(causal_flops(N, Hq, D) / (best * 1e-3) / 1e12, 1)}
+        a, b = outs.values()
+        row["max_abs_diff"] = float((a.float() - b.float()).abs().max())
+        res[f"N={N}"] = row
+    return res
+
+
 # --------------------------------------------------------------------------- reference arm
 def reference_main(args):
     """The reference's CPU ring simulation (restated in numpy, ``oracle/``) on the host
@@ -927,6 +978,9 @@ def main():
     ap.add_argument("--timeline", action="store_true",
                     help="with --quick: print each rank's launch/hop timeline of the last "
                          "forward to stderr")
+    ap.add_argument("--library-compare", action="store_true",
+                    help="only time flashinfer's CUTLASS SM100 FMHA beside this repo's attention "
+                         "kernel on the same causal bf16 inputs (comparison, not a bench line)")
     ap.add_argument("--aux", action="store_true",
                     help="only the HBM-bound kernels (merges, zig-zag) against the HBM peak")
     ap.add_argument("--bwd", action="store_true",
@@ -946,6 +1000,11 @@ def main():
         return 0
 
     torch.cuda.set_device(local_rank)
+    if args.library_compare:
+        if rank == 0:
+            print(json.dumps({"library_compare": library_compare(torch.device("cuda", local_rank))}),
+                  flush=True)
+        return 0
     if args.aux:
         if rank == 0:
             print(json.dumps({"aux": True, "hbm_kernels": hbm_kernels(torch.device("cuda", local_rank))}),
