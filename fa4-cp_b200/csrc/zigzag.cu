@@ -7,7 +7,8 @@
 //
 // All kernels are pure byte movement (HBM-bound): one output row per loop trip,
 // copied with the widest vector (16/8/4/2/1 bytes) that the row size and the
-// pointers allow, grid sized to a multiple of the SM count.
+// pointers allow, four vectors per thread in flight, grid sized to a multiple of the SM
+// count.
 #include "common.cuh"
 
 namespace fa4cp {
@@ -15,14 +16,31 @@ namespace {
 
 constexpr int kThreads = 256;
 
+// One row: each thread loads up to kUnroll vectors before it stores any, so that enough
+// bytes are in flight per SM to cover HBM latency (a load-then-store loop keeps one vector per
+// thread in flight: 78% of the copy bandwidth measured on 8 KB rows).
+constexpr int kUnroll = 4;
+
 template <typename V>
 struct Copier {
   __device__ __forceinline__ static void row(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst,
                                              int64_t row_bytes) {
-    const V* s = reinterpret_cast<const V*>(src);
-    V* d = reinterpret_cast<V*>(dst);
+    const V* __restrict__ s = reinterpret_cast<const V*>(src);
+    V* __restrict__ d = reinterpret_cast<V*>(dst);
     const int64_t n = row_bytes / int64_t(sizeof(V));
-    for (int64_t i = threadIdx.x; i < n; i += blockDim.x) d[i] = s[i];
+    for (int64_t i0 = threadIdx.x; i0 < n; i0 += int64_t(kUnroll) * blockDim.x) {
+      V v[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int64_t i = i0 + int64_t(u) * blockDim.x;
+        if (i < n) v[u] = s[i];
+      }
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int64_t i = i0 + int64_t(u) * blockDim.x;
+        if (i < n) d[i] = v[u];
+      }
+    }
   }
 };
 
