@@ -107,8 +107,13 @@ struct Geometry {
 // kQtileChunk, heaviest (latest, under causal masking) chunk first; inside a chunk all
 // CTAs of one kv head run before the next kv head's, q-tile major, q head minor.  The
 // CTAs resident at any time then read the K/V of only a few kv heads, which stay in L2
-// instead of every kv head's K/V streaming through it.
-constexpr int kQtileChunk = 16;
+// instead of every kv head's K/V streaming through it.  Each chunk reads the K/V of every
+// kv head once more (a kv head's CTAs of the next chunk start after all other kv heads' K/V
+// went through L2), so the chunk sets the K/V re-reads: measured on the two-tile kernel,
+// causal bf16 N=32768 Hq=32 Hkv=8 D=128, DRAM traffic 1.67x the algorithmic bytes with
+// chunks of 16 pairs, 1.22x with 32, 1.05x with 64, 0.97x with one chunk, at equal kernel
+// time; a single chunk slowed the persistent e4m3 kernel by 3% (its heavy-first balance).
+constexpr int kQtileChunk = 64;
 
 __device__ __forceinline__ bool cta_tile(const Params& p, int& head, int& qtile) {
   const int ch = min(kQtileChunk, p.n_qtiles);
