@@ -506,6 +506,8 @@ def gpu_main(args, rank, world, local_rank):
                    "seq_len": N, "num_seqs": len(lens), "num_heads_q": Hq, "num_heads_kv": Hkv,
                    "head_dim": D,
                    "cp": cp, "merge_mode": args.merge, "parallelism": f"cp{cp} zig-zag ring",
+                   "transport": args.transport if world > 1 else None,
+                   "ring_kernel": args.ring_kernel if world > 1 else None,
                    "l2": "flushed before every timed step (256 MiB write, untimed)"},
         "per_gpu_tflops": round(value / world, 2),
         "pct_tensor_peak": round(value / world / peak * 100.0, 2),
@@ -603,6 +605,24 @@ def local_schedule_ms(lq, lk, lv, cfg, desc, lcu, nseq, max_local, fused, flush,
                 slots_k[0].numel(), out.data_ptr(), lse.data_ptr(), lcu.data_ptr(), nseq, max_local,
                 T, Hq, Hkv, D, _lib.dtype_code(lq.dtype), scale, _lib.ptr(qd), _lib.ptr(kds),
                 _lib.ptr(vds), S, rank, None, 0, st), "ring_attn_fused")
+        if kv8 and lq.dtype == torch.bfloat16:
+            # bf16 q x e4m3 K/V: as the executor runs it, this rank converts its K/V to their
+            # exact bf16 images (timed) and every slot already holds a peer's bf16 images
+            slots_k = torch.stack([ks[(rank - i - 1) % S].to(torch.bfloat16) for i in range(S - 1)])
+            slots_v = torch.stack([vs[(rank - i - 1) % S].to(torch.bfloat16) for i in range(S - 1)])
+            kb = torch.empty(lk.shape, dtype=torch.bfloat16, device=lq.device)
+            vb = torch.empty_like(kb)
+
+            def one():
+                for x8, xb in ((lk, kb), (lv, vb)):
+                    _lib.check(lib.fa4cp_dequant_e4m3(x8.data_ptr(), None, xb.data_ptr(), T, Hkv,
+                                                      D, st), "dequant_e4m3")
+                _lib.check(lib.fa4cp_ring_attn_fused_mixed(
+                    lq.data_ptr(), kb.data_ptr(), vb.data_ptr(), slots_k.data_ptr(),
+                    slots_v.data_ptr(), slots_k[0].numel() * slots_k.element_size(),
+                    out.data_ptr(), lse.data_ptr(), lcu.data_ptr(), nseq, max_local, T, Hq, Hkv, D,
+                    scale, _lib.ptr(kds), _lib.ptr(vds), S, rank, None, 0, st),
+                    "ring_attn_fused_mixed")
     else:
         def one():
             ring_forward(lq, lambda s: (ks[(rank - s) % S], vs[(rank - s) % S]), lambda s: None,
@@ -969,9 +989,11 @@ def main():
                     help="K/V transport of the native ring executor (N > 1): direct pushes to "
                          "every peer (copy_engine), the chained rotation on the copy engines, "
                          "or NCCL send/recv")
-    ap.add_argument("--ring-kernel", choices=["fused", "fused-16bit", "steps"], default="fused",
+    ap.add_argument("--ring-kernel", choices=["fused", "fused-16bit", "fused-all", "steps"],
+                    default="fused",
                     help="copy-engine ring: one ring-kernel launch per forward (fused; "
-                         "fused-16bit: not for e4m3) or one attention launch per step")
+                         "fused-16bit: not for e4m3; fused-all: also head_dim 256, cfg5) or one "
+                         "attention launch per step")
     ap.add_argument("--sm-reserve", type=int, default=None,
                     help="SMs the persistent attention grid leaves to NCCL during a ring call "
                          "(native executor; default: the library's)")
@@ -1017,7 +1039,8 @@ def main():
                                 pg_options=nccl_pg_options(args.nccl_cta_policy))
     from fa4_ring import ring_attention
     ring_attention.RING_TRANSPORT = args.transport
-    ring_attention.RING_FUSED = {"fused": True, "fused-16bit": "16bit", "steps": False}[args.ring_kernel]
+    ring_attention.RING_FUSED = {"fused": True, "fused-16bit": "16bit", "fused-all": "all",
+                                 "steps": False}[args.ring_kernel]
     try:
         line = (bwd_main if args.bwd else gpu_main)(args, rank, world, local_rank)
     finally:

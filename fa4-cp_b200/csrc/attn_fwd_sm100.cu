@@ -1465,6 +1465,37 @@ int launch_ring_fused(const void* q, const void* k, const void* v, const void* s
   return FA4CP_OK;
 }
 
+// The one-query-tile ring kernel (head_dim 256): one CTA per 128-row query tile of a half.
+template <class TR>
+int launch_ring_fused_1q(const void* q, const void* k, const void* v, const void* slots_k,
+                         const void* slots_v, int64_t slot_stride, int64_t total, int max_seqlen,
+                         const RingFusedParams& p0, cudaStream_t stream) {
+  static std::atomic<uint64_t> optin{0};
+  if (int rc0 = smem_optin(ring_fused_1q_kernel<TR>, TR::SMEM_BYTES, optin)) return rc0;
+  RingFusedParams p = p0;
+  p.n_pairs = (max_seqlen / 2 + BM - 1) / BM;  // query tiles per half
+  if (p.n_pairs <= 0 || total <= 0) return FA4CP_OK;
+  FA4CP_CHECK_ARG(int64_t(2) * ((p.n_pairs + kQtileChunk - 1) / kQtileChunk + 1) * kQtileChunk * p.Hq * p.nseq <
+                      (int64_t(1) << 31), "too many tiles");
+  p.n_tiles = int(ring_grid(p.n_pairs, p.Hq, p.nseq));
+  CUtensorMap mq, mk0, mv0, mks, mvs;
+  int rc;
+  if ((rc = make_map(&mq, q, total, p.Hq, TR::D, TR::ELEM, BM))) return rc;
+  if ((rc = make_map(&mk0, k, total, p.Hkv, TR::D, TR::ELEM, TR::BN))) return rc;
+  if ((rc = make_map(&mv0, v, total, p.Hkv, TR::D, TR::ELEM, TR::BN))) return rc;
+  if (p.S > 1) {
+    if ((rc = make_map4(&mks, slots_k, total, p.Hkv, TR::D, TR::ELEM, TR::BN, p.S - 1, slot_stride)))
+      return rc;
+    if ((rc = make_map4(&mvs, slots_v, total, p.Hkv, TR::D, TR::ELEM, TR::BN, p.S - 1, slot_stride)))
+      return rc;
+  } else {
+    mks = mk0;  // no step reads a slot
+    mvs = mv0;
+  }
+  ring_fused_1q_kernel<TR><<<p.n_tiles, kThreads, TR::SMEM_BYTES, stream>>>(mq, mk0, mv0, mks, mvs, p);
+  return check_launch("ring_fused_1q");
+}
+
 }  // namespace
 }  // namespace fa4cp
 
@@ -1562,10 +1593,30 @@ extern "C" int fa4cp_ring_attn_fused(const void* q, const void* k, const void* v
                                      const float* v_descales, int32_t nranks, int32_t rank,
                                      const uint32_t* arrived, uint32_t arrived_base,
                                      void* stream) {
+  FA4CP_CHECK_ARG(dtype == FA4CP_DTYPE_E4M3 || (!q_descale && !k_descales && !v_descales),
+                  "descales apply to e4m3 inputs only");
   return ring_attn_fused_flags(q, k, v, slots_k, slots_v, slot_stride, out, lse, cu, nseq,
                                max_seqlen, total, num_heads_q, num_heads_kv, head_dim, dtype,
                                softmax_scale, q_descale, k_descales, v_descales, nranks, rank,
                                arrived, arrived_base, 0, 1, 0, 0, stream);
+}
+
+extern "C" int fa4cp_ring_attn_fused_mixed(const void* q, const void* k, const void* v,
+                                           const void* slots_k, const void* slots_v,
+                                           int64_t slot_stride, void* out, float* lse,
+                                           const int32_t* cu, int32_t nseq, int32_t max_seqlen,
+                                           int64_t total, int32_t num_heads_q,
+                                           int32_t num_heads_kv, int32_t head_dim,
+                                           float softmax_scale, const float* k_descales,
+                                           const float* v_descales, int32_t nranks, int32_t rank,
+                                           const uint32_t* arrived, uint32_t arrived_base,
+                                           void* stream) {
+  FA4CP_CHECK_ARG(head_dim == 256, "the bf16 x e4m3-K/V ring kernel takes head_dim 256 (got %d)",
+                  head_dim);
+  return ring_attn_fused_flags(q, k, v, slots_k, slots_v, slot_stride, out, lse, cu, nseq,
+                               max_seqlen, total, num_heads_q, num_heads_kv, head_dim,
+                               FA4CP_DTYPE_BF16, softmax_scale, nullptr, k_descales, v_descales,
+                               nranks, rank, arrived, arrived_base, 0, 1, 0, 0, stream);
 }
 
 extern "C" int fa4cp_ring_attn_fused_remote(const void* q, const void* k, const void* v,
@@ -1609,12 +1660,15 @@ int fa4cp::ring_attn_fused_flags(const void* q, const void* k, const void* v,
   FA4CP_CHECK_ARG(softmax_scale > 0.f, "softmax_scale must be positive");
   const bool fp8 = dtype == FA4CP_DTYPE_E4M3;
   if (dtype != FA4CP_DTYPE_BF16 && dtype != FA4CP_DTYPE_F16 && !(fp8 && head_dim == 128)) {
-    set_last_error("the ring kernel takes f16 / bf16 (D 64, 128) or e4m3 (D 128); got dtype %d, D %d",
+    set_last_error("the ring kernel takes f16 / bf16 (D 64, 128, 256) or e4m3 (D 128); got dtype %d, D %d",
                    dtype, head_dim);
     return FA4CP_ERR_UNSUPPORTED;
   }
-  FA4CP_CHECK_ARG(fp8 || (!q_descale && !k_descales && !v_descales),
-                  "descales apply to e4m3 inputs only");
+  // f16 / bf16 with descales: K/V are exact images of e4m3 values (the head_dim 256 kernel)
+  FA4CP_CHECK_ARG(fp8 || head_dim == 256 || (!q_descale && !k_descales && !v_descales),
+                  "descales apply to e4m3 inputs (or e4m3 K/V images at head_dim 256) only");
+  FA4CP_CHECK_ARG(head_dim != 256 || (first_step == 0 && accumulate == 0),
+                  "the head_dim 256 ring kernel walks every step in one launch");
   if (total == 0) return FA4CP_OK;
   FA4CP_CHECK_ARG(q && k && v && out && lse, "null tensor pointer");
   FA4CP_CHECK_ARG(nranks == 1 || (slots_k && slots_v), "slots are required for nranks > 1");
@@ -1656,7 +1710,10 @@ int fa4cp::ring_attn_fused_flags(const void* q, const void* k, const void* v,
   if (head_dim == 64)
     return launch_ring_fused<Traits2<64, 128, 3, false>>(q, k, v, slots_k, slots_v, slot_stride,
                                                          total, max_seqlen, p, st);
-  set_last_error("the ring kernel takes head_dim 64 or 128 (got %d)", head_dim);
+  if (head_dim == 256)
+    return launch_ring_fused_1q<Traits<256, 64, 2, false>>(q, k, v, slots_k, slots_v,
+                                                           slot_stride, total, max_seqlen, p, st);
+  set_last_error("the ring kernel takes head_dim 64, 128 or 256 (got %d)", head_dim);
   return FA4CP_ERR_UNSUPPORTED;
 }
 

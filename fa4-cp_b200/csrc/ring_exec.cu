@@ -91,7 +91,9 @@ struct RingComm {
   cudaEvent_t ev_hop[kMaxRing] = {};   // hop s landed
   cudaEvent_t ev_step[kMaxRing] = {};  // attention of step s done (its K/V slot is free)
   int sm_reserve = kDefaultSmReserve;  // SMs the persistent attention grid leaves to NCCL
-  int fused = 2;  // ring kernel: 0 never, 1 for f16 / bf16 only, 2 also for e4m3 (default)
+  // ring kernel: 0 never, 1 for f16 / bf16 (D 64, 128), 2 also for e4m3 (default), 3 also at
+  // head_dim 256 (f16 / bf16, and bf16 q x e4m3 K/V)
+  int fused = 2;
   // optional timing: 2 timing events per attention launch and per hop, filled in call order
   std::vector<cudaEvent_t> tev, hev;
   int t_used = 0, h_used = 0;
@@ -607,7 +609,7 @@ extern "C" int fa4cp_ring_timing(int64_t handle, int32_t max_launches) {
 
 extern "C" int fa4cp_ring_set_fused(int64_t handle, int32_t fused) {
   FA4CP_CHECK_ARG(handle != 0, "null ring handle");
-  FA4CP_CHECK_ARG(fused >= 0 && fused <= 2, "fused mode %d not in 0..2", fused);
+  FA4CP_CHECK_ARG(fused >= 0 && fused <= 3, "fused mode %d not in 0..3", fused);
   RingComm* rc = ring_of(handle);
   FA4CP_CHECK_ARG(rc != nullptr, "unknown ring handle");
   rc->fused = fused;
@@ -841,35 +843,61 @@ extern "C" int fa4cp_ring_attn_fwd(int64_t handle, const void* q, const void* k,
   // remote steps after its own short step-0 tiles and waits for slots still in flight.  With
   // fewer ranks step 0 is a large share of the work and the second launch's tail and merge
   // cost more than they hide (cfg2 at cp=2: 2064 against 2240-2316 TF/s in one launch).
+  // bf16 q x e4m3 K/V at head_dim 256 (the ring kernel fa4cp_ring_attn_fused_mixed): the rank
+  // converts its K/V to bf16 once (exact: e4m3 values are bf16 values) into the workspace,
+  // pushes those images and the kernel applies the per-source descales.  The pushes carry twice
+  // the e4m3 bytes; at the shapes this serves (cfg5: 64 MB per rank against a forward of tens of
+  // ms) they stay hidden behind step 0.
+  const bool mixed_fused = mixed && rc->fused >= 3 && head_dim == 256;
+  const void* k_loc = k;
+  const void* v_loc = v;
+  int64_t push_bytes = kv_bytes;
+  const int32_t fused_dtype = mixed ? FA4CP_DTYPE_BF16 : q_dtype;
   auto attn_fused = [&](const void* sk, const void* sv, int64_t stride, const uint32_t* arrived,
                         uint32_t base, int32_t flag_stride, int32_t flag_step) -> int {
     const bool timed = rc->t_used < int(rc->tev.size() / 2);
     if (timed) FA4CP_CHECK_CUDA(cudaEventRecord(rc->tev[2 * rc->t_used], st));
-    const bool two_pass = S >= 8 && flag_stride == 1 && q_dtype != FA4CP_DTYPE_E4M3;
+    const bool two_pass = S >= 8 && flag_stride == 1 && q_dtype != FA4CP_DTYPE_E4M3 &&
+                          head_dim != 256;
     int r = FA4CP_OK;
     if (two_pass)
       r = fa4cp_attn_fwd(q, k, v, out, lse, cu, cu, nseq, max_seqlen, total, total, num_heads_q,
                          num_heads_kv, head_dim, q_dtype, out_dtype, FA4CP_PATTERN_VARLEN, 1,
                          softmax_scale, nullptr, nullptr, nullptr, 0, stream);
     if (r == FA4CP_OK)
-      r = ring_attn_fused_flags(q, k, v, sk, sv, stride, out, lse, cu, nseq, max_seqlen, total,
-                                num_heads_q, num_heads_kv, head_dim, q_dtype, softmax_scale,
-                                q_descale, k_descales, v_descales, S, rank, arrived, base,
-                                flag_stride, flag_step, two_pass ? 1 : 0, two_pass ? 1 : 0,
+      r = ring_attn_fused_flags(q, k_loc, v_loc, sk, sv, stride, out, lse, cu, nseq, max_seqlen,
+                                total, num_heads_q, num_heads_kv, head_dim, fused_dtype,
+                                softmax_scale, q_descale, k_descales, v_descales, S, rank, arrived,
+                                base, flag_stride, flag_step, two_pass ? 1 : 0, two_pass ? 1 : 0,
                                 stream);
     if (r != FA4CP_OK) return r;
     if (timed) FA4CP_CHECK_CUDA(cudaEventRecord(rc->tev[2 * rc->t_used++ + 1], st));
     return FA4CP_OK;
   };
   const bool fusable =
-      q_dtype == kv_dtype &&
-      ((rc->fused >= 1 && (q_dtype == FA4CP_DTYPE_BF16 || q_dtype == FA4CP_DTYPE_F16) &&
-        (head_dim == 64 || head_dim == 128)) ||
-       (rc->fused >= 2 && q_dtype == FA4CP_DTYPE_E4M3 && head_dim == 128));
+      mixed_fused ||
+      (q_dtype == kv_dtype &&
+       ((rc->fused >= 1 && (q_dtype == FA4CP_DTYPE_BF16 || q_dtype == FA4CP_DTYPE_F16) &&
+         (head_dim == 64 || head_dim == 128 || (head_dim == 256 && rc->fused >= 3))) ||
+        (rc->fused >= 2 && q_dtype == FA4CP_DTYPE_E4M3 && head_dim == 128)));
+  if (mixed_fused && (S == 1 || rc->ce)) {
+    push_bytes = total * num_heads_kv * int64_t(head_dim) * 2;
+    FA4CP_CHECK_ARG(workspace != nullptr && workspace_bytes >= 2 * push_bytes &&
+                        uintptr_t(workspace) % 16 == 0,
+                    "bf16 x e4m3 K/V: the workspace must hold the bf16 K and V (%lld bytes, "
+                    "16-byte aligned)", static_cast<long long>(2 * push_bytes));
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    int r = launch_dequant_e4m3(k, nullptr, ws, total, num_heads_kv, head_dim, st);
+    if (r == FA4CP_OK)
+      r = launch_dequant_e4m3(v, nullptr, ws + push_bytes, total, num_heads_kv, head_dim, st);
+    if (r != FA4CP_OK) return r;
+    k_loc = ws;
+    v_loc = ws + push_bytes;
+  }
   if (S == 1)
     return fusable ? attn_fused(nullptr, nullptr, 0, nullptr, 0, 0, 1) : attn_step(0, k, v);
   if (rc->ce)
-    return run_ce(rc, attn_step, fusable ? &attn_fused : nullptr, k, v, kv_bytes, st);
+    return run_ce(rc, attn_step, fusable ? &attn_fused : nullptr, k_loc, v_loc, push_bytes, st);
 
   // ---- NCCL transport
   FA4CP_CHECK_ARG(kv_bufs != nullptr && kv_bufs_bytes >= 4 * kv_bytes,

@@ -631,6 +631,373 @@ __global__ void __launch_bounds__(TR::THREADS, 1)
   if (warp == 9) tmem_dealloc(tmem, TR::TM_COLS);
 }
 
+// ---------------------------------------------------------------------------
+// One query tile per CTA (head_dim 256): S (64 keys) x 2 + O (256) fill 384 TMEM columns, so a
+// CTA holds a single 128-row query tile, with the per-step single-tile kernel's roles (warps
+// 0-3 softmax + epilogue, warp 4 TMA, warp 5 MMA) and the ring walk above.  ring_tile's
+// "pair" is a 128-row query tile here (RingFusedParams::n_pairs counts query tiles per half).
+// f16 / bf16 operands; descales (per source rank, as the e4m3 kernel) are for K/V that are
+// the exact f16 / bf16 images of e4m3 values: the score scale of a step is
+// scale * q_descale * k_descale[src], and O is kept in units of the current step's V descale
+// (rescaled by old / new on entering a step, the epilogue multiplies by the last one).
+// Reference: the bf16-Q x e4m3-K/V ring of fa4_ring/ring_attention.py:139-166 with the
+// descales of fa4_ring/fa4_backend.py:99-120.
+struct RingTileGeo1 {
+  RingTile w;
+  RingSegs g;
+  int q_start, q0, rows, n;
+};
+
+__device__ __forceinline__ bool ring_tile_geo1(const RingFusedParams& p, int tile, int BN,
+                                               RingTileGeo1& x) {
+  if (!ring_tile(p, tile, x.w)) return false;  // padding of the schedule
+  x.g.a = p.cu[x.w.seq];
+  const int L = p.cu[x.w.seq + 1] - x.g.a;
+  x.g.hh = L / 2;
+  x.g.half = x.w.half;
+  x.g.S = p.S;
+  x.g.rank = p.rank;
+  x.q_start = x.g.a + x.w.half * x.g.hh;
+  const int q_len = x.w.half ? L - x.g.hh : x.g.hh;
+  x.q0 = x.w.pair * BM;
+  if (x.q0 >= q_len) return false;  // past this sequence's half
+  x.rows = min(BM, q_len - x.q0);
+  x.g.k0_len = x.w.half ? L : x.g.hh;
+  x.g.diag = x.g.k0_len - q_len;
+  const int kv_end0 = min(x.g.k0_len, x.q0 + x.rows + x.g.diag);  // >= 1
+  x.g.n0 = (kv_end0 + BN - 1) / BN;
+  int n = 0;
+  for (int s = 0; s < p.S; ++s) n += x.g.tiles(s, BN);
+  x.n = n;
+  return true;
+}
+
+template <class TR>
+__global__ void __launch_bounds__(kThreads, 1)
+    ring_fused_1q_kernel(const __grid_constant__ CUtensorMap tmQ,
+                         const __grid_constant__ CUtensorMap tmK0,
+                         const __grid_constant__ CUtensorMap tmV0,
+                         const __grid_constant__ CUtensorMap tmKs,
+                         const __grid_constant__ CUtensorMap tmVs, const RingFusedParams p) {
+  static_assert(!TR::FP8, "the one-query-tile ring kernel takes f16 / bf16 operands");
+  constexpr int D = TR::D, BN = TR::BN, ST = TR::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  RingTileGeo1 x;
+  if (!ring_tile_geo1(p, int(blockIdx.x), BN, x)) return;  // uniform, before any set-up
+  const RingTile w = x.w;
+  const RingSegs g = x.g;
+  const int q0 = x.q0, rows = x.rows, n_kv = x.n;
+
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TR::OFF_BAR);
+  const uint32_t bar0 = smem_u32(bars);
+  auto BAR = [&](int i) -> uint32_t { return bar0 + 8u * uint32_t(i); };
+  const uint32_t q_full = BAR(0);
+  auto k_full = [&](int s) { return BAR(1 + s); };
+  auto k_empty = [&](int s) { return BAR(1 + ST + s); };
+  auto v_full = [&](int s) { return BAR(1 + 2 * ST + s); };
+  auto v_empty = [&](int s) { return BAR(1 + 3 * ST + s); };
+  auto s_full = [&](int b) { return BAR(1 + 4 * ST + b); };
+  auto p_full = [&](int b) { return BAR(3 + 4 * ST + b); };
+  // PV_i commits o_done(i & 1), as in the per-step single-tile kernel
+  auto o_done = [&](int b) { return BAR(5 + 4 * ST + b); };
+  const uint32_t td_bar = BAR(7 + 4 * ST);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + TR::NUM_BARS);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* status = &g_attn_status;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(k_full(s), 1);
+      mbar_init(k_empty(s), 1);
+      mbar_init(v_full(s), 1);
+      mbar_init(v_empty(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(s_full(b), 1);
+      mbar_init(p_full(b), 128);
+    }
+    mbar_init(o_done(0), 1);
+    mbar_init(o_done(1), 1);
+    mbar_init(td_bar, 1);
+    *abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 4 && lane == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK0);
+    tma_prefetch_desc(&tmV0);
+    tma_prefetch_desc(&tmKs);
+    tma_prefetch_desc(&tmVs);
+  }
+  if (warp == 5) {
+    tmem_alloc(smem_u32(tmem_slot), TR::TM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 4) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      const uint64_t pol_kv = policy_evict_last();
+      int last_k[ST], last_v[ST];
+      for (int s = 0; s < ST; ++s) last_k[s] = last_v[s] = -1;
+      mbar_arrive_expect_tx(q_full, TR::Q_BYTES);
+#pragma unroll
+      for (int c = 0; c < TR::NCH; ++c)
+        tma_load_3d(smem_u32(smem + TR::OFF_Q + c * TR::Q_CHUNK_BYTES), &tmQ, c * TR::CHUNK,
+                    w.head, x.q_start + q0, q_full);
+      SegCursor cur;
+      cur.start(g, BN);
+      int waited = 0;  // highest step whose slot is known present
+      for (int j = 0; j < n_kv; ++j) {
+        cur.seek(g, j, BN);
+        const int s = j % ST, ph = (j / ST) & 1;
+        const int row = g.a + (j - cur.first) * BN;
+        if (cur.s > waited) {
+          if (p.arrived != nullptr &&
+              !wait_arrived(p.arrived + (cur.s - 1) * p.arrived_stride,
+                            p.arrived_base + uint32_t(cur.s * p.arrived_step), p.arrive_wait_ns,
+                            abort, status))
+            break;
+          waited = cur.s;
+        }
+        if (j >= ST && !mbar_wait(k_empty(s), ph ^ 1, abort, kErrKEmpty, status)) break;
+        mbar_arrive_expect_tx(k_full(s), TR::KV_BYTES);
+#pragma unroll
+        for (int c = 0; c < TR::NCH; ++c) {
+          const uint32_t dst = smem_u32(smem + TR::OFF_K + s * TR::KV_BYTES + c * TR::KV_CHUNK_BYTES);
+          if (cur.s == 0)
+            tma_load_3d_hint(dst, &tmK0, c * TR::CHUNK, w.kvh, row, k_full(s), pol_kv);
+          else
+            tma_load_4d_hint(dst, &tmKs, c * TR::CHUNK, w.kvh, row, cur.s - 1, k_full(s), pol_kv);
+        }
+        last_k[s] = j;
+        if (j >= ST && !mbar_wait(v_empty(s), ph ^ 1, abort, kErrVEmpty, status)) break;
+        mbar_arrive_expect_tx(v_full(s), TR::KV_BYTES);
+#pragma unroll
+        for (int c = 0; c < TR::NCH; ++c) {
+          const uint32_t dst = smem_u32(smem + TR::OFF_V + s * TR::KV_BYTES + c * TR::KV_CHUNK_BYTES);
+          if (cur.s == 0)
+            tma_load_3d_hint(dst, &tmV0, c * TR::CHUNK, w.kvh, row, v_full(s), pol_kv);
+          else
+            tma_load_4d_hint(dst, &tmVs, c * TR::CHUNK, w.kvh, row, cur.s - 1, v_full(s), pol_kv);
+        }
+        last_v[s] = j;
+      }
+      // every copy this thread issued has landed before it leaves its role
+      mbar_wait_drain(q_full, 0, kErrDrain, status);
+      for (int s = 0; s < ST; ++s) {
+        if (last_k[s] >= 0) mbar_wait_drain(k_full(s), (last_k[s] / ST) & 1, kErrDrain, status);
+        if (last_v[s] >= 0) mbar_wait_drain(v_full(s), (last_v[s] / ST) & 1, kErrDrain, status);
+      }
+    }
+  } else if (warp == 5) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const int fmt = p.in_fmt;
+      const uint32_t idesc_qk = make_idesc(BM, BN, fmt, fmt, 0, 0);
+      const uint32_t idesc_pv = make_idesc(BM, D, fmt, fmt, 0, 1);
+      const uint32_t sQ = smem_u32(smem + TR::OFF_Q);
+      auto issue_pv = [&](int i) -> bool {
+        const int s = i % ST, b = i & 1;
+        if (!mbar_wait(p_full(b), (i >> 1) & 1, abort, kErrPFull, status)) return false;
+        if (!mbar_wait(v_full(s), (i / ST) & 1, abort, kErrVFull, status)) return false;
+        tc_fence_after();
+        const uint32_t sV = smem_u32(smem + TR::OFF_V + s * TR::KV_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < BN / TR::MMA_K; ++kk) {
+          const uint64_t bdesc = make_desc_sw128(sV + kk * TR::MMA_K * 128, TR::KV_CHUNK_BYTES, 1024);
+          const uint32_t a_tmem = tmem + uint32_t(b * BN + kk * 8);
+          mma_f16_ts(tmem + TR::TM_O, a_tmem, bdesc, idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
+        }
+        tc_commit(o_done(b));
+        tc_commit(v_empty(s));
+        return true;
+      };
+      bool ok = mbar_wait(q_full, 0, abort, kErrQ, status);
+      tc_fence_after();
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int s = j % ST, b = j & 1;
+        if (!mbar_wait(k_full(s), (j / ST) & 1, abort, kErrKFull, status)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t sK = smem_u32(smem + TR::OFF_K + s * TR::KV_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < D / TR::MMA_K; ++kk) {
+          const int off = kk * 32;  // bytes along D of this K-step
+          const uint32_t ca = (off / 128) * TR::Q_CHUNK_BYTES + (off % 128);
+          const uint32_t cb = (off / 128) * TR::KV_CHUNK_BYTES + (off % 128);
+          const uint64_t adesc = make_desc_sw128(sQ + ca, 16, 1024);
+          const uint64_t bdesc = make_desc_sw128(sK + cb, 16, 1024);
+          mma_f16_ss(tmem + uint32_t(b * BN), adesc, bdesc, idesc_qk, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(s_full(b));
+        tc_commit(k_empty(s));
+        if (j > 0 && !issue_pv(j - 1)) { ok = false; break; }
+      }
+      if (ok && n_kv > 0) issue_pv(n_kv - 1);
+      // every MMA issued above has completed before TMEM is released
+      tc_commit(td_bar);
+      mbar_wait_drain(td_bar, 0, kErrDrain, status);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax + epilogue
+    const int r = warp * 32 + lane;
+    const uint32_t t_lane = tmem + (uint32_t(warp * 32) << 16);
+    const int key_lim = q0 + r + g.diag;  // step 0 only
+    const float qd = p.q_descale != nullptr ? p.q_descale[w.kvh] : 1.0f;
+    // score scale (log2 units) and V descale of step s: the descales of its source rank
+    auto step_scales = [&](int s, float& sc, float& vs) {
+      const int src = (p.rank - s + p.S) % p.S;
+      sc = p.scale_log2 * qd;
+      vs = 1.0f;
+      if (p.k_descales != nullptr) sc *= p.k_descales[src * p.Hkv + w.kvh];
+      if (p.v_descales != nullptr) vs = p.v_descales[src * p.Hkv + w.kvh];
+    };
+    float scale, vscale;
+    step_scales(0, scale, vscale);
+    int step = 0;
+    float m = kNegInf, l = 0.f;  // m: running max of the scaled scores (log2 units)
+    bool aborted = false;
+    SegCursor cur;
+    cur.start(g, BN);
+
+    for (int j = 0; j < n_kv; ++j) {
+      cur.seek(g, j, BN);
+      float fo = 1.0f;  // O factor when the V descale changes with the step (CTA-uniform)
+      if (cur.s != step) {
+        step = cur.s;
+        float vs_new;
+        step_scales(step, scale, vs_new);
+        fo = vscale / vs_new;
+        vscale = vs_new;
+      }
+      const int b = j & 1;
+      bool ok = mbar_wait(s_full(b), (j >> 1) & 1, abort, kErrSFull, status);
+      if (!__all_sync(0xffffffffu, ok)) { aborted = true; break; }
+      tc_fence_after();
+      uint32_t sr[BN / 32][32];
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) tmem_ld32(t_lane + uint32_t(b * BN + c * 32), sr[c]);
+      tmem_wait_ld();
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) reg_fence32(sr[c]);
+
+      const int kbase = (j - cur.first) * BN;
+      const int seg_len = g.len(cur.s);
+      const bool causal = cur.s == 0;
+      const bool need_mask = (kbase + BN > seg_len) || (causal && kbase + BN - 1 > q0 + g.diag);
+      if (need_mask) {
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c)
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int key = kbase + c * 32 + e;
+            if (key >= seg_len || (causal && key > key_lim)) sr[c][e] = __float_as_uint(kNegInf);
+          }
+      }
+      float mx = kNegInf;
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c)
+#pragma unroll
+        for (int e = 0; e < 32; ++e) mx = fmaxf(mx, __uint_as_float(sr[c][e]));
+      const float m_new = fmaxf(m, mx * scale);  // scale > 0
+      if (j == 0) {
+        m = m_new;
+      } else {
+        const bool need = (m_new - m) > kRescaleThreshold;
+        if (__any_sync(0xffffffffu, need) || fo != 1.0f) {
+          const float f = need ? ex2_approx(m - m_new) : 1.0f;
+          if (need) { l *= f; m = m_new; }
+          // PV_{j-1} has completed before O is rescaled
+          ok = mbar_wait(o_done((j - 1) & 1), ((j - 1) >> 1) & 1, abort, kErrODone, status);
+          if (!__all_sync(0xffffffffu, ok)) { aborted = true; break; }
+          tc_fence_after();
+          const float fof = f * fo;
+#pragma unroll 1
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t o[32];
+            tmem_ld32(t_lane + uint32_t(TR::TM_O + c * 32), o);
+            tmem_wait_ld();
+            reg_fence32(o);
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * fof);
+            tmem_st32(t_lane + uint32_t(TR::TM_O + c * 32), o);
+          }
+          tmem_wait_st();
+        }
+      }
+      const float neg_m = (m == kNegInf) ? 0.f : -m;
+      float rs = 0.f;
+#pragma unroll
+      for (int half = 0; half < BN / 64; ++half) {
+        uint32_t pw[32];
+#pragma unroll
+        for (int e = 0; e < 64; e += 2) {
+          const int c = half * 2 + (e >> 5), ee = e & 31;
+          const float x0 = ex2_approx(fmaf(__uint_as_float(sr[c][ee]), scale, neg_m));
+          const float x1 = ex2_approx(fmaf(__uint_as_float(sr[c][ee + 1]), scale, neg_m));
+          rs += x0 + x1;
+          pw[e >> 1] = p.in_fmt ? pack_bf16x2(x0, x1) : pack_f16x2(x0, x1);
+        }
+        tmem_st32(t_lane + uint32_t(b * BN + half * 32), pw);
+      }
+      l += rs;
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(p_full(b));
+    }
+
+    // ------------------------------------------------------------ epilogue
+    if (!aborted && n_kv > 0) {
+      bool ok = mbar_wait(o_done((n_kv - 1) & 1), ((n_kv - 1) >> 1) & 1, abort, kErrODone, status);
+      if (!__all_sync(0xffffffffu, ok)) aborted = true;
+      tc_fence_after();
+    }
+    if (!aborted) {  // warp-uniform: every lane takes part in the TMEM loads
+      const bool valid = r < rows;
+      const int64_t grow = int64_t(x.q_start) + q0 + r;
+      const bool any_key = (m != kNegInf) && (l > 0.f);
+      const float cb = any_key ? vscale / l : 0.f;
+      uint8_t* orow = static_cast<uint8_t*>(p.out) + (grow * p.Hq + w.head) * int64_t(D) * 2;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        tmem_ld32(t_lane + uint32_t(TR::TM_O + c * 32), o);
+        tmem_wait_ld();
+        reg_fence32(o);
+        if (valid) {
+          uint4* dst = reinterpret_cast<uint4*>(orow + c * 64);
+#pragma unroll
+          for (int v4 = 0; v4 < 4; ++v4) {
+            uint32_t wd[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float f0 = __uint_as_float(o[v4 * 8 + 2 * i]) * cb;
+              const float f1 = __uint_as_float(o[v4 * 8 + 2 * i + 1]) * cb;
+              wd[i] = p.out_bf16 ? pack_bf16x2(f0, f1) : pack_f16x2(f0, f1);
+            }
+            dst[v4] = make_uint4(wd[0], wd[1], wd[2], wd[3]);
+          }
+        }
+      }
+      if (valid) p.lse[grow * p.Hq + w.head] = any_key ? (m + lg2_approx(l)) * kLn2 : kNegInf;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 5) tmem_dealloc(tmem, TR::TM_COLS);
+}
+
 // Persistent form (e4m3): one CTA per SM walks the heaviest-first tile list (static
 // boustrophedon schedule), with the per-step kernel's cross-tile hand-offs: the Q buffers are
 // refilled once the previous tile's S MMAs completed (q_empty), and PV_t of a new tile waits

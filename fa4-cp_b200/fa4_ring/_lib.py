@@ -77,6 +77,9 @@ _SIGNATURES = {
     "fa4cp_ring_attn_fused": [_vp, _vp, _vp, _vp, _vp, _i64, _vp, _vp, _vp, _i32, _i32, _i64,
                               _i32, _i32, _i32, _i32, _f32, _vp, _vp, _vp, _i32, _i32, _vp,
                               ctypes.c_uint32, _vp],
+    "fa4cp_ring_attn_fused_mixed": [_vp, _vp, _vp, _vp, _vp, _i64, _vp, _vp, _vp, _i32, _i32,
+                                    _i64, _i32, _i32, _i32, _f32, _vp, _vp, _i32, _i32, _vp,
+                                    ctypes.c_uint32, _vp],
     "fa4cp_ring_attn_fused_remote": [_vp, _vp, _vp, _vp, _vp, _i64, _vp, _vp, _vp, _i32, _i32,
                                      _i64, _i32, _i32, _i32, _i32, _f32, _i32, _i32, _vp,
                                      ctypes.c_uint32, _vp],

@@ -406,7 +406,8 @@ class NativeRing:
         _lib.check(self.lib.fa4cp_ring_timing(self.handle, int(max_launches)), "ring_timing")
 
     def set_fused(self, mode: int) -> None:
-        """Ring kernel: 0 never, 1 for f16 / bf16 only, 2 also for e4m3 (the library default)."""
+        """Ring kernel: 0 never, 1 for f16 / bf16 (D 64, 128), 2 also for e4m3 (the library
+        default), 3 also at head_dim 256 (f16 / bf16, and bf16 q with e4m3 K/V)."""
         from . import _lib
 
         if getattr(self, "_fused", None) != int(mode):

@@ -181,8 +181,9 @@ NATIVE_EXECUTOR = True
 # (send/recv on the executor's own communicator)
 RING_TRANSPORT = "copy_engine"
 # copy engine: run the whole forward as one launch of the ring kernel -- True: for f16 / bf16
-# with D 64 or 128 and e4m3 with D 128; "16bit": f16 / bf16 only; False: one attention launch
-# per step
+# with D 64 or 128 and e4m3 with D 128; "all": also at head_dim 256 (f16 / bf16, and bf16 q
+# with e4m3 K/V -- measured 2-5% slower than the per-step kernels at cfg5's sizes, so not the
+# default); "16bit": f16 / bf16 (D 64, 128) only; False: one attention launch per step
 RING_FUSED = True
 
 
@@ -215,12 +216,15 @@ def _native_forward(q, k, v, cfg: RingConfig, group, *, cu, nseq, max_seqlen,
     lse = torch.empty((T, Hq), dtype=torch.float32, device=dev)
     kv_bytes = k.numel() * k.element_size()
     ring = native_ring(rank, S, dev, group, RING_TRANSPORT)
+    # bf16 q x e4m3 K/V at head_dim 256: the ring kernel takes the K/V as exact bf16 images,
+    # which the executor converts once and pushes (twice the e4m3 bytes per slot)
+    mixed_fused = is_mixed(q, k) and D == 256 and ring.copy_engine and RING_FUSED == "all"
     bufs = None
     if ring.transport == "nccl":
         bufs = torch.empty(4 * kv_bytes, dtype=torch.uint8, device=dev)  # two [K | V] slots
     else:
-        ring.ensure_capacity(kv_bytes)
-        ring.set_fused(1 if RING_FUSED == "16bit" else (2 if RING_FUSED else 0))
+        ring.ensure_capacity(2 * kv_bytes if mixed_fused else kv_bytes)
+        ring.set_fused({"16bit": 1, "all": 3}.get(RING_FUSED, 2 if RING_FUSED else 0))
     ws = None
     if is_mixed(q, k):
         nbytes = _lib.load().fa4cp_attn_kv8_workspace_bytes(T, Hkv, D)
@@ -229,12 +233,19 @@ def _native_forward(q, k, v, cfg: RingConfig, group, *, cu, nseq, max_seqlen,
         q, k, v, out, lse, cu, nseq=nseq, max_seqlen=max_seqlen, softmax_scale=scale,
         q_descale=qd, k_descales=kds, v_descales=vds, kv_bufs=bufs, workspace=ws)
     fused = (ring.copy_engine and bool(RING_FUSED) and q.dtype == k.dtype
-             and ((q.dtype in (torch.float16, torch.bfloat16) and D in (64, 128))
-                  or (RING_FUSED is True and q.dtype == torch.float8_e4m3fn and D == 128)))
+             and ((q.dtype in (torch.float16, torch.bfloat16)
+                   and (D in (64, 128) or (D == 256 and RING_FUSED == "all")))
+                  or (RING_FUSED in (True, "all") and q.dtype == torch.float8_e4m3fn
+                      and D == 128)))
     # the ring kernel: e4m3 runs a main pass and a split pass (rows that see few keys); with
-    # direct pushes and S >= 8 f16 / bf16 run step 0 in a launch of its own before the remote walk
-    two_pass = q.dtype == torch.float8_e4m3fn or (ring.transport == "copy_engine" and S >= 8)
-    _lib.count_launches((2 if two_pass else 1) if fused else S * (3 if ws is not None else 1))
+    # direct pushes and S >= 8 f16 / bf16 (D 64, 128) run step 0 in a launch of its own before
+    # the remote walk; bf16 x e4m3 K/V converts K and V (two launches) before its one launch
+    two_pass = q.dtype == torch.float8_e4m3fn or (ring.transport == "copy_engine" and S >= 8
+                                                  and D != 256)
+    if mixed_fused:
+        _lib.count_launches(3)
+    else:
+        _lib.count_launches((2 if two_pass else 1) if fused else S * (3 if ws is not None else 1))
     return out, lse
 
 

@@ -298,8 +298,10 @@ FA4CP_API int fa4cp_local_cu(const int32_t* full_cu, int32_t nseq, int32_t cp_si
  *   free during a ring call, so that the hop's NCCL kernel runs beside it.
  * fa4cp_ring_set_fused: mode 2 (default) runs the whole forward as one launch of the ring
  *   kernel (fa4cp_ring_attn_fused) for f16 / bf16 with D 64 or 128 and e4m3 with D 128
- *   (copy-engine transport or a single rank); mode 1 for f16 / bf16 only; 0 keeps one
- *   attention launch per step.
+ *   (copy-engine transport or a single rank); mode 1 for f16 / bf16 only; mode 3 also at
+ *   head_dim 256 (f16 / bf16, and bf16 q with e4m3 K/V through fa4cp_ring_attn_fused_mixed,
+ *   the K/V converted to bf16 once per rank and pushed as such; the workspace of
+ *   fa4cp_ring_attn_fwd then holds them); 0 keeps one attention launch per step.
  * fa4cp_ring_timing: time the next `max_launches` attention launches and hops (0 = off) with
  *   CUDA events; fa4cp_ring_timeline writes (start, end) pairs in ms relative to the first
  *   timed launch's start into HOST float arrays (attention launches and hops, in issue order,
@@ -399,8 +401,9 @@ FA4CP_API int fa4cp_ring_ce_direct_plan(int32_t nranks, int32_t rank, int64_t ca
  *   q [total, Hq, D], k/v [total, Hkv, D] local; slots_k / slots_v: slot i at
  *   slots_k + i * slot_stride bytes, each [total, Hkv, D] (the source's shard, same cu);
  *   out [total, Hq, D] (q dtype; bf16 for e4m3); lse [total, Hq] float32.  f16 / bf16 with
- *   D 64 or 128, or e4m3 with D 128: then q_descale [Hkv] and k_descales / v_descales
+ *   D 64, 128 or 256, or e4m3 with D 128: then q_descale [Hkv] and k_descales / v_descales
  *   [nranks, Hkv] indexed by SOURCE rank (each may be NULL = 1); NULL for 16-bit inputs.
+ *   D 256 runs one 128-row query tile per CTA (S and O of two tiles exceed TMEM).
  */
 /*
  * Wall-time bound (ms, default 10000) of the ring kernel's wait for a hop counter; past it
@@ -419,6 +422,26 @@ FA4CP_API int fa4cp_ring_attn_fused(const void* q, const void* k, const void* v,
                                     const float* v_descales, int32_t nranks, int32_t rank,
                                     const uint32_t* arrived, uint32_t arrived_base,
                                     void* stream);
+/*
+ * fa4cp_ring_attn_fused_mixed: the ring kernel for a bf16 query with e4m3 K/V at head_dim 256
+ * (the reference's bf16-Q x e4m3-K/V ring, fa4_ring/ring_attention.py:139-166, with the per-
+ * source descales of fa4_ring/fa4_backend.py:99-120).  k, v and every slot hold the EXACT bf16
+ * images of the e4m3 shards (fa4cp_dequant_e4m3 with a NULL descale: e4m3 -> bf16 is exact);
+ * k_descales / v_descales [nranks, Hkv] by source rank (NULL = 1) are applied in fp32 inside the
+ * kernel (score scale, output factor), so the result equals attention over the dequantised
+ * K/V up to the kernel's bf16 P.  Slot stride and layout as fa4cp_ring_attn_fused (bf16
+ * bytes).  out bf16 [total, Hq, 256]; lse float32 [total, Hq].
+ */
+FA4CP_API int fa4cp_ring_attn_fused_mixed(const void* q, const void* k, const void* v,
+                                          const void* slots_k, const void* slots_v,
+                                          int64_t slot_stride, void* out, float* lse,
+                                          const int32_t* cu, int32_t nseq, int32_t max_seqlen,
+                                          int64_t total, int32_t num_heads_q,
+                                          int32_t num_heads_kv, int32_t head_dim,
+                                          float softmax_scale, const float* k_descales,
+                                          const float* v_descales, int32_t nranks, int32_t rank,
+                                          const uint32_t* arrived, uint32_t arrived_base,
+                                          void* stream);
 /*
  * fa4cp_ring_attn_fused_remote: the same ring kernel over the remote steps 1 .. nranks-1 only,
  * merged into the (out, lse) already there -- the partial of step 0, the local K/V, causal, as

@@ -10,7 +10,9 @@ the Python step loop over ``KVRing``, and in ``batched`` mode; FP8 e4m3 Q/K/V an
 with e4m3 K/V (quantised per rank, descales all-gathered by source rank) through the
 native executor, checked against the dense attention of the dequantised tensors.  The
 copy-engine cases run twice in a row (the hop counters carry over between calls), and
-the packed case makes the receive slots grow.  Tolerances: bf16 2e-2, FP8 6e-2.  Then the
+the packed case makes the receive slots grow.  Tolerances: bf16 2e-2, FP8 6e-2.  bf16 Q with
+e4m3 K/V at head_dim 256 through the one-query-tile ring kernel and the per-step kernels,
+against the dequantised K/V in fp32, within 2e-2.  Then the
 ring backward (autograd through ``ring_flash_attn``: K/V hops plus the rotating fp32 dK/dV
 accumulators over NCCL) against the oracle's dense gradient, within 2e-2 * max(1, max|ref|).
 Last, the GDN all-gather CP wrapper (``fa4_ring.gdn_cp.gdn_cp_allgather``) against the
@@ -137,6 +139,46 @@ def main():
                         print(f"world={world} seqs={num_seqs} backward seq{j} {name} "
                               f"max_err={err:.3e} (max|ref| {mag:.2f})")
                         ok &= err <= 2e-2 * mag
+        # head_dim 256 with a bf16 q and e4m3 K/V (cfg5's operands): the one-query-tile ring
+        # kernel behind direct pushes (each rank converts its K/V to bf16 once; two calls in a
+        # row), and the per-step kernels; against dense attention of the dequantised K/V (fp32)
+        H2, Hkv2, D2 = 4, 2, 256
+        scale2 = 1.0 / math.sqrt(D2)
+        for num_seqs in (1, 3):
+            g = torch.Generator().manual_seed(4321)
+            lens = [2 * world * 160] if num_seqs == 1 else [2 * world * n for n in (64, 16, 80)]
+            cu = [0] + list(np.cumsum(lens))
+            q, k, v = (torch.randn(cu[-1], h, D2, generator=g).bfloat16().to(dev)
+                       for h in (H2, Hkv2, Hkv2))
+            if num_seqs == 1:
+                lq, lk, lv = (zigzag_shard(t, rank, world) for t in (q, k, v))
+                kw = {}
+            else:
+                lq, lcu = zigzag_shard_varlen(q, cu, rank, world)
+                lk, _ = zigzag_shard_varlen(k, cu, rank, world)
+                lv, _ = zigzag_shard_varlen(v, cu, rank, world)
+                kw = {"cu_seqlens": lcu, "max_seqlen": max(lens) // world}
+            tk, ks = quantize_e4m3(lk)
+            tv, vs = quantize_e4m3(lv)
+            desc = Descales(q=None, k=allgather_descales(ks), v=allgather_descales(vs))
+            ins = [gather_full(t, world, cu, num_seqs)
+                   for t in (lq, tk.float() * desc.k[rank], tv.float() * desc.v[rank])]
+            for executor in ("copy_engine", "copy_engine", "copy_engine_steps"):
+                ring_attention.NATIVE_EXECUTOR = True
+                ring_attention.RING_FUSED = "all" if executor != "copy_engine_steps" else False
+                ring_attention.RING_TRANSPORT = "copy_engine"
+                cfg = RingConfig(cp_size=world, cp_rank=rank)
+                out = ring_flash_attn(lq, tk, tv, cfg, descales=desc, **kw)
+                full = gather_full(out, world, cu, num_seqs)
+                if rank == 0:
+                    qn, kn, vn = ins
+                    for j in range(len(lens)):
+                        a, b = cu[j], cu[j + 1]
+                        ref, _ = orc.dense_causal(qn[a:b], kn[a:b], vn[a:b], scale2)
+                        err = float(np.abs(full[a:b] - ref).max())
+                        print(f"world={world} seqs={num_seqs} mixed D=256 executor={executor} "
+                              f"seq{j} max_err={err:.3e}")
+                        ok &= err <= 2e-2
         # GDN all-gather CP (Plan A): the CP output equals the single-device scan, exactly
         from fa4_ring.gdn_cp import build_gdn_cp_metadata, gdn_cp_allgather
         lens = [2 * world * n for n in (5, 12)]

@@ -12,8 +12,11 @@ shards (scale = amax/448), the K/V descales are indexed by source rank, and the 
 on the dequantised shards: out <= 6e-2 on every row, LSE <= 1e-3 (the tolerances of the
 FP8 path).  Rows that see only a handful of keys are the hard case for an e4m3 P (3 mantissa
 bits): the kernel feeds the causal diagonal tile's P to the PV MMA as two e4m3 terms
-(P = hi + lo), so those rows are as accurate as the rest.  The multi-GPU run of the same
-kernel behind the copy-engine transport is ``tests/dist_ring_check.py``.
+(P = hi + lo), so those rows are as accurate as the rest.  head_dim 256 runs the one-query-
+tile ring kernel, for f16 / bf16 and for a bf16 query with e4m3 K/V
+(``fa4cp_ring_attn_fused_mixed``: the K/V as exact bf16 images, descales by source rank).  The
+multi-GPU run of the same kernels behind the copy-engine transport is
+``tests/dist_ring_check.py``.
 """
 
 import ctypes
@@ -31,7 +34,8 @@ pytestmark = pytest.mark.gpu
 OUT_TOL, LSE_TOL = 2e-2, 1e-3
 
 
-def run_fused(cp, lens, H, Hkv, D, dtype, seed, counter=False, fp8=False, two_pass=False):
+def run_fused(cp, lens, H, Hkv, D, dtype, seed, counter=False, fp8=False, two_pass=False,
+              mixed=False):
     from fa4_ring import _lib
     from fa4_ring.zigzag import zigzag_shard_varlen
     lib = _lib.load()
@@ -63,6 +67,17 @@ def run_fused(cp, lens, H, Hkv, D, dtype, seed, counter=False, fp8=False, two_pa
         vd = torch.stack([b.reshape(1).expand(Hkv) for _, b in vq]).contiguous().cuda()
         qds = [b.reshape(1).expand(Hkv).contiguous().cuda() for _, b in qq]
         dtype, out_dt = torch.float8_e4m3fn, torch.bfloat16
+    elif mixed:  # bf16 q; e4m3 K/V quantised per rank, passed as their exact bf16 images
+        kq = [quant_e4m3(t) for t in ks]
+        vq = [quant_e4m3(t) for t in vs]
+        q_np = [to_np(t) for t in qs]
+        k_np = [dequant(a, b) for a, b in kq]
+        v_np = [dequant(a, b) for a, b in vq]
+        ks = [a.to(torch.bfloat16) for a, _ in kq]
+        vs = [a.to(torch.bfloat16) for a, _ in vq]
+        assert all(torch.equal(a.float(), b.float()) for a, b in zip(ks, (x for x, _ in kq)))
+        kd = torch.stack([b.reshape(1).expand(Hkv) for _, b in kq]).contiguous().cuda()
+        vd = torch.stack([b.reshape(1).expand(Hkv) for _, b in vq]).contiguous().cuda()
     else:
         q_np = [to_np(t) for t in qs]
         k_np = [to_np(t) for t in ks]
@@ -85,7 +100,14 @@ def run_fused(cp, lens, H, Hkv, D, dtype, seed, counter=False, fp8=False, two_pa
         if counter:
             base = 1000
             ctr = torch.tensor([base + cp - 1], dtype=torch.int32, device="cuda")
-        if two_pass:
+        if mixed:
+            rc = lib.fa4cp_ring_attn_fused_mixed(
+                qs[r].data_ptr(), ks[r].data_ptr(), vs[r].data_ptr(), slots_k.data_ptr(),
+                slots_v.data_ptr(), T * Hkv * D * 2, out.data_ptr(), lse.data_ptr(),
+                lcu.data_ptr(), len(lens), max_local, T, H, Hkv, D, scale, _lib.ptr(kd),
+                _lib.ptr(vd), cp, r, None if ctr is None else ctypes.c_void_p(ctr.data_ptr()),
+                base, stream)
+        elif two_pass:
             # step 0 (local K/V, causal) on its own, then the remote steps merged into it
             rc = lib.fa4cp_attn_fwd(
                 qs[r].data_ptr(), ks[r].data_ptr(), vs[r].data_ptr(), out.data_ptr(),
@@ -112,7 +134,7 @@ def run_fused(cp, lens, H, Hkv, D, dtype, seed, counter=False, fp8=False, two_pa
         np.testing.assert_allclose(got_o, want_o, atol=tol_o, rtol=0)
         np.testing.assert_allclose(to_np(lse), want_l, atol=tol_l, rtol=0)
         outs.append(to_np(out))
-    if fp8:
+    if fp8 or mixed:
         assert_device_ok()
         return
     # the stitched output is plain causal attention of every sequence
@@ -160,6 +182,35 @@ def test_ring_remote_walk_merged_into_step0(cp, lens, H, Hkv, D, dtype):
     run_fused(cp, lens, H, Hkv, D, dtype, seed=40 + cp, two_pass=True)
 
 
+@pytest.mark.parametrize("cp,lens,H,Hkv,D,dtype", [
+    (1, [512], 4, 2, 256, torch.bfloat16),
+    (2, [2 * 2 * 160], 4, 2, 256, torch.bfloat16),         # 160-row halves: a partial tile
+    (4, [2 * 4 * n for n in (40, 3, 97, 64)], 4, 1, 256, torch.float16),  # packed sequences
+])
+def test_ring_fused_head_dim_256(cp, lens, H, Hkv, D, dtype):
+    """head_dim 256: one 128-row query tile per CTA (fa4cp_ring_attn_fused)."""
+    run_fused(cp, lens, H, Hkv, D, dtype, seed=60 + cp)
+
+
+@pytest.mark.parametrize("cp,lens,H,Hkv", [
+    (1, [512], 4, 2),
+    (2, [2 * 2 * 160], 4, 2),
+    (4, [2 * 4 * 200], 4, 1),
+    (8, [2 * 8 * 128], 2, 1),
+    (3, [2 * 3 * n for n in (40, 97)], 4, 2),
+])
+def test_ring_fused_mixed_bf16_q_e4m3_kv(cp, lens, H, Hkv):
+    """bf16 q with e4m3 K/V at head_dim 256 (fa4cp_ring_attn_fused_mixed): K/V passed as the
+    exact bf16 images of every rank's e4m3 shards, the K/V descales by source rank applied in
+    the kernel; against the oracle on the dequantised shards at the bf16 tolerances (out 2e-2,
+    LSE 1e-3): no operand is rounded beyond the e4m3 values themselves."""
+    run_fused(cp, lens, H, Hkv, 256, torch.bfloat16, seed=80 + cp, mixed=True)
+
+
+def test_ring_fused_mixed_counter_already_reached():
+    run_fused(4, [2 * 4 * 128], 4, 2, 256, torch.bfloat16, seed=6, counter=True, mixed=True)
+
+
 def test_ring_fused_counter_already_reached():
     run_fused(4, [2 * 4 * 128], 4, 2, 128, torch.bfloat16, seed=5, counter=True)
 
@@ -171,5 +222,11 @@ def test_ring_fused_rejects_unsupported_shapes():
     args = [dummy] * 5 + [1 << 20, dummy, dummy, dummy, 1, 64, 128, 4, 2]
     tail = [None, None, None, 2, 0, None, 0, None]
     assert lib.fa4cp_ring_attn_fused(*args, 64, _lib.DTYPE_E4M3, 0.1, *tail) == _lib.ERR_UNSUPPORTED
-    assert lib.fa4cp_ring_attn_fused(*args, 256, _lib.DTYPE_BF16, 0.1, *tail) == _lib.ERR_UNSUPPORTED
+    assert lib.fa4cp_ring_attn_fused(*args, 96, _lib.DTYPE_BF16, 0.1, *tail) == _lib.ERR_UNSUPPORTED
+    # descales with 16-bit operands: only through the e4m3-K/V entry (head_dim 256)
+    d = ctypes.c_void_p(256)
+    assert lib.fa4cp_ring_attn_fused(*args, 256, _lib.DTYPE_BF16, 0.1, None, d, d,
+                                     *tail[3:]) == _lib.ERR_INVALID
+    assert lib.fa4cp_ring_attn_fused_mixed(*args, 128, 0.1, d, d, 2, 0, None, 0,
+                                           None) == _lib.ERR_INVALID
     assert lib.fa4cp_ring_attn_fused(*args, 128, _lib.DTYPE_F32, 0.1, *tail) == _lib.ERR_UNSUPPORTED
