@@ -565,8 +565,8 @@ def gpu_main(args, rank, world, local_rank):
 
 
 def local_schedule_ms(lq, lk, lv, cfg, desc, lcu, nseq, max_local, fused, flush, steps, world):
-    """Exposed communication as SURVEY's measurement section defines it: the same schedule
-    with the transfers skipped.  Every rank's K/V shard is all-gathered first (untimed), so
+    """Exposed communication defined as ring time minus the same schedule run with the
+    transfers skipped.  Every rank's K/V shard is all-gathered first (untimed), so
     each step's K/V is already in this GPU's memory; then this rank's forward is timed exactly
     as the ring ran it -- the ring kernel through its public C entry point with every receive
     slot filled and no hop counter (``fa4cp_ring_attn_fused``, arrived = NULL), or the
