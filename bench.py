@@ -554,7 +554,8 @@ def gpu_main(args, rank, world, local_rank):
             "kind": "port",
             "sample": "oracle (numpy restatement of the reference's CPU ring simulation) on "
                       "rank 0 of cfg2 at cp=8: all 8 ring steps, 32 heads, T=4096 local "
-                      f"tokens; {flops_cpu:.3e} FLOP in {secs_cpu:.1f} s"}
+                      f"tokens; {flops_cpu:.3e} FLOP in {secs_cpu:.1f} s",
+            "vs_reference_cpu_code": _cpu_speed_pin()}
     if world == 1:
         line["hbm_kernels"] = hbm_kernels(dev)
     traffic, traffic_src = _traffic_from_profile(args.config, world)
@@ -807,6 +808,24 @@ def bwd_main(args, rank, world, local_rank):
     }
 
 
+def _cpu_speed_pin():
+    """The port's speed against the reference's own CPU ring code on one sample, measured
+    where the reference checkout exists (``oracle/cpu_speed_pin.py`` writes
+    ``oracle/cpu_speed_pin.json``); None when absent."""
+    try:
+        with open(os.path.join(ROOT, "oracle", "cpu_speed_pin.json")) as f:
+            pin = json.load(f)
+    except (OSError, ValueError):
+        return None
+    return {"port_over_reference": pin.get("port_over_reference"),
+            "reference_gflops": pin.get("reference_gflops"), "port_gflops": pin.get("port_gflops"),
+            "threads": pin.get("threads"), "sample": pin.get("sample"),
+            "how": "oracle/cpu_speed_pin.py: the reference's cpu_attn / merge driven as its "
+                   "simulate_ring, and this port, on the same sample in the build container "
+                   "(the reference checkout is not on the GPU box); > 1 means the port is the "
+                   "faster, so the reported CPU baseline does not understate the reference"}
+
+
 def _bwd_cpu_baseline():
     flops, secs, threads = cpu_sample_bwd()
     return {"value": round(flops / secs / 1e12, 5), "unit": "TFLOP/s", "cores": threads,
@@ -965,7 +984,8 @@ def reference_main(args):
         "cpu_baseline": {"value": round(value, 5), "unit": "TFLOP/s", "cores": threads,
                          "kind": "port",
                          "sample": "one ring step (T=4096 local tokens, 32 heads) of rank 0 of "
-                                   "cfg2 at cp=8 per bench step, cycling through the 8 steps"},
+                                   "cfg2 at cp=8 per bench step, cycling through the 8 steps",
+                         "vs_reference_cpu_code": _cpu_speed_pin()},
         "e2e": {"value": round(value, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }

@@ -26,9 +26,18 @@ Pinned against golden vectors produced by importing the reference itself:
 from __future__ import annotations
 
 import math
+import os
+from concurrent.futures import ThreadPoolExecutor
 from typing import List, Sequence, Tuple
 
 import numpy as np
+
+# Large attention blocks are split by query rows over this many threads (softmax rows are
+# independent, so the result is the same); numpy's elementwise ops (mask, exp, sums) are
+# single-threaded, and the reference's torch CPU code uses every host thread.  Threads, not
+# processes: nothing here forks.
+ATTN_WORKERS = max(1, os.cpu_count() or 1)
+_PARALLEL_MIN_SCORES = 1 << 22   # score elements per kv head below which one thread runs it
 
 # Step patterns of the zig-zag ring (fa4_ring/ring_attention.py:11-16).
 PATTERN_LOCAL_CAUSAL = 0   # step 0: local causal over [early | late]
@@ -130,27 +139,47 @@ def attn(q: np.ndarray, k: np.ndarray, v: np.ndarray, causal: bool, scale: float
     qf = q.astype(dtype)
     kf = k.astype(dtype)
     vf = v.astype(dtype)
-    mask = None
-    if causal:
-        mask = np.tril(np.ones((tq, tk), dtype=bool))
-    for hk in range(Hkv):
-        kh = kf[:, hk, :]                                  # [Tk, D]
-        vh = vf[:, hk, :]
-        qh = qf[:, hk * g:(hk + 1) * g, :].transpose(1, 0, 2)   # [g, Tq, D]
-        s = np.matmul(qh, kh.T) * dtype(scale)             # [g, Tq, Tk]
-        if mask is not None:
-            s = np.where(mask[None], s, -np.inf)
+    key_idx = np.arange(tk)
+
+    def rows(qh, kh, vh, r0, r1):
+        """Query rows [r0, r1) of one kv head's group: (o [g, r, D], lse [g, r])."""
+        s = np.matmul(qh[:, r0:r1], kh.T) * dtype(scale)   # [g, r, Tk]
+        if causal:  # the reference's square top-left tril: key j visible to row i iff j <= i
+            s = np.where((key_idx[None, :] <= np.arange(r0, r1)[:, None])[None], s, -np.inf)
         m = s.max(axis=-1, keepdims=True)
         m_safe = np.where(np.isfinite(m), m, 0)
         p = np.exp(s - m_safe)
         l = p.sum(axis=-1, keepdims=True)
         with np.errstate(divide="ignore", invalid="ignore"):
-            lse_h = (np.log(l) + m_safe)[..., 0]            # [g, Tq]
-            o = np.matmul(p, vh) / l                        # [g, Tq, D]
+            lse_h = (np.log(l) + m_safe)[..., 0]            # [g, r]
+            o = np.matmul(p, vh) / l                        # [g, r, D]
         o = np.where(l > 0, o, 0)
         lse_h = np.where(l[..., 0] > 0, lse_h, -np.inf)
-        out[:, hk * g:(hk + 1) * g, :] = o.transpose(1, 0, 2)
-        lse[:, hk * g:(hk + 1) * g] = lse_h.T
+        return o, lse_h
+
+    workers = ATTN_WORKERS if g * tq * tk >= _PARALLEL_MIN_SCORES else 1
+    bounds = np.linspace(0, tq, min(workers * 2, tq) + 1).astype(int) if workers > 1 else [0, tq]
+    pool = ThreadPoolExecutor(max_workers=workers) if workers > 1 else None
+    blas_limit = None
+    if pool is not None:  # one BLAS thread per worker: the parallelism is over row blocks
+        from threadpoolctl import threadpool_limits
+        blas_limit = threadpool_limits(limits=1, user_api="blas")
+    try:
+        for hk in range(Hkv):
+            kh = kf[:, hk, :]                                  # [Tk, D]
+            vh = vf[:, hk, :]
+            qh = qf[:, hk * g:(hk + 1) * g, :].transpose(1, 0, 2)   # [g, Tq, D]
+            spans = list(zip(bounds[:-1], bounds[1:]))
+            parts = (list(pool.map(lambda b: rows(qh, kh, vh, *b), spans)) if pool is not None
+                     else [rows(qh, kh, vh, r0, r1) for r0, r1 in spans])
+            for (r0, r1), (o, lse_h) in zip(spans, parts):
+                out[r0:r1, hk * g:(hk + 1) * g, :] = o.transpose(1, 0, 2)
+                lse[r0:r1, hk * g:(hk + 1) * g] = lse_h.T
+    finally:
+        if blas_limit is not None:
+            blas_limit.restore_original_limits()
+        if pool is not None:
+            pool.shutdown()
     return out, lse
 
 
