@@ -754,30 +754,32 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = 0; c < TR::NCH; ++c)
         tma_load_3d(smem_u32(smem + TR::OFF_Q + c * TR::Q_CHUNK_BYTES), &tmQ, c * TR::CHUNK,
                     w.head, x.q_start + q0, q_full);
-      SegCursor cur;
-      cur.start(g, BN);
-      int waited = 0;  // highest step whose slot is known present
+      // the step of tile j and its first K/V row, advanced at step boundaries only
+      int step = 0, step_end = g.tiles(0, BN), row = g.a - BN;
       for (int j = 0; j < n_kv; ++j) {
-        cur.seek(g, j, BN);
-        const int s = j % ST, ph = (j / ST) & 1;
-        const int row = g.a + (j - cur.first) * BN;
-        if (cur.s > waited) {
+        row += BN;
+        if (j == step_end) {  // next step with tiles (steps without any are skipped)
+          do {
+            ++step;
+            step_end += g.tiles(step, BN);
+          } while (j >= step_end);
+          row = g.a;
           if (p.arrived != nullptr &&
-              !wait_arrived(p.arrived + (cur.s - 1) * p.arrived_stride,
-                            p.arrived_base + uint32_t(cur.s * p.arrived_step), p.arrive_wait_ns,
+              !wait_arrived(p.arrived + (step - 1) * p.arrived_stride,
+                            p.arrived_base + uint32_t(step * p.arrived_step), p.arrive_wait_ns,
                             abort, status))
             break;
-          waited = cur.s;
         }
+        const int s = j % ST, ph = (j / ST) & 1;
         if (j >= ST && !mbar_wait(k_empty(s), ph ^ 1, abort, kErrKEmpty, status)) break;
         mbar_arrive_expect_tx(k_full(s), TR::KV_BYTES);
 #pragma unroll
         for (int c = 0; c < TR::NCH; ++c) {
           const uint32_t dst = smem_u32(smem + TR::OFF_K + s * TR::KV_BYTES + c * TR::KV_CHUNK_BYTES);
-          if (cur.s == 0)
+          if (step == 0)
             tma_load_3d_hint(dst, &tmK0, c * TR::CHUNK, w.kvh, row, k_full(s), pol_kv);
           else
-            tma_load_4d_hint(dst, &tmKs, c * TR::CHUNK, w.kvh, row, cur.s - 1, k_full(s), pol_kv);
+            tma_load_4d_hint(dst, &tmKs, c * TR::CHUNK, w.kvh, row, step - 1, k_full(s), pol_kv);
         }
         last_k[s] = j;
         if (j >= ST && !mbar_wait(v_empty(s), ph ^ 1, abort, kErrVEmpty, status)) break;
@@ -785,10 +787,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int c = 0; c < TR::NCH; ++c) {
           const uint32_t dst = smem_u32(smem + TR::OFF_V + s * TR::KV_BYTES + c * TR::KV_CHUNK_BYTES);
-          if (cur.s == 0)
+          if (step == 0)
             tma_load_3d_hint(dst, &tmV0, c * TR::CHUNK, w.kvh, row, v_full(s), pol_kv);
           else
-            tma_load_4d_hint(dst, &tmVs, c * TR::CHUNK, w.kvh, row, cur.s - 1, v_full(s), pol_kv);
+            tma_load_4d_hint(dst, &tmVs, c * TR::CHUNK, w.kvh, row, step - 1, v_full(s), pol_kv);
         }
         last_v[s] = j;
       }
@@ -863,17 +865,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     float scale, vscale;
     step_scales(0, scale, vscale);
-    int step = 0;
+    // the step of tile j, its key length and tile j's first key within it, advanced at step
+    // boundaries only (CTA-uniform)
+    int step = 0, step_end = g.tiles(0, BN), seg_len = g.len(0), kbase = -BN;
     float m = kNegInf, l = 0.f;  // m: running max of the scaled scores (log2 units)
     bool aborted = false;
-    SegCursor cur;
-    cur.start(g, BN);
 
     for (int j = 0; j < n_kv; ++j) {
-      cur.seek(g, j, BN);
-      float fo = 1.0f;  // O factor when the V descale changes with the step (CTA-uniform)
-      if (cur.s != step) {
-        step = cur.s;
+      kbase += BN;
+      float fo = 1.0f;  // O factor when the V descale changes with the step
+      if (j == step_end) {
+        do {
+          ++step;
+          step_end += g.tiles(step, BN);
+        } while (j >= step_end);
+        seg_len = g.len(step);
+        kbase = 0;
         float vs_new;
         step_scales(step, scale, vs_new);
         fo = vscale / vs_new;
@@ -890,9 +897,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int c = 0; c < BN / 32; ++c) reg_fence32(sr[c]);
 
-      const int kbase = (j - cur.first) * BN;
-      const int seg_len = g.len(cur.s);
-      const bool causal = cur.s == 0;
+      const bool causal = step == 0;
       const bool need_mask = (kbase + BN > seg_len) || (causal && kbase + BN - 1 > q0 + g.diag);
       if (need_mask) {
 #pragma unroll
