@@ -11,6 +11,7 @@ step patterns of every rank tile each (query, key) pair of the causal triangle e
 import math
 
 import numpy as np
+import pytest
 from hypothesis import given, settings
 from hypothesis import strategies as st
 
@@ -123,3 +124,22 @@ def test_step_patterns_tile_the_causal_triangle_once(cp, h):
                 else:
                     count[np.ix_(qrows, krows)] += 1
     assert np.array_equal(count, np.tril(np.ones((n, n), dtype=np.int64)))
+
+
+@pytest.mark.parametrize("causal,tq,tk", [(True, 1024, 1024), (False, 512, 1536),
+                                          (True, 300, 300)])
+def test_threaded_attention_equals_one_thread(causal, tq, tk, monkeypatch):
+    """Large attention blocks run split by query rows over a thread pool (the CPU baseline's
+    speed); the rows are independent, so the result equals the single-threaded computation."""
+    rng = np.random.default_rng(3)
+    H, Hkv, D = 8, 2, 64
+    q = rng.standard_normal((tq, H, D), dtype=np.float32)
+    k = rng.standard_normal((tk, Hkv, D), dtype=np.float32)
+    v = rng.standard_normal((tk, Hkv, D), dtype=np.float32)
+    monkeypatch.setattr(orc, "_PARALLEL_MIN_SCORES", 1)
+    monkeypatch.setattr(orc, "ATTN_WORKERS", 4)
+    o4, l4 = orc.attn(q, k, v, causal, 0.125)
+    monkeypatch.setattr(orc, "ATTN_WORKERS", 1)
+    o1, l1 = orc.attn(q, k, v, causal, 0.125)
+    np.testing.assert_allclose(o4, o1, atol=1e-6, rtol=0)
+    np.testing.assert_allclose(l4, l1, atol=1e-6, rtol=0)
