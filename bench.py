@@ -456,7 +456,11 @@ def gpu_main(args, rank, world, local_rank):
         run_serial()
     run_pipelined(2)
     torch.cuda.synchronize()
-    e2e_steps = max(2, min(args.steps, 10))
+    # as many steps as the timed loop (the pipeline's fill -- the first step's copy in -- and
+    # drain -- the last copy out -- are then spread over the same count), capped near 5 s from
+    # the FLOP count (the same on every rank, so all ranks run the same steps)
+    est_ms = step_flops / world / 1.0e15 * 1e3
+    e2e_steps = max(2, min(args.steps, int(5000.0 / max(est_ms, 1e-3))))
     ev3 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(e2e_steps)]
     barrier()
