@@ -186,10 +186,10 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------------------- CPU baseline
-def cpu_sample(rank_steps=None, threads=None):
+def cpu_sample(rank_steps=None, threads=None, min_seconds=10.0):
     """Time the oracle (numpy restatement of the reference's CPU ring simulation) on rank 0's
-    share of the cfg2 ring at cp=8: every step of rank 0 (or the given subset), all heads.
-    Returns (flops, seconds, threads)."""
+    share of the cfg2 ring at cp=8: every step of rank 0, repeated until ``min_seconds`` of
+    work (or the given subset of steps once), all heads.  Returns (flops, seconds, threads)."""
     from threadpoolctl import threadpool_info, threadpool_limits
 
     from oracle import ring_oracle as orc
@@ -210,12 +210,16 @@ def cpu_sample(rank_steps=None, threads=None):
         sched = [sched[i % len(sched)] for i in rank_steps]
     flops = 0.0
     t0 = time.perf_counter()
-    acc = None
-    for (_step, _src, pat) in sched:
-        o, l = orc.ring_step(q, k, v, [0, T], pat, scale)
-        acc = (o, l) if acc is None else orc.merge(acc[0], acc[1], o, l)
-        # local causal T x T (N^2/2 convention) and T x T/2 non-causal both count 2*T^2*Hq*D
-        flops += 2.0 * T * T * Hq * D
+    # the rank's ring, repeated until about 10 s of CPU work (at least one pass)
+    while True:
+        acc = None
+        for (_step, _src, pat) in sched:
+            o, l = orc.ring_step(q, k, v, [0, T], pat, scale)
+            acc = (o, l) if acc is None else orc.merge(acc[0], acc[1], o, l)
+            # local causal T x T (N^2/2 convention) and T x T/2 non-causal both count 2*T^2*Hq*D
+            flops += 2.0 * T * T * Hq * D
+        if rank_steps is not None or time.perf_counter() - t0 >= min_seconds:
+            break
     dt = time.perf_counter() - t0
     limiter.restore_original_limits()
     return flops, dt, threads
@@ -572,7 +576,7 @@ def gpu_main(args, rank, world, local_rank):
             "kind": "port",
             "sample": "oracle (numpy restatement of the reference's CPU ring simulation) on "
                       "rank 0 of cfg2 at cp=8: all 8 ring steps, 32 heads, T=4096 local "
-                      f"tokens; {flops_cpu:.3e} FLOP in {secs_cpu:.1f} s",
+                      f"tokens, repeated to about 10 s; {flops_cpu:.3e} FLOP in {secs_cpu:.1f} s",
             "vs_reference_cpu_code": _cpu_speed_pin()}
     if world == 1:
         line["hbm_kernels"] = hbm_kernels(dev)
